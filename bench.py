@@ -1,0 +1,332 @@
+#!/usr/bin/env python
+"""Batch-1 greedy decode throughput of the c2slm token loop on B200.
+
+Workload: Qwen2.5-0.5B-shaped Q4_K_M-style GGUF with
+seeded random weights (Q5_0 q/k/v/o/gate/up, Q4_K/Q6_K ffn_down, Q8_0 tied
+vocabulary projection of 151,936 rows), a 32-token uniform-random prompt,
+then greedy decode with the reference's repetition penalty (1.15 over 64).
+One step = one decoded token = logits + penalty + argmax + Forward of the
+chosen token.  Decoding stays at config 1's positions (32..159): every 128
+steps SeqLen is rewound to the prompt (KVCache.Rewind), so any --steps K
+measures the same workload.
+
+  value  device-resident decode (CUDA graph replays, inputs in HBM), CUDA
+         events on the engine's stream, max over ranks.
+  e2e    the public C ABI driven from the host one token per call
+         (c2s_decode_step: host token in, next token out, synchronised).
+--impl reference times the reference's algorithm on the host cores instead
+(the CPU port in oracle/, with the WorkerPool's row split; Go is absent).
+
+Multi-GPU (torchrun): one independent request stream per GPU (data
+parallel, no collective on the data path), weak scaling.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PERIOD = 128          # decode steps per request (config 1)
+PROMPT = 32           # prompt tokens (config 1)
+PENALTY, WINDOW = 1.15, 64
+METRIC = "batch-1 greedy decode tokens/s (Qwen2.5-0.5B-shaped Q4_K_M, config 1)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8192)
+    ap.add_argument("--warmup", type=int, default=64)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", default="qwen05b")
+    ap.add_argument("--profile-steps", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def stage_bytes(path: str) -> dict:
+    """Algorithmic bytes per decoded token by stage, from the GGUF tensor table."""
+    from c2slm_b200 import gguf
+    out = {"qkv": 0, "o_proj": 0, "gate_up": 0, "down": 0, "logits": 0, "attention": 0}
+    with gguf.File(path) as f:
+        T = f.tensor_map
+        L = f.get_uint32("qwen2.block_count")[0]
+        H = f.get_uint32("qwen2.embedding_length")[0]
+        for l in range(L):
+            p = f"blk.{l}."
+            for n in ("attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight",
+                      "attn_q.bias", "attn_k.bias", "attn_v.bias"):
+                if p + n in T:
+                    out["qkv"] += len(T[p + n].data)
+            out["o_proj"] += len(T[p + "attn_output.weight"].data)
+            out["gate_up"] += sum(len(T[p + n].data) for n in ("ffn_norm.weight", "ffn_gate.weight", "ffn_up.weight"))
+            out["down"] += len(T[p + "ffn_down.weight"].data)
+        te = T["token_embd.weight"]
+        out["qkv"] += len(te.data) // int(te.dimensions[1])  # one embedding row
+        ow = T.get("output.weight", te)
+        out["logits"] = len(ow.data) + len(T["output_norm.weight"].data)
+        kvh = f.get_uint32("qwen2.attention.head_count_kv")[0]
+        hd = H // f.get_uint32("qwen2.attention.head_count")[0]
+        out["kv_per_pos"] = 2 * L * kvh * hd * 4  # fp32 K and V read per position
+        out["layers"] = L
+    return out
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=self.tmp,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.tmp.flush()
+        rows = [r.split(",") for r in open(self.tmp.name).read().strip().splitlines() if r.strip()]
+        os.unlink(self.tmp.name)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_decode_rate(path: str, prompt, warmup: int, max_steps: int, budget_s: float, threads: int):
+    """The reference algorithm on the host cores (oracle port, WorkerPool split)."""
+    from oracle import oracle as O
+    with O.OracleModel(path, max_tokens=PROMPT + PERIOD + 8, nthreads=threads) as o:
+        nx = o.ingest_from(0, prompt)
+        done = 0
+        o.generate(nx, warmup, penalty=PENALTY, window=WINDOW, stop_on_special=False)
+        t0 = time.perf_counter()
+        while done < max_steps and time.perf_counter() - t0 < budget_s:
+            if o.seq_len >= PROMPT + PERIOD:
+                o.seq_len = PROMPT  # same rewind as the GPU arm
+            # one decode step: logits + penalty + argmax + Forward (c2slm.go:148-223)
+            o.generate(nx, 1, penalty=PENALTY, window=WINDOW, stop_on_special=False)
+            done += 1
+        t_total = time.perf_counter() - t0
+    return done / t_total, done, t_total
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from c2slm_b200 import synth
+    import numpy as np
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle")], check=True)
+    path = synth.cached_model(args.model)
+    prompt = np.random.default_rng(0).integers(0, 151643, PROMPT).astype(np.int32)
+    threads = min(os.cpu_count() or 1, 32)  # engine/pool.go:47-53
+    max_steps = min(args.steps, 256)
+    rate, done, secs = cpu_decode_rate(path, prompt, min(args.warmup, 2), max_steps, 120.0, threads)
+    sample = (f"{done} decode steps (of --steps {args.steps}) at positions {PROMPT}..{PROMPT + PERIOD - 1} "
+              f"after a {PROMPT}-token prompt, {secs:.1f} s")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(rate, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / rate, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (int8 dot for K-quants)", "data": "synthetic",
+        "config": {"workload": "config 1: qwen2.5-0.5b-shaped Q4_K_M, 32-token prompt, greedy decode",
+                   "model": args.model},
+        "cpu_baseline": {"value": round(rate, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(rate, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "hazyhaar/c2slm is Go (GOEXPERIMENT=simd, Go 1.27); no Go toolchain on this image, so the "
+                "reference's scalar algorithm is timed through its C restatement in oracle/",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import c2slm_b200 as K
+    from c2slm_b200 import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if rank == 0:
+        path = synth.cached_model(args.model)
+    barrier()
+    path = synth.cached_model(args.model)
+    eng = K.Engine(path, device=local, max_tokens=16384)
+    prompt = np.random.default_rng(rank).integers(0, 151643, PROMPT).astype(np.int32)
+    eng.ingest_from(0, prompt)
+
+    # ---- value: device-resident decode ---------------------------------
+    eng.bench_decode_timed(max(args.warmup, 3), PENALTY, WINDOW, period=PERIOD)
+    eng.seq_len = PROMPT
+    clocks = Clocks(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    ms = eng.bench_decode_timed(args.steps, PENALTY, WINDOW, period=PERIOD)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms_max = max_over_ranks(ms)
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- e2e: host-driven, one public call per token ---------------------
+    eng.seq_len = PROMPT - 1
+    tok = int(prompt[-1])
+    e2e_steps = min(args.steps, 4096)
+    for _ in range(8):
+        tok = eng.decode_step(tok, PENALTY, WINDOW)
+    eng.seq_len = PROMPT - 1
+    tok = int(prompt[-1])
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        if eng_seq_wrap(i):
+            eng.seq_len = PROMPT - 1
+        tok = eng.decode_step(tok, PENALTY, WINDOW)
+    torch.cuda.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = world * e2e_steps / e2e_s
+
+    # ---- per-stage table and the dominant kernel's roofline ---------------
+    eng.seq_len = PROMPT
+    prof = eng.profile_step(args.profile_steps, PENALTY, WINDOW)
+    sb = stage_bytes(path)
+    mean_pos = PROMPT + args.profile_steps / 2.0
+    sb["attention"] = sb["kv_per_pos"] * (mean_pos + 1)
+    peak, peak_kind = measured_peaks()
+    stages = {}
+    for name, d in prof.items():
+        if d["launches"] == 0:
+            continue
+        per_launch_bytes = sb[name] * args.profile_steps / d["launches"]
+        avg_s = d["ms"] / d["launches"] / 1000.0
+        stages[name] = {"ms_per_step": round(d["ms"] / args.profile_steps, 4), "launches": d["launches"],
+                        "bytes_per_launch": int(per_launch_bytes),
+                        "gbs": round(per_launch_bytes / avg_s / 1e9, 1)}
+    dom = max(stages, key=lambda k: stages[k]["ms_per_step"])
+    dstage = stages[dom]
+    achieved = dstage["gbs"]
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(dom)
+    per_token = sum(sb[k] for k in ("qkv", "o_proj", "gate_up", "down", "logits")) + \
+        sb["kv_per_pos"] * (PROMPT + PERIOD / 2.0)
+    step_ms = ms_max / args.steps
+
+    # ---- CPU baseline (rank 0, N=1) ---------------------------------------
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        threads = min(os.cpu_count() or 1, 32)
+        rate, done, secs = cpu_decode_rate(path, prompt, 1, 64, 20.0, threads)
+        cpu = {"value": round(rate, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"{done} decode steps at positions {PROMPT}.. after a {PROMPT}-token prompt, {secs:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 activations; int8 dp4a for K-quant x Q8_K", "data": "synthetic",
+            "config": {"workload": "config 1: qwen2.5-0.5b-shaped Q4_K_M (Q5_0/Q4_K/Q6_K/Q8_0), 32-token prompt, "
+                                   "greedy decode at positions 32..159 (rewound every 128 steps)",
+                       "model": args.model, "global_batch": world, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (%.0f MB of weights streamed per step)" % (per_token / 1e6),
+                       "bytes_per_token": int(per_token),
+                       "step_hbm_frac": round(per_token / (step_ms / 1000.0) / 1e9 / peak, 4)},
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+                         "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "bytes_per_launch": dstage["bytes_per_launch"]},
+            "stages": stages,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 36, "d2h_bytes_per_step": 4,
+                    "api": "c2s_decode_step"},
+            "gpu_launches": eng.kernels_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def eng_seq_wrap(i: int) -> bool:
+    return i > 0 and i % PERIOD == 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

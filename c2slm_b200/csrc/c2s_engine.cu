@@ -1,0 +1,1384 @@
+// c2s_engine.cu -- host side of the sm_100a token loop and its C ABI.
+//
+// Replaces engine.LoadModel / Forward / ComputeLogits and c2slm.Engine's
+// generate loop (see include/c2slm_b200.h for the per-function mapping).
+// Model tensors are uploaded once, in their GGML block layouts, into one HBM
+// arena; a decode step is a CUDA graph of 5 kernels per layer plus one logits
+// kernel, chained with programmatic dependent launch.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/c2slm_b200.h"
+#include "c2s_kernels.cuh"
+
+using namespace c2s;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CK(call)                                                                                  \
+  do {                                                                                            \
+    cudaError_t e_ = (call);                                                                      \
+    if (e_ != cudaSuccess) return fail(C2S_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr int kMaxContext = 16384;  // engine.MaxContextLen (engine/kvcache.go:11)
+
+size_t row_bytes_of(int type, int64_t cols) {
+  switch (type) {
+    case T_Q5_0: return static_cast<size_t>(cols / 32) * 22;
+    case T_Q8_0: return static_cast<size_t>(cols / 32) * 34;
+    case T_Q4_K: return static_cast<size_t>(cols / 256) * 144;
+    case T_Q6_K: return static_cast<size_t>(cols / 256) * 210;
+    case T_F32: return static_cast<size_t>(cols) * 4;
+    default: return 0;
+  }
+}
+
+bool is_kquant(int t) { return t == T_Q4_K || t == T_Q6_K; }
+bool is_f32x(int t) { return t == T_Q5_0 || t == T_Q8_0; }
+
+int check_matrix(int type, int64_t rows, int64_t cols, const char *what) {
+  if (!(is_kquant(type) || is_f32x(type)))
+    return fail(C2S_ERR_UNSUPPORTED, "%s: GGML type %d is not a supported matrix type", what, type);
+  if (rows <= 0 || cols <= 0) return fail(C2S_ERR_ARG, "%s: bad shape %lld x %lld", what, (long long)rows, (long long)cols);
+  if (is_kquant(type) && cols % 256) return fail(C2S_ERR_UNSUPPORTED, "%s: K-quant needs cols %% 256 == 0 (cols=%lld)", what, (long long)cols);
+  if (is_f32x(type) && cols % 32) return fail(C2S_ERR_UNSUPPORTED, "%s: cols %% 32 != 0", what);
+  if (row_bytes_of(type, cols) > static_cast<size_t>(kStageBytes))
+    return fail(C2S_ERR_UNSUPPORTED, "%s: row of %zu bytes exceeds the %d-byte staging slot", what,
+                row_bytes_of(type, cols), kStageBytes);
+  return C2S_OK;
+}
+
+int units_of(int type, int cols) { return is_kquant(type) ? (cols / 256) * 4 : cols / 32; }
+
+// ---------------------------------------------------------------------------
+// launch helper (programmatic dependent launch attribute)
+// ---------------------------------------------------------------------------
+bool g_use_pdl = [] {
+  const char *e = getenv("C2S_NO_PDL");
+  return !(e && *e && *e != '0');
+}();
+
+template <class P>
+cudaError_t launch(void (*kernel)(P), dim3 grid, dim3 block, size_t smem, cudaStream_t s, const P &params) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_use_pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+// shared-memory layout of one k_matvec launch
+void layout_matvec(MatParams &P, int grid) {
+  size_t off = static_cast<size_t>(kStages) * kStageAlloc;
+  P.off_bars = static_cast<int>(off);
+  off += 64;
+  const bool normed = P.kind == K_QKV || P.kind == K_FFN_UP || P.kind == K_NORM ||
+                      (P.kind == K_LOGITS && P.x_in == nullptr);
+  P.off_xn = static_cast<int>(off);
+  if (normed) off += (static_cast<size_t>(P.cols) * 4 + 15) & ~size_t(15);
+  P.off_xt = static_cast<int>(off);
+  if (P.need_f32) off += (static_cast<size_t>(P.cols) * 4 + 15) & ~size_t(15);
+  P.off_q8 = static_cast<int>(off);
+  if (P.need_q8k) {
+    const int nsb = P.cols / 256;
+    off += (static_cast<size_t>(q8_qs_bytes(P.cols)) + 4 * nsb + 64 * nsb + 15) & ~size_t(15);
+  }
+  int yr = 1;
+  for (int s = 0; s < P.nseg; ++s) yr = std::max(yr, (P.seg[s].rows + grid - 1) / grid + 1);
+  P.ybuf_rows = yr;
+  P.off_y = static_cast<int>(off);
+  off += static_cast<size_t>(std::max(P.nseg, 1)) * yr * 4;
+  P.smem_bytes = static_cast<int>(off);
+}
+
+Seg make_seg(const uint8_t *w, int type, int rows, int cols, const float *bias, float *out) {
+  Seg s{};
+  s.w = w;
+  s.type = type;
+  s.rows = rows;
+  s.row_bytes = static_cast<int>(row_bytes_of(type, cols));
+  s.units = units_of(type, cols);
+  s.rows_per_chunk = std::max(1, kStageBytes / std::max(1, s.row_bytes));
+  s.bias = bias;
+  s.out = out;
+  return s;
+}
+
+void finish_needs(MatParams &P) {
+  P.need_f32 = 0;
+  P.need_q8k = 0;
+  for (int s = 0; s < P.nseg; ++s) {
+    if (is_f32x(P.seg[s].type)) P.need_f32 = 1;
+    if (is_kquant(P.seg[s].type)) P.need_q8k = 1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// GGUF (gguf/reader.go:394-546), host side
+// ---------------------------------------------------------------------------
+struct GTensor {
+  std::string name;
+  int type = 0;
+  int n_dims = 0;
+  int64_t dims[4] = {0, 0, 0, 0};
+  const uint8_t *data = nullptr;
+  uint64_t nbytes = 0;
+};
+
+struct GFile {
+  uint8_t *map = nullptr;
+  size_t size = 0;
+  std::vector<GTensor> tensors;
+  struct KV {
+    std::string key;
+    uint32_t vt;
+    uint64_t u;
+    int64_t i;
+    double f;
+  };
+  std::vector<KV> kvs;
+  int32_t im_end = 0, eos = 0;
+  ~GFile() {
+    if (map) munmap(map, size);
+  }
+  bool u32(const char *k, uint32_t *out) const {  // GetUint32, gguf/reader.go:559-576
+    for (auto &kv : kvs)
+      if (kv.key == k) {
+        if (kv.vt == 4 || kv.vt == 10) { *out = static_cast<uint32_t>(kv.u); return true; }
+        if (kv.vt == 5 || kv.vt == 11) { *out = static_cast<uint32_t>(kv.i); return true; }
+        return false;
+      }
+    return false;
+  }
+  bool f32(const char *k, float *out) const {  // GetFloat32, gguf/reader.go:579-592
+    for (auto &kv : kvs)
+      if (kv.key == k) {
+        if (kv.vt == 6 || kv.vt == 12) { *out = static_cast<float>(kv.f); return true; }
+        return false;
+      }
+    return false;
+  }
+};
+
+struct Rd {
+  const uint8_t *p;
+  size_t n, pos = 0;
+  bool bad = false;
+  bool need(size_t k) {
+    if (pos + k > n) bad = true;
+    return !bad;
+  }
+  uint8_t u8() { return need(1) ? p[pos++] : 0; }
+  uint16_t u16() { if (!need(2)) return 0; uint16_t v; memcpy(&v, p + pos, 2); pos += 2; return v; }
+  uint32_t u32() { if (!need(4)) return 0; uint32_t v; memcpy(&v, p + pos, 4); pos += 4; return v; }
+  uint64_t u64() { if (!need(8)) return 0; uint64_t v; memcpy(&v, p + pos, 8); pos += 8; return v; }
+  bool str(std::string *s) {
+    const uint64_t l = u64();
+    if (bad || !need(l)) return false;
+    if (s) s->assign(reinterpret_cast<const char *>(p + pos), l);
+    pos += l;
+    return true;
+  }
+};
+
+bool skip_value(Rd &r, uint32_t vt, GFile::KV *kv, int depth) {
+  switch (vt) {
+    case 0: case 7: { uint8_t v = r.u8(); if (kv) kv->u = v; } break;
+    case 1: { int8_t v = static_cast<int8_t>(r.u8()); if (kv) kv->i = v; } break;
+    case 2: { uint16_t v = r.u16(); if (kv) kv->u = v; } break;
+    case 3: { int16_t v = static_cast<int16_t>(r.u16()); if (kv) kv->i = v; } break;
+    case 4: { uint32_t v = r.u32(); if (kv) kv->u = v; } break;
+    case 5: { int32_t v = static_cast<int32_t>(r.u32()); if (kv) kv->i = v; } break;
+    case 6: { uint32_t b = r.u32(); float f; memcpy(&f, &b, 4); if (kv) kv->f = f; } break;
+    case 8: if (!r.str(nullptr)) return false; break;
+    case 9: {
+      if (depth > 4) return false;
+      const uint32_t et = r.u32();
+      const uint64_t n = r.u64();
+      for (uint64_t i = 0; i < n && !r.bad; ++i)
+        if (!skip_value(r, et, nullptr, depth + 1)) return false;
+    } break;
+    case 10: { uint64_t v = r.u64(); if (kv) kv->u = v; } break;
+    case 11: { int64_t v = static_cast<int64_t>(r.u64()); if (kv) kv->i = v; } break;
+    case 12: { uint64_t b = r.u64(); double d; memcpy(&d, &b, 8); if (kv) kv->f = d; } break;
+    default: return false;
+  }
+  return !r.bad;
+}
+
+uint64_t tensor_nbytes(int type, const int64_t *dims, int nd) {  // gguf/reader.go:513-546
+  if (nd == 0) return 0;
+  uint64_t n = 1;
+  for (int i = 0; i < nd; ++i) n *= static_cast<uint64_t>(dims[i]);
+  switch (type) {
+    case 0: return n * 4;
+    case 1: return n * 2;
+    case 2: return (n / 32) * 18;
+    case 6: return (n / 32) * 22;
+    case 8: return (n / 32) * 34;
+    case 12: return (n / 256) * 144;
+    case 14: return (n / 256) * 210;
+    default: return n * 4;
+  }
+}
+
+int gguf_open(const char *path, std::unique_ptr<GFile> &out) {
+  const int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(C2S_ERR_ARG, "gguf open %s: %s", path, strerror(errno));
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size < 24) {
+    close(fd);
+    return fail(C2S_ERR_FORMAT, "gguf: file too small");
+  }
+  void *m = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_SHARED | MAP_POPULATE, fd, 0);
+  close(fd);
+  if (m == MAP_FAILED) return fail(C2S_ERR_FORMAT, "gguf mmap failed");
+  auto f = std::make_unique<GFile>();
+  f->map = static_cast<uint8_t *>(m);
+  f->size = static_cast<size_t>(st.st_size);
+  Rd r{f->map, f->size};
+  if (r.u32() != 0x46554747u) return fail(C2S_ERR_FORMAT, "invalid GGUF magic");
+  const uint32_t ver = r.u32();
+  if (ver < 2 || ver > 3) return fail(C2S_ERR_FORMAT, "unsupported GGUF version %u", ver);
+  const uint64_t nt = r.u64(), nkv = r.u64();
+  if (r.bad || nt > (1u << 20) || nkv > (1u << 20)) return fail(C2S_ERR_FORMAT, "bad GGUF header");
+  uint64_t alignment = 32;
+  for (uint64_t i = 0; i < nkv; ++i) {
+    GFile::KV kv{};
+    if (!r.str(&kv.key)) return fail(C2S_ERR_FORMAT, "metadata key truncated");
+    kv.vt = r.u32();
+    if (kv.vt == 9 && kv.key == "tokenizer.ggml.tokens") {
+      const uint32_t et = r.u32();
+      const uint64_t n = r.u64();
+      if (et != 8) return fail(C2S_ERR_FORMAT, "tokenizer.ggml.tokens is not a string array");
+      std::string s;
+      for (uint64_t t = 0; t < n && !r.bad; ++t) {
+        if (!r.str(&s)) break;
+        if (s == "<|im_end|>") f->im_end = static_cast<int32_t>(t);        // tokenizer/bpe.go:284-289
+        if (s == "<|endoftext|>") f->eos = static_cast<int32_t>(t);
+      }
+    } else if (!skip_value(r, kv.vt, &kv, 0)) {
+      return fail(C2S_ERR_FORMAT, "metadata[%s] unreadable", kv.key.c_str());
+    }
+    if (kv.key == "general.alignment" && (kv.vt == 4 || kv.vt == 10) && kv.u) alignment = kv.u;
+    if (r.bad) return fail(C2S_ERR_FORMAT, "metadata truncated");
+    f->kvs.push_back(kv);
+  }
+  std::vector<uint64_t> offs;
+  for (uint64_t i = 0; i < nt; ++i) {
+    GTensor t;
+    if (!r.str(&t.name)) return fail(C2S_ERR_FORMAT, "tensor name truncated");
+    t.n_dims = static_cast<int>(r.u32());
+    if (t.n_dims > 4) return fail(C2S_ERR_FORMAT, "tensor %s has %d dims", t.name.c_str(), t.n_dims);
+    for (int d = 0; d < t.n_dims; ++d) t.dims[d] = static_cast<int64_t>(r.u64());
+    t.type = static_cast<int>(r.u32());
+    offs.push_back(r.u64());
+    if (r.bad) return fail(C2S_ERR_FORMAT, "tensor infos truncated");
+    f->tensors.push_back(t);
+  }
+  size_t pos = r.pos;
+  if (pos % alignment) pos += alignment - pos % alignment;
+  for (size_t i = 0; i < f->tensors.size(); ++i) {
+    GTensor &t = f->tensors[i];
+    t.nbytes = tensor_nbytes(t.type, t.dims, t.n_dims);
+    if (pos + offs[i] + t.nbytes > f->size) return fail(C2S_ERR_FORMAT, "tensor[%s] data out of range", t.name.c_str());
+    t.data = f->map + pos + offs[i];
+  }
+  out = std::move(f);
+  return C2S_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Engine
+// ---------------------------------------------------------------------------
+struct LayerDev {
+  const uint8_t *q, *k, *v, *o, *gate, *up, *down;
+  int tq, tk, tv, to, tgate, tup, tdown;
+  const float *attn_norm, *ffn_norm, *qb, *kb, *vb, *qn, *kn;
+};
+
+struct HostFwdIn {
+  int token, pos, commit;
+};
+
+struct c2s_engine {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  c2s_model_desc d{};
+  int tok_type = 0, out_type = 0;
+  const uint8_t *tok_embd = nullptr, *output = nullptr;
+  const float *out_norm = nullptr;
+  std::vector<LayerDev> layers;
+  // device memory
+  uint8_t *weights = nullptr;
+  size_t weights_bytes = 0;
+  float *kv = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  float *X = nullptr, *normx = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn_out = nullptr,
+        *h = nullptr, *logits = nullptr, *part = nullptr, *scratch_x = nullptr;
+  float2 *amax_part = nullptr;
+  int *token_ids = nullptr, *out_tokens = nullptr, *rows_idx = nullptr;
+  DevState *st = nullptr;
+  // pinned host mirrors
+  HostFwdIn *h_in = nullptr;  // ring of forward inputs
+  int h_in_next = 0;
+  float *h_buf = nullptr;     // staging for normx/logits
+  DevState *h_st = nullptr;
+  int *h_tokens = nullptr;
+  int host_seq = 0;
+  int max_splits = 1, chunk_cap = 32;
+  size_t attn_smem = 0;
+  int kernels_per_step = 0;
+  cudaGraphExec_t g_forward = nullptr, g_step = nullptr, g_logits = nullptr, g_fwd_select = nullptr;
+  std::vector<MatParams> mp_cache;
+  uint64_t algorithmic_bytes = 0;
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+const c2s_tensor_desc *find_t(const c2s_tensor_desc *ts, int n, const std::string &name) {
+  for (int i = 0; i < n; ++i)
+    if (ts[i].name && name == ts[i].name) return &ts[i];
+  return nullptr;
+}
+
+int64_t t_cols(const c2s_tensor_desc *t) { return t->n_dims > 0 ? t->dims[0] : 0; }
+int64_t t_rows(const c2s_tensor_desc *t) { return t->n_dims > 1 ? t->dims[1] : 1; }
+
+int matvec_params_common(c2s_engine *e, MatParams &P) {
+  P.eps = e->d.eps;
+  P.X = e->X;
+  P.st = e->st;
+  P.token_ids = e->token_ids;
+  P.out_tokens = e->out_tokens;
+  P.part = e->amax_part;
+  finish_needs(P);
+  layout_matvec(P, e->num_sms);
+  return C2S_OK;
+}
+
+// Builds the kernel sequence of one forward (L layers) on `s`.
+// Optional per-kernel timing (eager launches only): events[k] brackets
+// kernel k of the sequence; kind_of[k] receives its stage id.
+struct KTimer {
+  std::vector<cudaEvent_t> *ev = nullptr;
+  std::vector<int> *kind = nullptr;
+};
+
+cudaError_t mark(KTimer *t, cudaStream_t s, int kind) {
+  if (!t || !t->ev) return cudaSuccess;
+  cudaEvent_t ev;
+  cudaError_t err = cudaEventCreate(&ev);
+  if (err) return err;
+  t->ev->push_back(ev);
+  if (kind >= 0) t->kind->push_back(kind);
+  return cudaEventRecord(ev, s);
+}
+
+cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool final_norm, KTimer *tm = nullptr) {
+  const int L = e->d.n_layers, H = e->d.embd, F = e->d.ffn, hd = e->d.head_dim;
+  const int kvd = e->d.n_kv_heads * hd;
+  const int G = e->num_sms;
+  cudaError_t err = cudaSuccess;
+  for (int l = 0; l < L && err == cudaSuccess; ++l) {
+    const LayerDev &Ld = e->layers[l];
+    // QKV (+ embedding on layer 0)
+    MatParams P{};
+    P.kind = K_QKV;
+    P.nseg = 3;
+    P.cols = H;
+    P.seg[0] = make_seg(Ld.q, Ld.tq, H, H, Ld.qb, e->q);
+    P.seg[1] = make_seg(Ld.k, Ld.tk, kvd, H, Ld.kb, e->k);
+    P.seg[2] = make_seg(Ld.v, Ld.tv, kvd, H, Ld.vb, e->v);
+    P.norm_w = Ld.attn_norm;
+    P.do_embed = (l == 0);
+    P.embd_w = e->tok_embd;
+    P.embd_type = e->tok_type;
+    P.embd_row_bytes = static_cast<int>(row_bytes_of(e->tok_type, H));
+    P.check_halt = check_halt;
+    matvec_params_common(e, P);
+    if ((err = mark(tm, s, -1))) break;
+    err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
+    if (err || (err = mark(tm, s, K_QKV))) break;
+    // attention
+    AttnParams A{};
+    A.layer = l;
+    A.n_heads = e->d.n_heads;
+    A.n_kv = e->d.n_kv_heads;
+    A.hd = hd;
+    A.max_tokens = e->d.max_tokens;
+    A.max_splits = e->max_splits;
+    A.rope_len = kMaxContext;
+    A.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
+    A.eps = e->d.eps;
+    A.q = e->q;
+    A.k = e->k;
+    A.v = e->v;
+    const size_t plane = static_cast<size_t>(L) * e->d.n_kv_heads * e->d.max_tokens * hd;
+    A.kcache = e->kv;
+    A.vcache = e->kv + plane;
+    A.rope_cos = e->rope_cos;
+    A.rope_sin = e->rope_sin;
+    A.q_norm = Ld.qn;
+    A.k_norm = Ld.kn;
+    A.part = e->part;
+    A.out = e->attn_out;
+    A.st = e->st;
+    A.check_halt = check_halt;
+    A.chunk_cap = e->chunk_cap;
+    if ((err = mark(tm, s, -1))) break;
+    err = launch(k_attention, dim3(e->d.n_kv_heads, e->max_splits), dim3(kThreads), e->attn_smem, s, A);
+    if (err || (err = mark(tm, s, 7))) break;
+    // o_proj + residual
+    P = MatParams{};
+    P.kind = K_OPROJ;
+    P.nseg = 1;
+    P.cols = e->d.n_heads * hd;
+    P.seg[0] = make_seg(Ld.o, Ld.to, H, e->d.n_heads * hd, nullptr, e->X);
+    P.x_in = e->attn_out;
+    P.check_halt = check_halt;
+    matvec_params_common(e, P);
+    if ((err = mark(tm, s, -1))) break;
+    err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
+    if (err || (err = mark(tm, s, K_OPROJ))) break;
+    // gate/up + SwiGLU
+    P = MatParams{};
+    P.kind = K_FFN_UP;
+    P.nseg = 2;
+    P.cols = H;
+    P.seg[0] = make_seg(Ld.gate, Ld.tgate, F, H, nullptr, nullptr);
+    P.seg[1] = make_seg(Ld.up, Ld.tup, F, H, nullptr, nullptr);
+    P.norm_w = Ld.ffn_norm;
+    P.h_out = e->h;
+    P.check_halt = check_halt;
+    matvec_params_common(e, P);
+    if ((err = mark(tm, s, -1))) break;
+    err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
+    if (err || (err = mark(tm, s, K_FFN_UP))) break;
+    // down + residual (+ commit on the last layer)
+    P = MatParams{};
+    P.kind = K_FFN_DOWN;
+    P.nseg = 1;
+    P.cols = F;
+    P.seg[0] = make_seg(Ld.down, Ld.tdown, H, F, nullptr, e->X);
+    P.x_in = e->h;
+    P.commit_here = (l == L - 1);
+    P.check_halt = check_halt;
+    matvec_params_common(e, P);
+    if ((err = mark(tm, s, -1))) break;
+    err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
+    if (err || (err = mark(tm, s, K_FFN_DOWN))) break;
+  }
+  if (err == cudaSuccess && final_norm) {
+    MatParams P{};
+    P.kind = K_NORM;
+    P.nseg = 0;
+    P.cols = H;
+    P.norm_w = e->out_norm;
+    P.normx_out = e->normx;
+    P.check_halt = check_halt;
+    matvec_params_common(e, P);
+    err = launch(k_matvec, dim3(1), dim3(kThreads), P.smem_bytes, s, P);
+  }
+  return err;
+}
+
+cudaError_t enqueue_logits(c2s_engine *e, cudaStream_t s, bool select, bool from_normx, bool check_halt,
+                           KTimer *tm = nullptr) {
+  MatParams P{};
+  P.kind = K_LOGITS;
+  P.nseg = 1;
+  P.cols = e->d.embd;
+  P.seg[0] = make_seg(e->output, e->out_type, e->d.vocab, e->d.embd, nullptr, e->logits);
+  P.norm_w = e->out_norm;
+  P.x_in = from_normx ? e->normx : nullptr;
+  P.normx_out = from_normx ? nullptr : e->normx;
+  P.select = select;
+  P.check_halt = check_halt;
+  matvec_params_common(e, P);
+  cudaError_t err = mark(tm, s, -1);
+  if (!err) err = launch(k_matvec, dim3(e->num_sms), dim3(kThreads), P.smem_bytes, s, P);
+  if (!err) err = mark(tm, s, K_LOGITS);
+  return err;
+}
+
+int capture(c2s_engine *e, cudaGraphExec_t *out, int which) {
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t err = cudaSuccess;
+  switch (which) {
+    case 0: err = enqueue_forward(e, e->stream, false, true); break;          // Forward + NormX
+    case 1:                                                                    // decode step
+      err = enqueue_logits(e, e->stream, true, false, true);
+      if (!err) err = enqueue_forward(e, e->stream, true, false);
+      break;
+    case 2: err = enqueue_logits(e, e->stream, false, true, false); break;   // ComputeLogits(NormX)
+    case 3:                                                                    // forward then select
+      err = enqueue_forward(e, e->stream, false, false);
+      if (!err) err = enqueue_logits(e, e->stream, true, false, false);
+      break;
+  }
+  cudaError_t e2 = cudaStreamEndCapture(e->stream, &g);
+  if (err != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return fail(C2S_ERR_CUDA, "kernel launch during capture: %s", cudaGetErrorString(err));
+  }
+  if (e2 != cudaSuccess) return fail(C2S_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e2));
+  cudaError_t e3 = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (e3 != cudaSuccess) return fail(C2S_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e3));
+  return C2S_OK;
+}
+
+int read_status(c2s_engine *e) {
+  // Reads back the device state (sync point); reports bounded-wait failures.
+  CK(cudaMemcpyAsync(e->h_st, e->st, sizeof(DevState), cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  if (e->h_st->err) {
+    const unsigned code = e->h_st->err;
+    CK(cudaMemsetAsync(&e->st->err, 0, sizeof(unsigned), e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    return fail(C2S_ERR_TIMEOUT, "device reported error flags 0x%x (bounded wait expired or bad position)", code);
+  }
+  e->host_seq = e->h_st->seq_len;
+  return C2S_OK;
+}
+
+int set_fwd_input(c2s_engine *e, int token, int pos, int commit) {
+  HostFwdIn *slot = &e->h_in[e->h_in_next];
+  e->h_in_next = (e->h_in_next + 1) % (e->d.max_tokens + 8);
+  slot->token = token;
+  slot->pos = pos;
+  slot->commit = commit;
+  CK(cudaMemcpyAsync(e->st, slot, sizeof(HostFwdIn), cudaMemcpyHostToDevice, e->stream));
+  return C2S_OK;
+}
+
+int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_desc *ts, int n) {
+  c2s_model_desc d = *desc;
+  if (d.embd <= 0 || d.n_layers <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.ffn <= 0)
+    return fail(C2S_ERR_ARG, "model desc: non-positive dimension");
+  if (d.head_dim <= 0) d.head_dim = d.embd / d.n_heads;  // engine/model.go:137
+  if (d.n_heads % d.n_kv_heads) return fail(C2S_ERR_UNSUPPORTED, "n_heads %% n_kv_heads != 0");
+  if (d.head_dim % 4 || d.head_dim > 256 || d.head_dim % 2)
+    return fail(C2S_ERR_UNSUPPORTED, "head_dim %d not supported", d.head_dim);
+  if (d.n_kv_heads > 64) return fail(C2S_ERR_UNSUPPORTED, "more than 64 kv heads");
+  if (d.max_tokens <= 0) d.max_tokens = kMaxContext;
+  if (d.max_tokens > kMaxContext) return fail(C2S_ERR_ARG, "max_tokens above %d", kMaxContext);
+  if (d.rope_base == 0) d.rope_base = 1000000.0f;
+  if (d.eps == 0) d.eps = 1e-6f;
+  const c2s_tensor_desc *te = find_t(ts, n, "token_embd.weight");
+  if (!te || te->n_dims < 2) return fail(C2S_ERR_FORMAT, "missing token_embd.weight");
+  if (d.vocab <= 0) d.vocab = static_cast<int32_t>(t_rows(te));  // engine/model.go:118
+  const c2s_tensor_desc *on = find_t(ts, n, "output_norm.weight");
+  if (!on) return fail(C2S_ERR_FORMAT, "missing output_norm.weight");
+  const c2s_tensor_desc *ow = find_t(ts, n, "output.weight");
+  if (!ow) ow = te;  // tied fallback (engine/model.go:126-130)
+  const int H = d.embd, F = d.ffn, hd = d.head_dim, kvd = d.n_kv_heads * hd;
+  if (d.n_heads * hd != H) return fail(C2S_ERR_UNSUPPORTED, "n_heads*head_dim != embd");
+  if (H % 256 && (is_kquant(te->type))) return fail(C2S_ERR_UNSUPPORTED, "embedding type needs embd %% 256 == 0");
+  if (int rc = check_matrix(ow->type, d.vocab, H, "output")) return rc;
+  if (!(te->type == T_Q8_0 || te->type == T_Q5_0 || te->type == T_Q4_K || te->type == T_Q6_K || te->type == T_F32))
+    return fail(C2S_ERR_UNSUPPORTED, "token_embd type %d", te->type);
+  if (H > 16384 || F > 65536) return fail(C2S_ERR_UNSUPPORTED, "dimensions too large");
+
+  // ---- collect the tensors to upload, with their arena offsets
+  struct Up {
+    const c2s_tensor_desc *t;
+    size_t off;
+  };
+  std::vector<Up> ups;
+  size_t total = 0;
+  auto add = [&](const c2s_tensor_desc *t) -> size_t {
+    for (auto &u : ups)
+      if (u.t == t) return u.off;
+    const size_t off = total;
+    ups.push_back({t, off});
+    total += (t->nbytes + 64 + 255) & ~size_t(255);
+    return off;
+  };
+  struct LOff {
+    size_t q, k, v, o, gate, up, down, an, fn, qb, kb, vb, qn, kn;
+    int tq, tk, tv, to, tg, tu, td;
+    bool hqb, hkb, hvb, hqn, hkn;
+  };
+  std::vector<LOff> lo(d.n_layers);
+  char nm[128];
+  for (int l = 0; l < d.n_layers; ++l) {
+    auto T = [&](const char *s) {
+      snprintf(nm, sizeof nm, "blk.%d.%s", l, s);
+      return find_t(ts, n, nm);
+    };
+    const c2s_tensor_desc *an = T("attn_norm.weight"), *q = T("attn_q.weight"), *k = T("attn_k.weight"),
+                          *v = T("attn_v.weight"), *o = T("attn_output.weight"), *fn = T("ffn_norm.weight"),
+                          *g = T("ffn_gate.weight"), *u = T("ffn_up.weight"), *dn = T("ffn_down.weight");
+    if (!an || !q || !k || !v || !o || !fn || !g || !u || !dn)
+      return fail(C2S_ERR_FORMAT, "blk.%d is missing a projection or norm tensor", l);
+    int rc;
+    if ((rc = check_matrix(q->type, H, H, "attn_q")) || (rc = check_matrix(k->type, kvd, H, "attn_k")) ||
+        (rc = check_matrix(v->type, kvd, H, "attn_v")) || (rc = check_matrix(o->type, H, H, "attn_output")) ||
+        (rc = check_matrix(g->type, F, H, "ffn_gate")) || (rc = check_matrix(u->type, F, H, "ffn_up")) ||
+        (rc = check_matrix(dn->type, H, F, "ffn_down")))
+      return rc;
+    if (t_cols(q) != H || t_rows(q) != H || t_cols(k) != H || t_rows(k) != kvd || t_cols(v) != H ||
+        t_rows(v) != kvd || t_cols(o) != H || t_rows(o) != H || t_cols(g) != H || t_rows(g) != F ||
+        t_cols(u) != H || t_rows(u) != F || t_cols(dn) != F || t_rows(dn) != H)
+      return fail(C2S_ERR_FORMAT, "blk.%d tensor shapes do not match the hyper-parameters", l);
+    LOff &x = lo[l];
+    x.an = add(an); x.q = add(q); x.k = add(k); x.v = add(v); x.o = add(o);
+    x.fn = add(fn); x.gate = add(g); x.up = add(u); x.down = add(dn);
+    x.tq = q->type; x.tk = k->type; x.tv = v->type; x.to = o->type; x.tg = g->type; x.tu = u->type; x.td = dn->type;
+    const c2s_tensor_desc *qb = T("attn_q.bias"), *kb = T("attn_k.bias"), *vb = T("attn_v.bias");
+    const c2s_tensor_desc *qn = T("attn_q_norm.weight"), *kn = T("attn_k_norm.weight");
+    x.hqb = qb; x.hkb = kb; x.hvb = vb; x.hqn = qn; x.hkn = kn;
+    if (qb) { if (qb->nbytes < static_cast<uint64_t>(H) * 4) return fail(C2S_ERR_FORMAT, "attn_q.bias too short"); x.qb = add(qb); }
+    if (kb) { if (kb->nbytes < static_cast<uint64_t>(kvd) * 4) return fail(C2S_ERR_FORMAT, "attn_k.bias too short"); x.kb = add(kb); }
+    if (vb) { if (vb->nbytes < static_cast<uint64_t>(kvd) * 4) return fail(C2S_ERR_FORMAT, "attn_v.bias too short"); x.vb = add(vb); }
+    if (qn) x.qn = add(qn);
+    if (kn) x.kn = add(kn);
+  }
+  const size_t off_te = add(te), off_on = add(on), off_ow = add(ow);
+
+  // ---- device memory
+  e->d = d;
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, e->device));
+  e->num_sms = prop.multiProcessorCount;
+  CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  if (cudaMalloc(&e->weights, total) != cudaSuccess) return fail(C2S_ERR_OOM, "weights: cudaMalloc(%zu) failed", total);
+  e->weights_bytes = total;
+  CK(cudaMemset(e->weights, 0, total));
+  for (auto &u : ups) CK(cudaMemcpy(e->weights + u.off, u.t->data, u.t->nbytes, cudaMemcpyHostToDevice));
+  const uint8_t *W = e->weights;
+  e->tok_embd = W + off_te;
+  e->tok_type = te->type;
+  e->output = W + off_ow;
+  e->out_type = ow->type;
+  e->out_norm = reinterpret_cast<const float *>(W + off_on);
+  e->layers.resize(d.n_layers);
+  for (int l = 0; l < d.n_layers; ++l) {
+    LayerDev &Ld = e->layers[l];
+    const LOff &x = lo[l];
+    Ld.q = W + x.q; Ld.k = W + x.k; Ld.v = W + x.v; Ld.o = W + x.o;
+    Ld.gate = W + x.gate; Ld.up = W + x.up; Ld.down = W + x.down;
+    Ld.tq = x.tq; Ld.tk = x.tk; Ld.tv = x.tv; Ld.to = x.to; Ld.tgate = x.tg; Ld.tup = x.tu; Ld.tdown = x.td;
+    Ld.attn_norm = reinterpret_cast<const float *>(W + x.an);
+    Ld.ffn_norm = reinterpret_cast<const float *>(W + x.fn);
+    Ld.qb = x.hqb ? reinterpret_cast<const float *>(W + x.qb) : nullptr;
+    Ld.kb = x.hkb ? reinterpret_cast<const float *>(W + x.kb) : nullptr;
+    Ld.vb = x.hvb ? reinterpret_cast<const float *>(W + x.vb) : nullptr;
+    Ld.qn = x.hqn ? reinterpret_cast<const float *>(W + x.qn) : nullptr;
+    Ld.kn = x.hkn ? reinterpret_cast<const float *>(W + x.kn) : nullptr;
+  }
+  // RoPE table over MaxContextLen, angles in float64 (tensor/ops.go:237-257)
+  {
+    const int half = hd / 2;
+    std::vector<float> c(static_cast<size_t>(kMaxContext) * half), s(c.size());
+    for (int p = 0; p < kMaxContext; ++p)
+      for (int i = 0; i < half; ++i) {
+        const double freq = 1.0 / pow(static_cast<double>(d.rope_base), static_cast<double>(2 * i) / hd);
+        const double val = static_cast<double>(p) * freq;
+        c[static_cast<size_t>(p) * half + i] = static_cast<float>(cos(val));
+        s[static_cast<size_t>(p) * half + i] = static_cast<float>(sin(val));
+      }
+    CK(cudaMalloc(&e->rope_cos, c.size() * 4));
+    CK(cudaMalloc(&e->rope_sin, s.size() * 4));
+    CK(cudaMemcpy(e->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  }
+  // KV cache [2][L][KVH][max_tokens][hd] fp32 (engine/kvcache.go:31)
+  const size_t kvn = static_cast<size_t>(2) * d.n_layers * d.n_kv_heads * d.max_tokens * hd;
+  if (cudaMalloc(&e->kv, kvn * 4) != cudaSuccess) return fail(C2S_ERR_OOM, "KV cache: cudaMalloc(%zu) failed", kvn * 4);
+  CK(cudaMemset(e->kv, 0, kvn * 4));
+  e->max_splits = std::max(1, std::min(kMaxSplits, e->num_sms / d.n_kv_heads));
+  // largest split over n <= max_tokens: <= kMinSplitLen while the split count
+  // grows, ceil(n / max_splits) once it saturates
+  e->chunk_cap = std::max(kMinSplitLen, (d.max_tokens + e->max_splits - 1) / e->max_splits);
+  const int qpk = d.n_heads / d.n_kv_heads;
+  e->attn_smem = (static_cast<size_t>(qpk) * hd + 2 * hd + static_cast<size_t>(qpk) * e->chunk_cap) * 4;
+  if (e->attn_smem > 200 * 1024) return fail(C2S_ERR_UNSUPPORTED, "attention smem %zu too large", e->attn_smem);
+  auto dalloc = [&](void **p, size_t bytes) -> int {
+    if (cudaMalloc(p, bytes) != cudaSuccess) return fail(C2S_ERR_OOM, "cudaMalloc(%zu) failed", bytes);
+    if (cudaMemset(*p, 0, bytes) != cudaSuccess) return fail(C2S_ERR_CUDA, "cudaMemset failed");
+    return C2S_OK;
+  };
+  int rc;
+  if ((rc = dalloc(reinterpret_cast<void **>(&e->X), H * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->normx), H * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->q), H * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->k), kvd * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->v), kvd * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->attn_out), H * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->h), static_cast<size_t>(F) * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->logits), static_cast<size_t>(d.vocab) * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->part),
+                   static_cast<size_t>(d.n_heads) * e->max_splits * (hd + 2) * 4)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->amax_part), static_cast<size_t>(e->num_sms) * sizeof(float2))) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->token_ids), static_cast<size_t>(d.max_tokens) * 4)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->out_tokens), static_cast<size_t>(d.max_tokens) * 4 + 64)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->rows_idx), static_cast<size_t>(d.vocab) * 4)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->scratch_x), static_cast<size_t>(d.vocab) * 4)) ||
+      (rc = dalloc(reinterpret_cast<void **>(&e->st), sizeof(DevState))))
+    return rc;
+  CK(cudaMallocHost(&e->h_in, sizeof(HostFwdIn) * (d.max_tokens + 8)));
+  CK(cudaMallocHost(&e->h_buf, static_cast<size_t>(std::max(d.vocab, H)) * 4 + 64));
+  CK(cudaMallocHost(&e->h_st, sizeof(DevState)));
+  CK(cudaMallocHost(&e->h_tokens, static_cast<size_t>(d.max_tokens) * 4 + 64));
+  DevState s0{};
+  s0.penalty = 1.15f;  // c2slm.go:165-167
+  s0.window = 64;      // c2slm.go:157
+  s0.stop_on_special = 1;
+  s0.out_cap = d.max_tokens;
+  s0.im_end = d.im_end;
+  s0.eos = d.eos;
+  s0.vocab = d.vocab;
+  CK(cudaMemcpy(e->st, &s0, sizeof s0, cudaMemcpyHostToDevice));
+
+  // ---- kernels: shared-memory limits, graphs
+  CK(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  if ((rc = capture(e, &e->g_forward, 0)) || (rc = capture(e, &e->g_step, 1)) ||
+      (rc = capture(e, &e->g_logits, 2)) || (rc = capture(e, &e->g_fwd_select, 3))) {
+    if (!g_use_pdl) return rc;
+    // graphs with programmatic edges refused: capture plain launches instead
+    fprintf(stderr, "c2slm_b200: PDL capture failed (%s); using plain launches\n", g_err.c_str());
+    cudaGetLastError();
+    g_use_pdl = false;
+    for (cudaGraphExec_t *gx : {&e->g_forward, &e->g_step, &e->g_logits, &e->g_fwd_select})
+      if (*gx) { cudaGraphExecDestroy(*gx); *gx = nullptr; }
+    if ((rc = capture(e, &e->g_forward, 0)) || (rc = capture(e, &e->g_step, 1)) ||
+        (rc = capture(e, &e->g_logits, 2)) || (rc = capture(e, &e->g_fwd_select, 3)))
+      return rc;
+  }
+  e->kernels_per_step = 5 * d.n_layers + 1;
+  CK(cudaStreamSynchronize(e->stream));
+  return C2S_OK;
+}
+
+void engine_free(c2s_engine *e) {
+  if (!e) return;
+  DeviceGuard g(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (cudaGraphExec_t *gx : {&e->g_forward, &e->g_step, &e->g_logits, &e->g_fwd_select})
+    if (*gx) cudaGraphExecDestroy(*gx);
+  for (void *p : {static_cast<void *>(e->weights), static_cast<void *>(e->kv), static_cast<void *>(e->rope_cos),
+                  static_cast<void *>(e->rope_sin), static_cast<void *>(e->X), static_cast<void *>(e->normx),
+                  static_cast<void *>(e->q), static_cast<void *>(e->k), static_cast<void *>(e->v),
+                  static_cast<void *>(e->attn_out), static_cast<void *>(e->h), static_cast<void *>(e->logits),
+                  static_cast<void *>(e->part), static_cast<void *>(e->amax_part), static_cast<void *>(e->token_ids),
+                  static_cast<void *>(e->out_tokens), static_cast<void *>(e->rows_idx),
+                  static_cast<void *>(e->scratch_x), static_cast<void *>(e->st)})
+    if (p) cudaFree(p);
+  for (void *p : {static_cast<void *>(e->h_in), static_cast<void *>(e->h_buf), static_cast<void *>(e->h_st),
+                  static_cast<void *>(e->h_tokens)})
+    if (p) cudaFreeHost(p);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+// per-device context for the op-level entry points
+struct OpCtx {
+  cudaStream_t stream = nullptr;
+  DevState *st = nullptr;
+  bool ready = false;
+};
+std::mutex g_op_mu;
+OpCtx g_op[64];
+
+int op_ctx(int device, OpCtx **out) {
+  if (device < 0 || device >= 64) return fail(C2S_ERR_ARG, "device %d out of range", device);
+  std::lock_guard<std::mutex> lk(g_op_mu);
+  OpCtx &c = g_op[device];
+  if (!c.ready) {
+    CK(cudaSetDevice(device));
+    CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+    CK(cudaMalloc(&c.st, sizeof(DevState)));
+    CK(cudaMemset(c.st, 0, sizeof(DevState)));
+    CK(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    c.ready = true;
+  }
+  *out = &c;
+  return C2S_OK;
+}
+
+int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+// RAW matvec launch on device pointers
+int gemv_launch(OpCtx *c, int type, const void *dw, const float *dx, float *dy, int rows, int cols, int32_t *dbg) {
+  if (int rc = check_matrix(type, rows, cols, "gemv")) return rc;
+  int nsm = 148;
+  int dev = current_device();
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  MatParams P{};
+  P.kind = K_RAW;
+  P.nseg = 1;
+  P.cols = cols;
+  P.seg[0] = make_seg(static_cast<const uint8_t *>(dw), type, rows, cols, nullptr, dy);
+  P.x_in = dx;
+  P.st = c->st;
+  P.dbg = dbg;
+  finish_needs(P);
+  layout_matvec(P, nsm);
+  CK(launch(k_matvec, dim3(nsm), dim3(kThreads), P.smem_bytes, c->stream, P));
+  return C2S_OK;
+}
+
+template <class T>
+struct DevBuf {
+  T *p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  int alloc(size_t n) {
+    if (cudaMalloc(&p, n * sizeof(T) + 64) != cudaSuccess) return fail(C2S_ERR_OOM, "cudaMalloc failed");
+    cudaMemset(p, 0, n * sizeof(T) + 64);
+    return C2S_OK;
+  }
+};
+
+int op_finish(OpCtx *c) {
+  CK(cudaStreamSynchronize(c->stream));
+  unsigned err = 0;
+  CK(cudaMemcpy(&err, &c->st->err, sizeof err, cudaMemcpyDeviceToHost));
+  if (err) {
+    cudaMemset(&c->st->err, 0, sizeof(unsigned));
+    return fail(C2S_ERR_TIMEOUT, "device reported error flags 0x%x", err);
+  }
+  return C2S_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+const char *c2s_last_error(void) { return g_err.c_str(); }
+const char *c2s_version(void) { return "c2slm_b200 0.1 sm_100a"; }
+
+int c2s_engine_create(const c2s_model_desc *desc, const c2s_tensor_desc *tensors, int n_tensors, int device,
+                      c2s_engine **out) {
+  if (!desc || !tensors || n_tensors <= 0 || !out) return fail(C2S_ERR_ARG, "null argument");
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(C2S_ERR_CUDA, "no CUDA device");
+  if (device < 0 || device >= ndev) return fail(C2S_ERR_ARG, "device %d of %d", device, ndev);
+  DeviceGuard g(device);
+  auto *e = new c2s_engine();
+  e->device = device;
+  const int rc = engine_build(e, desc, tensors, n_tensors);
+  if (rc != C2S_OK) {
+    const std::string msg = g_err;
+    engine_free(e);
+    g_err = msg;
+    return rc;
+  }
+  *out = e;
+  return C2S_OK;
+}
+
+int c2s_engine_open(const char *path, int device, int max_tokens, c2s_engine **out) {
+  if (!path || !out) return fail(C2S_ERR_ARG, "null argument");
+  std::unique_ptr<GFile> f;
+  if (int rc = gguf_open(path, f)) return rc;
+  // engine/model.go:64-112: qwen2.* keys, then qwen3.*, then defaults
+  c2s_model_desc d{};
+  uint32_t u;
+  auto hp = [&](const char *k2, const char *k3, int dflt) {
+    u = 0;
+    f->u32(k2, &u);
+    if (u == 0) f->u32(k3, &u);
+    if (u == 0) u = static_cast<uint32_t>(dflt);
+    return static_cast<int32_t>(u);
+  };
+  d.embd = hp("qwen2.embedding_length", "qwen3.embedding_length", 896);
+  d.n_layers = hp("qwen2.block_count", "qwen3.block_count", 24);
+  d.n_heads = hp("qwen2.attention.head_count", "qwen3.attention.head_count", 14);
+  d.n_kv_heads = hp("qwen2.attention.head_count_kv", "qwen3.attention.head_count_kv", 2);
+  d.ffn = hp("qwen2.feed_forward_length", "qwen3.feed_forward_length", 4864);
+  float fv = 0;
+  f->f32("qwen2.rope.freq_base", &fv);
+  if (fv == 0) f->f32("qwen3.rope.freq_base", &fv);
+  d.rope_base = fv == 0 ? 1000000.0f : fv;
+  fv = 0;
+  f->f32("qwen2.attention.layer_norm_rms_epsilon", &fv);
+  if (fv == 0) f->f32("qwen3.attention.layer_norm_rms_epsilon", &fv);
+  d.eps = fv == 0 ? 1e-6f : fv;
+  d.max_tokens = max_tokens > 0 ? max_tokens : kMaxContext;
+  d.im_end = f->im_end;
+  d.eos = f->eos;
+  std::vector<c2s_tensor_desc> ts(f->tensors.size());
+  for (size_t i = 0; i < ts.size(); ++i) {
+    const GTensor &t = f->tensors[i];
+    ts[i].name = t.name.c_str();
+    ts[i].type = t.type;
+    ts[i].n_dims = t.n_dims;
+    for (int k = 0; k < 4; ++k) ts[i].dims[k] = t.dims[k];
+    ts[i].data = t.data;
+    ts[i].nbytes = t.nbytes;
+  }
+  return c2s_engine_create(&d, ts.data(), static_cast<int>(ts.size()), device, out);
+}
+
+void c2s_engine_close(c2s_engine *e) { engine_free(e); }
+
+int c2s_engine_desc(const c2s_engine *e, c2s_model_desc *out) {
+  if (!e || !out) return fail(C2S_ERR_ARG, "null argument");
+  *out = e->d;
+  return C2S_OK;
+}
+
+int c2s_forward(c2s_engine *e, int32_t token, int32_t pos, float *normx_out) {
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  if (pos < 0 || pos >= e->d.max_tokens) return fail(C2S_ERR_ARG, "pos %d outside [0, %d)", pos, e->d.max_tokens);
+  DeviceGuard g(e->device);
+  if (int rc = set_fwd_input(e, token, pos, 0)) return rc;
+  CK(cudaGraphLaunch(e->g_forward, e->stream));
+  if (normx_out) CK(cudaMemcpyAsync(e->h_buf, e->normx, e->d.embd * 4, cudaMemcpyDeviceToHost, e->stream));
+  if (int rc = read_status(e)) return rc;
+  if (normx_out) memcpy(normx_out, e->h_buf, e->d.embd * 4);
+  return C2S_OK;
+}
+
+int c2s_compute_logits(c2s_engine *e, const float *normx_in, const int32_t *targets, int n_targets,
+                       float *logits_out) {
+  if (!e || !logits_out) return fail(C2S_ERR_ARG, "null argument");
+  if (n_targets < 0) return fail(C2S_ERR_ARG, "n_targets < 0");
+  DeviceGuard g(e->device);
+  if (normx_in) {
+    memcpy(e->h_buf, normx_in, e->d.embd * 4);
+    CK(cudaMemcpyAsync(e->normx, e->h_buf, e->d.embd * 4, cudaMemcpyHostToDevice, e->stream));
+  }
+  if (targets && n_targets > 0) {
+    if (n_targets > e->d.vocab) return fail(C2S_ERR_ARG, "too many targets");
+    memcpy(e->h_tokens, targets, static_cast<size_t>(n_targets) * 4);
+    CK(cudaMemcpyAsync(e->rows_idx, e->h_tokens, static_cast<size_t>(n_targets) * 4, cudaMemcpyHostToDevice,
+                       e->stream));
+    k_dot_rows_f32x<<<n_targets, kThreads, 0, e->stream>>>(e->out_type, e->output,
+                                                           static_cast<int>(row_bytes_of(e->out_type, e->d.embd)),
+                                                           e->normx, e->rows_idx, n_targets, e->scratch_x,
+                                                           e->d.vocab, e->d.embd);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(e->h_buf, e->scratch_x, static_cast<size_t>(n_targets) * 4, cudaMemcpyDeviceToHost,
+                       e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n_targets; ++i) {
+      const int t = targets[i];
+      if (t < 0 || t >= e->d.vocab) continue;  // engine/forward.go:177-179
+      logits_out[t] = e->h_buf[i];
+    }
+    return C2S_OK;
+  }
+  CK(cudaGraphLaunch(e->g_logits, e->stream));
+  CK(cudaMemcpyAsync(e->h_buf, e->logits, static_cast<size_t>(e->d.vocab) * 4, cudaMemcpyDeviceToHost, e->stream));
+  if (int rc = read_status(e)) return rc;
+  memcpy(logits_out, e->h_buf, static_cast<size_t>(e->d.vocab) * 4);
+  return C2S_OK;
+}
+
+int c2s_kv_seq_len(const c2s_engine *e) {
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  return e->host_seq;
+}
+
+int c2s_kv_set_seq_len(c2s_engine *e, int seq_len) {
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  if (seq_len < 0 || seq_len > e->d.max_tokens) return fail(C2S_ERR_ARG, "seq_len %d out of range", seq_len);
+  DeviceGuard g(e->device);
+  e->h_st->seq_len = seq_len;
+  CK(cudaMemcpyAsync(&e->st->seq_len, &e->h_st->seq_len, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  e->host_seq = seq_len;
+  return C2S_OK;
+}
+
+int c2s_kv_reset(c2s_engine *e) { return c2s_kv_set_seq_len(e, 0); }
+
+int c2s_kv_rewind(c2s_engine *e, int n) {  // engine/kvcache.go:109-117
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  if (n < 0) n = 0;
+  if (n > e->host_seq) n = e->host_seq;
+  return c2s_kv_set_seq_len(e, e->host_seq - n);
+}
+
+int c2s_kv_store_token_id(c2s_engine *e, int pos, int32_t token) {  // engine/kvcache.go:120-125
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  if (pos < 0 || pos >= e->d.max_tokens) return C2S_OK;  // ignored like the reference
+  DeviceGuard g(e->device);
+  e->h_tokens[0] = token;
+  CK(cudaMemcpyAsync(e->token_ids + pos, e->h_tokens, 4, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  return C2S_OK;
+}
+
+int c2s_kv_token_ids(const c2s_engine *e, int32_t *out, int n) {
+  if (!e || !out) return fail(C2S_ERR_ARG, "null argument");
+  if (n < 0 || n > e->d.max_tokens) return fail(C2S_ERR_ARG, "n out of range");
+  DeviceGuard g(e->device);
+  CK(cudaMemcpy(out, e->token_ids, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost));
+  return C2S_OK;
+}
+
+int c2s_kv_get(const c2s_engine *e, int is_value, int layer, int kv_head, int pos, float *out) {
+  if (!e || !out) return fail(C2S_ERR_ARG, "null argument");
+  if (layer < 0 || layer >= e->d.n_layers || kv_head < 0 || kv_head >= e->d.n_kv_heads || pos < 0 ||
+      pos >= e->d.max_tokens)
+    return fail(C2S_ERR_ARG, "kv index out of range");
+  DeviceGuard g(e->device);
+  const size_t hd = e->d.head_dim;
+  const size_t plane = static_cast<size_t>(e->d.n_layers) * e->d.n_kv_heads * e->d.max_tokens * hd;
+  const size_t off = (is_value ? plane : 0) +
+                     ((static_cast<size_t>(layer) * e->d.n_kv_heads + kv_head) * e->d.max_tokens + pos) * hd;
+  CK(cudaMemcpy(out, e->kv + off, hd * 4, cudaMemcpyDeviceToHost));
+  return C2S_OK;
+}
+
+int c2s_ingest_from(c2s_engine *e, int pos, const int32_t *tokens, int n, float *last_normx_out) {
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  if (n <= 0) return 0;
+  if (!tokens) return fail(C2S_ERR_ARG, "null tokens");
+  DeviceGuard g(e->device);
+  // c2slm.go:96-104: clamp into [0, SeqLen] and rewind in place
+  if (pos < 0) pos = 0;
+  if (pos > e->host_seq) pos = e->host_seq;
+  if (pos < e->host_seq)
+    if (int rc = c2s_kv_set_seq_len(e, pos)) return rc;
+  int done = 0;
+  for (int i = 0; i < n; ++i) {
+    const int p = pos + i;
+    if (p >= e->d.max_tokens) break;
+    if (int rc = set_fwd_input(e, tokens[i], p, 1)) return rc;
+    CK(cudaGraphLaunch(e->g_forward, e->stream));
+    ++done;
+  }
+  if (done > 0 && last_normx_out)
+    CK(cudaMemcpyAsync(e->h_buf, e->normx, e->d.embd * 4, cudaMemcpyDeviceToHost, e->stream));
+  if (int rc = read_status(e)) return rc;
+  if (done > 0 && last_normx_out) memcpy(last_normx_out, e->h_buf, e->d.embd * 4);
+  return done;
+}
+
+static int set_gen_state(c2s_engine *e, float penalty, int window, int stop_on_special) {
+  // halted, halt_pending, stop_on_special, window, penalty, n_out (contiguous)
+  DevState *h = e->h_st;
+  h->halted = 0;
+  h->halt_pending = 0;
+  h->stop_on_special = stop_on_special ? 1 : 0;
+  h->window = window;
+  h->penalty = penalty;
+  h->n_out = 0;
+  const size_t off = offsetof(DevState, halted);
+  const size_t len = offsetof(DevState, out_cap) - off;
+  CK(cudaMemcpyAsync(reinterpret_cast<uint8_t *>(e->st) + off, reinterpret_cast<uint8_t *>(h) + off, len,
+                     cudaMemcpyHostToDevice, e->stream));
+  return C2S_OK;
+}
+
+int c2s_generate(c2s_engine *e, int max_new, float penalty, int window, int stop_on_special, int32_t *tokens_out,
+                 int *n_out) {
+  if (!e || !n_out) return fail(C2S_ERR_ARG, "null argument");
+  if (max_new > 0 && !tokens_out) return fail(C2S_ERR_ARG, "null tokens_out");
+  if (window < 0) return fail(C2S_ERR_ARG, "window < 0");
+  *n_out = 0;
+  DeviceGuard g(e->device);
+  // c2slm.go:78-80 / 149-151: never past the KV capacity
+  const int remaining = e->d.max_tokens - e->host_seq;
+  if (max_new > remaining) max_new = remaining;
+  if (max_new <= 0) return C2S_OK;
+  if (e->host_seq <= 0) return fail(C2S_ERR_STATE, "generate needs a forwarded prefix (SeqLen == 0)");
+  if (int rc = set_gen_state(e, penalty, window, stop_on_special)) return rc;
+  for (int i = 0; i < max_new; ++i) CK(cudaGraphLaunch(e->g_step, e->stream));
+  CK(cudaMemcpyAsync(e->h_tokens, e->out_tokens, static_cast<size_t>(max_new) * 4, cudaMemcpyDeviceToHost,
+                     e->stream));
+  if (int rc = read_status(e)) return rc;
+  const int n = std::min(e->h_st->n_out, max_new);
+  memcpy(tokens_out, e->h_tokens, static_cast<size_t>(n) * 4);
+  *n_out = n;
+  return C2S_OK;
+}
+
+int c2s_decode_step(c2s_engine *e, int32_t token, float penalty, int window, int32_t *next_out) {
+  if (!e || !next_out) return fail(C2S_ERR_ARG, "null argument");
+  if (e->host_seq >= e->d.max_tokens) return fail(C2S_ERR_STATE, "KV cache full");
+  DeviceGuard g(e->device);
+  if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
+  if (int rc = set_fwd_input(e, token, e->host_seq, 1)) return rc;
+  CK(cudaGraphLaunch(e->g_fwd_select, e->stream));
+  CK(cudaMemcpyAsync(e->h_tokens, e->out_tokens, 4, cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  *next_out = e->h_tokens[0];
+  e->host_seq += 1;
+  return C2S_OK;
+}
+
+int c2s_engine_sync(c2s_engine *e) {
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  DeviceGuard g(e->device);
+  return read_status(e);
+}
+
+int c2s_bench_decode(c2s_engine *e, int n_steps, float penalty, int window) {
+  if (!e) return fail(C2S_ERR_ARG, "null engine");
+  if (n_steps > e->d.max_tokens - e->host_seq) return fail(C2S_ERR_ARG, "n_steps exceeds KV capacity");
+  DeviceGuard g(e->device);
+  if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
+  for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(e->g_step, e->stream));
+  e->host_seq += n_steps;  // confirmed by the next read_status
+  return C2S_OK;
+}
+
+int c2s_kernels_per_step(const c2s_engine *e) { return e ? e->kernels_per_step : 0; }
+
+int c2s_bench_decode_timed(c2s_engine *e, int n_steps, float penalty, int window, int period, float *ms_out) {
+  if (!e || !ms_out) return fail(C2S_ERR_ARG, "null argument");
+  const int span = period > 0 ? std::min(period, n_steps) : n_steps;
+  if (n_steps <= 0 || span > e->d.max_tokens - e->host_seq) return fail(C2S_ERR_ARG, "n_steps out of range");
+  DeviceGuard g(e->device);
+  if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
+  // every `period` steps SeqLen is rewound to its value at entry (KVCache.Rewind:
+  // no copy), so the decoded positions stay in [base, base + period)
+  e->h_st->fwd_token = e->host_seq;  // pinned source for the rewinds
+  cudaEvent_t a, b;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&b));
+  CK(cudaEventRecord(a, e->stream));
+  for (int i = 0; i < n_steps; ++i) {
+    if (period > 0 && i > 0 && i % period == 0)
+      CK(cudaMemcpyAsync(&e->st->seq_len, &e->h_st->fwd_token, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    CK(cudaGraphLaunch(e->g_step, e->stream));
+  }
+  CK(cudaEventRecord(b, e->stream));
+  CK(cudaEventSynchronize(b));
+  CK(cudaEventElapsedTime(ms_out, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return read_status(e);
+}
+
+int c2s_profile_step(c2s_engine *e, int n_steps, float penalty, int window, float *stage_ms, int *stage_launches) {
+  if (!e || !stage_ms || !stage_launches) return fail(C2S_ERR_ARG, "null argument");
+  if (n_steps <= 0 || n_steps > e->d.max_tokens - e->host_seq) return fail(C2S_ERR_ARG, "n_steps out of range");
+  DeviceGuard g(e->device);
+  if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kind;
+  KTimer tm{&ev, &kind};
+  cudaError_t err = cudaSuccess;
+  for (int i = 0; i < n_steps && !err; ++i) {
+    err = enqueue_logits(e, e->stream, true, false, true, &tm);
+    if (!err) err = enqueue_forward(e, e->stream, true, false, &tm);
+  }
+  if (err) return fail(C2S_ERR_CUDA, "profile launch: %s", cudaGetErrorString(err));
+  CK(cudaStreamSynchronize(e->stream));
+  for (int k = 0; k < 8; ++k) {
+    stage_ms[k] = 0.f;
+    stage_launches[k] = 0;
+  }
+  for (size_t i = 0; i < kind.size(); ++i) {
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, ev[2 * i], ev[2 * i + 1]));
+    stage_ms[kind[i]] += ms;
+    stage_launches[kind[i]] += 1;
+  }
+  for (auto x : ev) cudaEventDestroy(x);
+  return read_status(e);
+}
+
+// ---- op-level entry points ------------------------------------------------
+int c2s_quantize_row_q8_k(const float *x, uint8_t *y, int cols) {
+  if (!x || !y) return fail(C2S_ERR_ARG, "null argument");
+  if (cols <= 0 || cols % 256) return fail(C2S_ERR_ARG, "cols must be a positive multiple of 256");
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  DevBuf<float> dx;
+  DevBuf<uint8_t> dy;
+  const size_t ybytes = static_cast<size_t>(cols / 256) * 292;
+  if (int rc = dx.alloc(cols)) return rc;
+  if (int rc = dy.alloc(ybytes)) return rc;
+  CK(cudaMemcpyAsync(dx.p, x, cols * 4, cudaMemcpyHostToDevice, c->stream));
+  const int nsb = cols / 256;
+  k_quantize_q8k<<<(nsb + kWarps - 1) / kWarps, kThreads, 0, c->stream>>>(dx.p, dy.p, cols);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(y, dy.p, ybytes, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, int cols) {
+  if (!weight || !x || !y) return fail(C2S_ERR_ARG, "null argument");
+  if (int rc = check_matrix(type, rows, cols, "gemv")) return rc;
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  const size_t wb = row_bytes_of(type, cols) * rows;
+  DevBuf<uint8_t> dw;
+  DevBuf<float> dx, dy;
+  if (int rc = dw.alloc(wb)) return rc;
+  if (int rc = dx.alloc(cols)) return rc;
+  if (int rc = dy.alloc(rows)) return rc;
+  CK(cudaMemcpyAsync(dw.p, weight, wb, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c->stream));
+  if (int rc = gemv_launch(c, type, dw.p, dx.p, dy.p, rows, cols, nullptr)) return rc;
+  CK(cudaMemcpyAsync(y, dy.p, static_cast<size_t>(rows) * 4, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x, float *d_y, int rows, int cols) {
+  if (!d_weight || !d_x || !d_y) return fail(C2S_ERR_ARG, "null argument");
+  if (reinterpret_cast<uintptr_t>(d_weight) & 255) return fail(C2S_ERR_ARG, "d_weight must be 256-byte aligned");
+  OpCtx *c;
+  if (int rc = op_ctx(device, &c)) return rc;
+  DeviceGuard g(device);
+  return gemv_launch(c, type, d_weight, d_x, d_y, rows, cols, nullptr);
+}
+
+int c2s_kquant_partials(int type, const void *weight, const float *x, int32_t *dots, int rows, int cols) {
+  if (!weight || !x || !dots) return fail(C2S_ERR_ARG, "null argument");
+  if (!is_kquant(type)) return fail(C2S_ERR_ARG, "partials exist for Q4_K and Q6_K only");
+  if (int rc = check_matrix(type, rows, cols, "partials")) return rc;
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  const size_t wb = row_bytes_of(type, cols) * rows;
+  const size_t nd = static_cast<size_t>(rows) * (cols / 256) * (type == T_Q4_K ? 8 : 1);
+  DevBuf<uint8_t> dw;
+  DevBuf<float> dx, dy;
+  DevBuf<int32_t> dd;
+  if (int rc = dw.alloc(wb)) return rc;
+  if (int rc = dx.alloc(cols)) return rc;
+  if (int rc = dy.alloc(rows)) return rc;
+  if (int rc = dd.alloc(nd)) return rc;
+  CK(cudaMemcpyAsync(dw.p, weight, wb, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c->stream));
+  if (int rc = gemv_launch(c, type, dw.p, dx.p, dy.p, rows, cols, dd.p)) return rc;
+  CK(cudaMemcpyAsync(dots, dd.p, nd * 4, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+int c2s_dot_rows_f32x(int type, const void *weight, const float *x, const int32_t *rows_idx, int n, float *out,
+                      int rows, int cols) {
+  if (!weight || !x || !rows_idx || !out) return fail(C2S_ERR_ARG, "null argument");
+  if (int rc = check_matrix(type, rows, cols, "dot_rows")) return rc;
+  if (n <= 0) return C2S_OK;
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  const size_t wb = row_bytes_of(type, cols) * rows;
+  DevBuf<uint8_t> dw;
+  DevBuf<float> dx, dout;
+  DevBuf<int> di;
+  if (int rc = dw.alloc(wb)) return rc;
+  if (int rc = dx.alloc(cols)) return rc;
+  if (int rc = dout.alloc(n)) return rc;
+  if (int rc = di.alloc(n)) return rc;
+  CK(cudaMemcpyAsync(dw.p, weight, wb, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(di.p, rows_idx, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+  k_dot_rows_f32x<<<n, kThreads, 0, c->stream>>>(type, dw.p, static_cast<int>(row_bytes_of(type, cols)), dx.p, di.p,
+                                                  n, dout.p, rows, cols);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(out, dout.p, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+int c2s_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
+  if (!out || !x || !w || n <= 0) return fail(C2S_ERR_ARG, "bad argument");
+  if (n > 48 * 1024) return fail(C2S_ERR_ARG, "n too large");
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  DevBuf<float> dx, dw, dout;
+  if (int rc = dx.alloc(n)) return rc;
+  if (int rc = dw.alloc(n)) return rc;
+  if (int rc = dout.alloc(n)) return rc;
+  CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(dw.p, w, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaFuncSetAttribute(k_rmsnorm_op, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  k_rmsnorm_op<<<1, kThreads, static_cast<size_t>(n) * 4, c->stream>>>(dout.p, dx.p, dw.p, n, eps);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(out, dout.p, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+int c2s_swiglu(float *out, const float *gate, const float *up, int n) {
+  if (!out || !gate || !up || n <= 0) return fail(C2S_ERR_ARG, "bad argument");
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  DevBuf<float> dg, du, dout;
+  if (int rc = dg.alloc(n)) return rc;
+  if (int rc = du.alloc(n)) return rc;
+  if (int rc = dout.alloc(n)) return rc;
+  CK(cudaMemcpyAsync(dg.p, gate, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(du.p, up, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
+  k_swiglu_op<<<(n + 255) / 256, 256, 0, c->stream>>>(dout.p, dg.p, du.p, n);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(out, dout.p, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+int c2s_dequant_row(int type, const void *row, float *out, int cols) {
+  if (!row || !out || cols <= 0) return fail(C2S_ERR_ARG, "bad argument");
+  const size_t rb = row_bytes_of(type, cols);
+  if (!rb) return fail(C2S_ERR_UNSUPPORTED, "type %d", type);
+  OpCtx *c;
+  if (int rc = op_ctx(current_device(), &c)) return rc;
+  DevBuf<uint8_t> dr;
+  DevBuf<float> dout;
+  if (int rc = dr.alloc(rb)) return rc;
+  if (int rc = dout.alloc(cols)) return rc;
+  CK(cudaMemcpyAsync(dr.p, row, rb, cudaMemcpyHostToDevice, c->stream));
+  k_dequant_op<<<1, kThreads, 0, c->stream>>>(type, dr.p, dout.p, cols);
+  CK(cudaGetLastError());
+  CK(cudaMemcpyAsync(out, dout.p, static_cast<size_t>(cols) * 4, cudaMemcpyDeviceToHost, c->stream));
+  return op_finish(c);
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+"""Model-level GPU parity: engine.Forward / ComputeLogits / generate against the
+CPU oracle on seeded synthetic models (the reference's integration tests,
+c2slm_test.go and engine/forward_test.go, need a real checkpoint; synthetic
+GGUFs with the same layouts stand in for it).
+
+Bars: NormX and logits within 1e-3 of max|ref|; greedy ids identical, where a
+divergence is accepted only at a step whose oracle top-1/top-2 margin is below
+1e-3 * max|logit| (a tolerance tie).
+"""
+import numpy as np
+import pytest
+
+import c2slm_b200 as K
+from c2slm_b200 import synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def rel(got, ref):
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(np.asarray(got, np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def assert_greedy_parity(got, want, margins, maxabs, min_steps):
+    n = min(len(got), len(want))
+    for i in range(n):
+        if got[i] != want[i]:
+            tie = margins[i] < 1e-3 * maxabs[i]
+            assert tie, f"step {i}: gpu {got[i]} != oracle {want[i]} (margin {margins[i]:.3e}, max {maxabs[i]:.3e})"
+            return i
+    assert len(got) == len(want)
+    assert n >= min_steps
+    return n
+
+
+@pytest.fixture(scope="module")
+def models(model_cache):
+    return {name: synth.cached_model(name, cache_dir=model_cache) for name in ("tiny05", "tiny15", "tiny7", "tiny3")}
+
+
+@pytest.mark.parametrize("name", ["tiny05", "tiny15", "tiny7", "tiny3"])
+def test_forward_and_logits_match_oracle(models, name):
+    path = models[name]
+    with K.Engine(path, max_tokens=256) as e, O.OracleModel(path, max_tokens=256, nthreads=4) as o:
+        rng = np.random.default_rng(7)
+        toks = rng.integers(0, e.desc.vocab, 40).astype(np.int32)
+        for p, t in enumerate(toks):
+            g = e.forward(int(t), p)
+            w = o.forward(int(t), p)
+            assert rel(g, w) <= TOL, (p, rel(g, w))
+        lg = e.compute_logits()
+        lw = o.compute_logits(w)
+        assert rel(lg, lw) <= TOL, rel(lg, lw)
+        # caller-supplied NormX path
+        lg2 = e.compute_logits(normx=w)
+        assert rel(lg2, lw) <= TOL
+        # KV cache contents (KVCache.GetKey/GetValue)
+        for layer in (0, e.desc.n_layers - 1):
+            for pos in (0, 17, 39):
+                assert rel(e.get_key(layer, 1, pos), o.kv_get(0, layer, 1, pos)) <= TOL
+                assert rel(e.get_value(layer, 0, pos), o.kv_get(1, layer, 0, pos)) <= TOL
+        # Forward does not touch SeqLen (engine/forward.go:54-138)
+        assert e.seq_len == 0
+
+
+@pytest.mark.parametrize("name", ["tiny05", "tiny15", "tiny7", "tiny3"])
+def test_generate_greedy_parity(models, name):
+    path = models[name]
+    with K.Engine(path, max_tokens=512) as e, O.OracleModel(path, max_tokens=512, nthreads=4) as o:
+        rng = np.random.default_rng(3)
+        prompt = rng.integers(0, e.desc.vocab - 3, 24).astype(np.int32)
+        nx_g = e.ingest_from(0, prompt)
+        nx_o = o.ingest_from(0, prompt)
+        assert rel(nx_g, nx_o) <= TOL
+        assert e.seq_len == len(prompt) == o.seq_len
+        assert np.array_equal(e.token_ids(), prompt)
+        got = e.generate(96, penalty=1.15, window=64, stop_on_special=True)
+        want, margins, maxabs = o.generate(nx_o, 96, penalty=1.15, window=64, stop_on_special=True)
+        k = assert_greedy_parity(got, want, margins, maxabs, min_steps=1)
+        if k == len(want):
+            assert e.seq_len == o.seq_len
+            assert np.array_equal(e.token_ids(), o.token_ids(o.seq_len))
+
+
+def test_chunked_ingestion_equals_one_shot(models):
+    """c2slm_test.go:42-89: prefix then suffix gives the one-shot logits, the
+    fingerprint is recorded, and a session turn grows the cache."""
+    with K.Engine(models["tiny15"], max_tokens=256) as e:
+        toks = np.arange(5, 37, dtype=np.int32) * 7 % e.desc.vocab
+        e.reset()
+        e.ingest_from(0, toks)
+        ref = e.compute_logits()
+        e.reset()
+        split = len(toks) // 2
+        e.ingest_from(0, toks[:split])
+        e.ingest_from(split, toks[split:])
+        assert e.seq_len == len(toks)
+        assert np.array_equal(e.token_ids(), toks)
+        got = e.compute_logits()
+        assert np.abs(got - ref).max() <= 1e-5
+        before = e.seq_len
+        e.generate_stream_session(np.array([3, 4, 5], np.int32), 4)
+        assert before < e.seq_len <= e.max_tokens
+
+
+def test_rewind_and_clamp_semantics(models):
+    """IngestFrom clamps pos into [0, SeqLen] and rewinds without copying
+    (c2slm.go:92-115, engine/kvcache.go:101-117)."""
+    with K.Engine(models["tiny05"], max_tokens=128) as e:
+        toks = np.arange(1, 21, dtype=np.int32)
+        e.ingest_from(0, toks)
+        assert e.seq_len == 20
+        e.rewind(5)
+        assert e.seq_len == 15
+        e.rewind(100)
+        assert e.seq_len == 0
+        e.ingest_from(0, toks)
+        e.ingest_from(50, toks[:2])  # pos > SeqLen is clamped to SeqLen
+        assert e.seq_len == 22
+        e.ingest_from(-3, toks[:4])  # negative pos -> 0, rewinds to 0
+        assert e.seq_len == 4
+        # capacity: ingestion stops at MaxTokens
+        e.reset()
+        e.ingest_from(0, np.arange(140, dtype=np.int32) % 100)
+        assert e.seq_len == 128
+        assert len(e.generate(10)) == 0
+
+
+def test_restricted_logits_match_full(models):
+    """engine/forward_test.go:123-172 (Q8_0 output: both paths use f32 x)."""
+    with K.Engine(models["tiny05"], max_tokens=64) as e:
+        nx = e.forward(5, 0)
+        full = e.compute_logits(normx=nx)
+        targets = np.array([0, 1, 100, 200, 300, 1000, 2000, 2047, -1, 99999], np.int32)
+        out = np.full(e.desc.vocab, np.nan, np.float32)
+        e.compute_logits(normx=nx, targets=targets, out=out)
+        for t in targets:
+            if 0 <= t < e.desc.vocab:
+                assert abs(out[t] - full[t]) <= 1e-5 * max(1.0, abs(full[t]))
+
+
+def test_stop_on_special_forwards_the_stop_token(models):
+    """c2slm.go:183-189: selecting im_end/eos forwards it, records it, stops."""
+    path = models["tiny05"]
+    with K.Engine(path, max_tokens=256) as e, O.OracleModel(path, max_tokens=256, nthreads=2) as o:
+        # find a prompt whose first selection is special by scanning with a
+        # huge penalty window on everything else is not possible; instead
+        # compare the full stop behaviour with the oracle on several prompts.
+        for seed in range(3):
+            prompt = np.random.default_rng(seed).integers(0, 2000, 8).astype(np.int32)
+            e.reset(); o.reset()
+            e.ingest_from(0, prompt)
+            nx = o.ingest_from(0, prompt)
+            got = e.generate(40, stop_on_special=True)
+            want, m, mx = o.generate(nx, 40, stop_on_special=True)
+            assert_greedy_parity(got, want, m, mx, 1)
+            assert e.seq_len == o.seq_len
+
+
+def test_decode_step_matches_generate(models):
+    path = models["tiny15"]
+    with K.Engine(path, max_tokens=256) as e:
+        prompt = np.arange(10, 26, dtype=np.int32)
+        e.ingest_from(0, prompt)
+        ref = e.generate(12, stop_on_special=False)
+        e.reset()
+        e.ingest_from(0, prompt[:-1])
+        tok = int(prompt[-1])
+        got = []
+        for _ in range(12):
+            tok = e.decode_step(tok)
+            got.append(tok)
+        assert got == list(ref)
+
+
+def test_engine_from_caller_mapped_tensors(models):
+    """c2s_engine_create: the cgo path, tensors mapped by the caller's reader."""
+    from c2slm_b200 import gguf
+    path = models["tiny7"]
+    with gguf.File(path) as f:
+        e = K.Engine(gguf_file=f, max_tokens=64)
+    with e, K.Engine(path, max_tokens=64) as e2:
+        assert np.array_equal(e.forward(11, 0), e2.forward(11, 0))
+
+
+@pytest.mark.slow
+def test_qwen05b_config1_greedy_64_steps(model_cache):
+    """BASELINE config 1 (0.5B-shaped, Q5_0/Q4_K/Q6_K/Q8_0): 32-token prompt,
+    >= 64 greedy steps identical to the oracle."""
+    path = synth.cached_model("qwen05b", cache_dir=model_cache)
+    with K.Engine(path, max_tokens=512) as e, O.OracleModel(path, max_tokens=512, nthreads=8) as o:
+        prompt = np.random.default_rng(0).integers(0, 151643, 32).astype(np.int32)
+        nx_g = e.ingest_from(0, prompt)
+        nx_o = o.ingest_from(0, prompt)
+        assert rel(nx_g, nx_o) <= TOL
+        assert rel(e.compute_logits(), o.compute_logits(nx_o)) <= TOL
+        got = e.generate(64, stop_on_special=False)
+        want, m, mx = o.generate(nx_o, 64, stop_on_special=False)
+        assert_greedy_parity(got, want, m, mx, 64)
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["qwen15b", "qwen7b"])
+def test_large_shapes_reduced_depth(model_cache, name):
+    """BASELINE configs 2 and 3 at full width, 2 layers (oracle time bound)."""
+    path = synth.cached_model(name, layers=2, cache_dir=model_cache)
+    with K.Engine(path, max_tokens=128) as e, O.OracleModel(path, max_tokens=128, nthreads=8) as o:
+        prompt = np.random.default_rng(1).integers(0, 151643, 12).astype(np.int32)
+        nx_g = e.ingest_from(0, prompt)
+        nx_o = o.ingest_from(0, prompt)
+        assert rel(nx_g, nx_o) <= TOL
+        assert rel(e.compute_logits(), o.compute_logits(nx_o)) <= TOL
+        got = e.generate(8, stop_on_special=False)
+        want, m, mx = o.generate(nx_o, 8, stop_on_special=False)
+        assert_greedy_parity(got, want, m, mx, 8)

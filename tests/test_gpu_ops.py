@@ -1,0 +1,138 @@
+"""GPU parity of the kernel-level entry points against the CPU oracle.
+
+Bar (north_star): Q8_K bytes and K-quant int32 partials bit-exact; f32
+outputs within 1e-3 of max|ref| (max-abs normalised).  All calls go through
+the C ABI of libc2slm_b200.so.
+"""
+import numpy as np
+import pytest
+
+import c2slm_b200 as K
+from c2slm_b200 import synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3  # f32 outputs: max|got-ref| <= TOL * max|ref|
+
+
+def maxabs_rel(got, ref):
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(np.asarray(got, np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def rng():
+    return np.random.default_rng(1234)
+
+
+@pytest.mark.parametrize("cols", [256, 512, 4864, 8960, 18944])
+def test_quantize_row_q8k_bit_exact(rng, cols):
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    x[:256] *= 1e-3
+    if cols >= 512:
+        x[256:512] = 0.0  # all-zero superblock
+    if cols >= 1024:
+        # values on the +-0.5 rounding boundary after scaling by 127/amax
+        blk = x[512:768]
+        blk[:] = np.float32(0)
+        blk[0] = 127.0
+        blk[1:64] = np.arange(1, 64, dtype=np.float32) + np.float32(0.5)
+        blk[64:128] = -(np.arange(1, 65, dtype=np.float32) + np.float32(0.5))
+    got = K.quantize_row_q8_k(x)
+    want = O.quantize_row_q8_k(x)
+    assert np.array_equal(got, want), np.nonzero(got != want)[0][:10]
+
+
+@pytest.mark.parametrize("kind", [O.Q4_K, O.Q6_K])
+@pytest.mark.parametrize("rows,cols", [(5, 256), (37, 1536), (896, 4864), (3, 18944)])
+def test_kquant_partials_bit_exact(rng, kind, rows, cols):
+    w = synth.gen_blocks(rng, kind, rows, cols)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    q8 = O.quantize_row_q8_k(x)
+    got = K.kquant_partials(kind, w, x, rows, cols)
+    if kind == O.Q4_K:
+        want, _ = O.q4k_q8k_partials(w, q8, rows, cols)
+    else:
+        want = O.q6k_q8k_partials(w, q8, rows, cols)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("kind", [O.Q5_0, O.Q8_0, O.Q4_K, O.Q6_K])
+@pytest.mark.parametrize("rows,cols", [(1, 256), (7, 512), (128, 896), (300, 1536), (896, 4864)])
+def test_gemv_matches_oracle(rng, kind, rows, cols):
+    if kind in (O.Q4_K, O.Q6_K) and cols % 256:
+        pytest.skip("K-quants need cols % 256 == 0")
+    w = synth.gen_blocks(rng, kind, rows, cols)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    got = K.gemv(kind, w, x, rows, cols)
+    want = O.gemv(kind, w, x, rows, cols)
+    assert maxabs_rel(got, want) <= 1e-5, maxabs_rel(got, want)
+
+
+def test_config0_q4k_q8k_matvec(rng):
+    """896 x 4864 Q4_K (19 superblocks per row), x ~ N(0,1)."""
+    r = np.random.default_rng(0)
+    w = synth.gen_blocks(r, O.Q4_K, 896, 4864)
+    x = r.normal(0, 1, 4864).astype(np.float32)
+    q8 = O.quantize_row_q8_k(x)
+    assert np.array_equal(K.quantize_row_q8_k(x), q8)
+    dots, _ = O.q4k_q8k_partials(w, q8, 896, 4864)
+    assert np.array_equal(K.kquant_partials(O.Q4_K, w, x, 896, 4864), dots)
+    got = K.gemv(O.Q4_K, w, x, 896, 4864)
+    want = O.gemv(O.Q4_K, w, x, 896, 4864)
+    assert maxabs_rel(got, want) <= TOL
+    assert maxabs_rel(got, want) <= 1e-5
+
+
+@pytest.mark.parametrize("kind,cols", [(O.Q8_0, 896), (O.Q5_0, 896), (O.Q4_K, 1536), (O.Q6_K, 1536), (O.F32, 512)])
+def test_dequant_row_bit_exact(rng, kind, cols):
+    if kind == O.F32:
+        row = rng.normal(0, 1, cols).astype(np.float32).view(np.uint8)
+    else:
+        row = synth.gen_blocks(rng, kind, 1, cols)
+    got = K.dequant_row(kind, row, cols)
+    want = O.dequant_row(kind, row, cols)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_reference_c_oracle_fixtures_on_gpu():
+    """The reference's inline-C dequant fixtures (tests/golden) through the GPU."""
+    import json, os
+    g = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "ref_c_oracles.json")))
+    for key, kind, n in (("q4_k", O.Q4_K, 256), ("q6_k", O.Q6_K, 256), ("q5_0", O.Q5_0, 32)):
+        for case in g[key]:
+            got = K.dequant_row(kind, bytes.fromhex(case["block"]), n)
+            want = np.array(case["dequant_bits"], np.uint32).view(np.float32)
+            assert np.array_equal(got, want), (key, case["name"])
+
+
+def test_rmsnorm_and_swiglu(rng):
+    for n in (4, 896, 3584):
+        x = rng.normal(0, 3, n).astype(np.float32)
+        w = (1 + rng.normal(0, 0.05, n)).astype(np.float32)
+        assert maxabs_rel(K.rmsnorm(x, w, 1e-6), O.rmsnorm(x, w, 1e-6)) <= 1e-6
+    out = K.rmsnorm([1, 2, 3, 4], [1, 1, 1, 1], 1e-6)  # tensor/ops_test.go:30-43
+    assert abs(out[0] - 1 / np.sqrt(7.5)) <= 1e-5
+    n = 6144
+    g = np.array([(i - 3072) / 256.0 for i in range(n)], np.float32)
+    u = np.array([(i % 100) / 100.0 for i in range(n)], np.float32)
+    got, want = K.swiglu(g, u), O.swiglu(g, u)
+    assert np.abs(got - want).max() <= 1e-6 * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("kind,cols", [(O.Q8_0, 896), (O.Q5_0, 896), (O.Q4_K, 1536), (O.Q6_K, 3584)])
+def test_restricted_f32x_dots(rng, kind, cols):
+    rows = 64
+    w = synth.gen_blocks(rng, kind, rows, cols)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    idx = np.array([0, 5, 63, 17, 17], np.int32)
+    got = K.dot_rows_f32x(kind, w, x, idx, rows, cols)
+    ref = O.gemv_f32x(kind, w, x, rows, cols)[idx]
+    assert maxabs_rel(got, ref) <= 1e-5
+
+
+def test_argument_errors_are_reported():
+    with pytest.raises(K.C2SError):
+        K.gemv(O.Q4_K, b"\0" * 144, np.zeros(300, np.float32), 1, 300)  # cols % 256
+    with pytest.raises(K.C2SError):
+        K.quantize_row_q8_k(np.zeros(100, np.float32))
