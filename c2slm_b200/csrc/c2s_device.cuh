@@ -122,14 +122,19 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Barrier over the kThreads compute threads of a CTA (named barrier 1).  In
+// the persistent kernel a producer warp runs beside them and must not be
+// waited for; in the per-phase kernels these are all the threads.
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory"); }
+
 // Block-wide sum with a fixed reduction tree (deterministic).  `scratch`
-// holds kWarps floats.  All threads get the result.
+// holds kWarps floats.  All compute threads get the result.
 __device__ __forceinline__ float block_sum(float v, float *scratch) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
+  csync();
   if (l == 0) scratch[w] = v;
-  __syncthreads();
+  csync();
   float r = 0.f;
 #pragma unroll
   for (int i = 0; i < kWarps; ++i) r += scratch[i];
@@ -342,7 +347,7 @@ __device__ __forceinline__ float unit_q8_0(const uint8_t *blk, const float *xt, 
 // t, t+blockDim, ... of out.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void dequant_row_cta(int type, const uint8_t *row, float *out, int cols) {
-  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+  for (int i = threadIdx.x; i < cols; i += kThreads) {
     float v = 0.f;
     if (type == T_Q8_0) {
       const uint8_t *b = row + (i >> 5) * 34;

@@ -22,7 +22,7 @@
 #include <vector>
 
 #include "../../include/c2slm_b200.h"
-#include "c2s_kernels.cuh"
+#include "c2s_persistent.cuh"
 
 using namespace c2s;
 
@@ -101,23 +101,30 @@ cudaError_t launch(void (*kernel)(P), dim3 grid, dim3 block, size_t smem, cudaSt
 
 // shared-memory layout of one k_matvec launch
 void layout_matvec(MatParams &P, int grid) {
+  auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
+  int yr = 1;
+  for (int s = 0; s < P.nseg; ++s) yr = std::max(yr, (P.seg[s].rows + grid - 1) / grid + 1);
+  P.ybuf_rows = yr;
   size_t off = static_cast<size_t>(kStages) * kStageAlloc;
   P.off_bars = static_cast<int>(off);
   off += 64;
   const bool normed = P.kind == K_QKV || P.kind == K_FFN_UP || P.kind == K_NORM ||
                       (P.kind == K_LOGITS && P.x_in == nullptr);
+  P.off_nw = static_cast<int>(off);
+  if (normed) off += a16(static_cast<size_t>(P.cols) * 4);
+  bool bias = false;
+  for (int s = 0; s < P.nseg; ++s) bias = bias || P.seg[s].bias != nullptr;
+  P.off_bias = static_cast<int>(off);
+  if (bias) off += a16(static_cast<size_t>(P.nseg) * yr * 4);
   P.off_xn = static_cast<int>(off);
-  if (normed) off += (static_cast<size_t>(P.cols) * 4 + 15) & ~size_t(15);
+  off += a16(static_cast<size_t>(P.cols) * 4);
   P.off_xt = static_cast<int>(off);
-  if (P.need_f32) off += (static_cast<size_t>(P.cols) * 4 + 15) & ~size_t(15);
+  if (P.need_f32) off += a16(static_cast<size_t>(P.cols) * 4);
   P.off_q8 = static_cast<int>(off);
   if (P.need_q8k) {
     const int nsb = P.cols / 256;
-    off += (static_cast<size_t>(q8_qs_bytes(P.cols)) + 4 * nsb + 64 * nsb + 15) & ~size_t(15);
+    off += a16(static_cast<size_t>(q8_qs_bytes(P.cols)) + 4 * nsb + 64 * nsb);
   }
-  int yr = 1;
-  for (int s = 0; s < P.nseg; ++s) yr = std::max(yr, (P.seg[s].rows + grid - 1) / grid + 1);
-  P.ybuf_rows = yr;
   P.off_y = static_cast<int>(off);
   off += static_cast<size_t>(std::max(P.nseg, 1)) * yr * 4;
   P.smem_bytes = static_cast<int>(off);
@@ -367,6 +374,13 @@ struct c2s_engine {
   cudaGraphExec_t g_forward = nullptr, g_step = nullptr, g_logits = nullptr, g_fwd_select = nullptr;
   std::vector<MatParams> mp_cache;
   uint64_t algorithmic_bytes = 0;
+  // persistent decode kernel
+  PPhase *d_phases = nullptr;
+  int nphase = 0;
+  unsigned *gbar = nullptr;
+  PParams pp{};
+  size_t p_smem = 0;
+  bool use_persistent = true;
 };
 
 namespace {
@@ -602,6 +616,184 @@ int set_fwd_input(c2s_engine *e, int token, int pos, int commit) {
   return C2S_OK;
 }
 
+// ---------------------------------------------------------------------------
+// persistent decode kernel: phase table, shared-memory layout, launch
+// ---------------------------------------------------------------------------
+int persistent_setup(c2s_engine *e) {
+  const c2s_model_desc &d = e->d;
+  const int L = d.n_layers, H = d.embd, F = d.ffn, hd = d.head_dim, kvd = d.n_kv_heads * hd;
+  const int G = e->num_sms;
+  std::vector<PPhase> ph;
+  auto mk = [&](int kind, int layer) {
+    PPhase p{};
+    p.kind = kind;
+    p.layer = layer;
+    return p;
+  };
+  auto needs = [](PPhase &p) {
+    p.need_f32 = 0;
+    p.need_q8k = 0;
+    for (int s = 0; s < p.nseg; ++s) {
+      if (is_f32x(p.seg[s].type)) p.need_f32 = 1;
+      if (is_kquant(p.seg[s].type)) p.need_q8k = 1;
+    }
+  };
+  {
+    PPhase p = mk(K_LOGITS, -1);
+    p.nseg = 1;
+    p.cols = H;
+    p.seg[0] = make_seg(e->output, e->out_type, d.vocab, H, nullptr, e->logits);
+    p.norm_w = e->out_norm;
+    needs(p);
+    ph.push_back(p);
+  }
+  for (int l = 0; l < L; ++l) {
+    const LayerDev &Ld = e->layers[l];
+    PPhase q = mk(K_QKV, l);
+    q.nseg = 3;
+    q.cols = H;
+    q.seg[0] = make_seg(Ld.q, Ld.tq, H, H, Ld.qb, e->q);
+    q.seg[1] = make_seg(Ld.k, Ld.tk, kvd, H, Ld.kb, e->k);
+    q.seg[2] = make_seg(Ld.v, Ld.tv, kvd, H, Ld.vb, e->v);
+    q.norm_w = Ld.attn_norm;
+    q.do_embed = (l == 0);
+    needs(q);
+    ph.push_back(q);
+    PPhase a = mk(K_ATTN, l);
+    a.q_norm = Ld.qn;
+    a.k_norm = Ld.kn;
+    ph.push_back(a);
+    PPhase o = mk(K_OPROJ, l);
+    o.nseg = 1;
+    o.cols = H;
+    o.seg[0] = make_seg(Ld.o, Ld.to, H, H, nullptr, e->X);
+    o.x_in = e->attn_out;
+    needs(o);
+    ph.push_back(o);
+    PPhase u = mk(K_FFN_UP, l);
+    u.nseg = 2;
+    u.cols = H;
+    u.seg[0] = make_seg(Ld.gate, Ld.tgate, F, H, nullptr, nullptr);
+    u.seg[1] = make_seg(Ld.up, Ld.tup, F, H, nullptr, nullptr);
+    u.norm_w = Ld.ffn_norm;
+    needs(u);
+    ph.push_back(u);
+    PPhase w = mk(K_FFN_DOWN, l);
+    w.nseg = 1;
+    w.cols = F;
+    w.seg[0] = make_seg(Ld.down, Ld.tdown, H, F, nullptr, e->X);
+    w.x_in = e->h;
+    w.commit_here = (l == L - 1);
+    needs(w);
+    ph.push_back(w);
+  }
+  // shared memory: weight ring | mbarriers | activation region (union of the
+  // matvec and attention working sets)
+  auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
+  int xn_cap = H, xt_cap = 0, q8_cap = 0, yrows = 1;
+  for (auto &p : ph) {
+    if (p.kind == K_ATTN) continue;
+    for (int s = 0; s < p.nseg; ++s) {
+      const int per = (p.seg[s].rows + G - 1) / G + 1;
+      yrows = std::max(yrows, per);
+      if (p.kind != K_LOGITS && per > kThreads)
+        return fail(C2S_ERR_UNSUPPORTED, "persistent decode: more than %d rows per CTA", kThreads);
+    }
+    if (p.need_f32) {
+      xt_cap = std::max(xt_cap, p.cols);
+      xn_cap = std::max(xn_cap, p.cols);
+    }
+    if (p.need_q8k) q8_cap = std::max(q8_cap, p.cols);
+  }
+  PParams &P = e->pp;
+  P.off_xn = 0;
+  P.off_xt = static_cast<int>(a16(static_cast<size_t>(xn_cap) * 4));
+  P.off_q8 = P.off_xt + static_cast<int>(a16(static_cast<size_t>(xt_cap) * 4));
+  const size_t q8b = q8_cap ? a16(static_cast<size_t>(q8_qs_bytes(q8_cap)) + 4 * (q8_cap / 256) + 64 * (q8_cap / 256)) : 0;
+  P.off_y = P.off_q8 + static_cast<int>(q8b);
+  P.yrows = yrows;
+  const size_t mv_act = static_cast<size_t>(P.off_y) + static_cast<size_t>(kMaxSegs) * yrows * 4;
+  const int qpk = d.n_heads / d.n_kv_heads, SUB = attn_sub(hd);
+  const size_t at_act = (static_cast<size_t>(4) * SUB * hd + 2 * static_cast<size_t>(qpk) * hd + 2 * hd +
+                         static_cast<size_t>(qpk) * SUB) * 4;
+  const size_t act = a16(std::max(mv_act, at_act));
+  const size_t budget = 227 * 1024 - 2048;  // dynamic smem; static smem of the kernel is < 2 KB
+  int nslot = static_cast<int>((budget - act - 64 * 8) / kStageAlloc);
+  nslot = std::min(nslot, 12);
+  if (nslot < 2) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: activation set too large for shared memory");
+  P.nslot = nslot;
+  size_t off = static_cast<size_t>(nslot) * kStageAlloc;
+  P.off_full = static_cast<int>(off);
+  off += 8 * nslot;
+  P.off_empty = static_cast<int>(off);
+  off += 8 * nslot;
+  P.off_abar = static_cast<int>(off);
+  off += 16;
+  off = (off + 127) & ~size_t(127);
+  P.off_act = static_cast<int>(off);
+  e->p_smem = off + act;
+  // parameters
+  e->nphase = static_cast<int>(ph.size());
+  CK(cudaMalloc(&e->d_phases, sizeof(PPhase) * ph.size()));
+  CK(cudaMemcpy(e->d_phases, ph.data(), sizeof(PPhase) * ph.size(), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&e->gbar, 64));
+  CK(cudaMemset(e->gbar, 0, 64));
+  P.phases = e->d_phases;
+  P.nphase = e->nphase;
+  P.H = H;
+  P.n_heads = d.n_heads;
+  P.n_kv = d.n_kv_heads;
+  P.hd = hd;
+  P.max_tokens = d.max_tokens;
+  P.max_splits = e->max_splits;
+  P.rope_len = kMaxContext;
+  P.eps = d.eps;
+  P.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
+  P.X = e->X;
+  P.normx = e->normx;
+  P.q = e->q;
+  P.k = e->k;
+  P.v = e->v;
+  P.attn_out = e->attn_out;
+  P.h = e->h;
+  P.logits = e->logits;
+  P.part = e->part;
+  P.amax_part = e->amax_part;
+  const size_t plane = static_cast<size_t>(L) * d.n_kv_heads * d.max_tokens * hd;
+  P.kcache = e->kv;
+  P.vcache = e->kv + plane;
+  P.rope_cos = e->rope_cos;
+  P.rope_sin = e->rope_sin;
+  P.embd_w = e->tok_embd;
+  P.embd_type = e->tok_type;
+  P.embd_row_bytes = static_cast<int>(row_bytes_of(e->tok_type, H));
+  P.st = e->st;
+  P.token_ids = e->token_ids;
+  P.out_tokens = e->out_tokens;
+  P.gbar = e->gbar;
+  CK(cudaFuncSetAttribute(k_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(e->p_smem)));
+  int blocks = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_persistent, kPThreads, e->p_smem));
+  const char *mode = getenv("C2S_DECODE");
+  e->use_persistent = blocks >= 1 && !(mode && strcmp(mode, "graph") == 0);
+  return C2S_OK;
+}
+
+// n_steps decode steps (logits+select+forward) in one cooperative launch
+int launch_persistent(c2s_engine *e, int n_steps, int rewind_period, int rewind_base,
+                      unsigned long long *trace = nullptr) {
+  PParams P = e->pp;
+  P.trace = trace;
+  P.n_steps = n_steps;
+  P.rewind_period = rewind_period;
+  P.rewind_base = rewind_base;
+  CK(cudaMemsetAsync(e->gbar, 0, sizeof(unsigned), e->stream));
+  void *args[] = {&P};
+  CK(cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(k_persistent), dim3(e->num_sms), dim3(kPThreads),
+                                 args, e->p_smem, e->stream));
+  return C2S_OK;
+}
+
 int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_desc *ts, int n) {
   c2s_model_desc d = *desc;
   if (d.embd <= 0 || d.n_layers <= 0 || d.n_heads <= 0 || d.n_kv_heads <= 0 || d.ffn <= 0)
@@ -743,7 +935,13 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   // grows, ceil(n / max_splits) once it saturates
   e->chunk_cap = std::max(kMinSplitLen, (d.max_tokens + e->max_splits - 1) / e->max_splits);
   const int qpk = d.n_heads / d.n_kv_heads;
-  e->attn_smem = (static_cast<size_t>(qpk) * hd + 2 * hd + static_cast<size_t>(qpk) * e->chunk_cap) * 4;
+  if (qpk > 8) return fail(C2S_ERR_UNSUPPORTED, "more than 8 query heads per kv head");
+  if (hd != 64 && hd != 128) return fail(C2S_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  {
+    const int SUB = attn_sub(hd);
+    e->attn_smem = (static_cast<size_t>(4) * SUB * hd + 2 * static_cast<size_t>(qpk) * hd + 2 * hd +
+                    static_cast<size_t>(qpk) * SUB) * 4;
+  }
   if (e->attn_smem > 200 * 1024) return fail(C2S_ERR_UNSUPPORTED, "attention smem %zu too large", e->attn_smem);
   auto dalloc = [&](void **p, size_t bytes) -> int {
     if (cudaMalloc(p, bytes) != cudaSuccess) return fail(C2S_ERR_OOM, "cudaMalloc(%zu) failed", bytes);
@@ -799,6 +997,7 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
       return rc;
   }
   e->kernels_per_step = 5 * d.n_layers + 1;
+  if ((rc = persistent_setup(e))) return rc;
   CK(cudaStreamSynchronize(e->stream));
   return C2S_OK;
 }
@@ -815,7 +1014,8 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->attn_out), static_cast<void *>(e->h), static_cast<void *>(e->logits),
                   static_cast<void *>(e->part), static_cast<void *>(e->amax_part), static_cast<void *>(e->token_ids),
                   static_cast<void *>(e->out_tokens), static_cast<void *>(e->rows_idx),
-                  static_cast<void *>(e->scratch_x), static_cast<void *>(e->st)})
+                  static_cast<void *>(e->scratch_x), static_cast<void *>(e->st),
+                  static_cast<void *>(e->d_phases), static_cast<void *>(e->gbar)})
     if (p) cudaFree(p);
   for (void *p : {static_cast<void *>(e->h_in), static_cast<void *>(e->h_buf), static_cast<void *>(e->h_st),
                   static_cast<void *>(e->h_tokens)})
@@ -1140,7 +1340,11 @@ int c2s_generate(c2s_engine *e, int max_new, float penalty, int window, int stop
   if (max_new <= 0) return C2S_OK;
   if (e->host_seq <= 0) return fail(C2S_ERR_STATE, "generate needs a forwarded prefix (SeqLen == 0)");
   if (int rc = set_gen_state(e, penalty, window, stop_on_special)) return rc;
-  for (int i = 0; i < max_new; ++i) CK(cudaGraphLaunch(e->g_step, e->stream));
+  if (e->use_persistent) {
+    if (int rc = launch_persistent(e, max_new, 0, 0)) return rc;
+  } else {
+    for (int i = 0; i < max_new; ++i) CK(cudaGraphLaunch(e->g_step, e->stream));
+  }
   CK(cudaMemcpyAsync(e->h_tokens, e->out_tokens, static_cast<size_t>(max_new) * 4, cudaMemcpyDeviceToHost,
                      e->stream));
   if (int rc = read_status(e)) return rc;
@@ -1175,7 +1379,11 @@ int c2s_bench_decode(c2s_engine *e, int n_steps, float penalty, int window) {
   if (n_steps > e->d.max_tokens - e->host_seq) return fail(C2S_ERR_ARG, "n_steps exceeds KV capacity");
   DeviceGuard g(e->device);
   if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
-  for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(e->g_step, e->stream));
+  if (e->use_persistent) {
+    if (int rc = launch_persistent(e, n_steps, 0, 0)) return rc;
+  } else {
+    for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(e->g_step, e->stream));
+  }
   e->host_seq += n_steps;  // confirmed by the next read_status
   return C2S_OK;
 }
@@ -1195,10 +1403,14 @@ int c2s_bench_decode_timed(c2s_engine *e, int n_steps, float penalty, int window
   CK(cudaEventCreate(&a));
   CK(cudaEventCreate(&b));
   CK(cudaEventRecord(a, e->stream));
-  for (int i = 0; i < n_steps; ++i) {
-    if (period > 0 && i > 0 && i % period == 0)
-      CK(cudaMemcpyAsync(&e->st->seq_len, &e->h_st->fwd_token, sizeof(int), cudaMemcpyHostToDevice, e->stream));
-    CK(cudaGraphLaunch(e->g_step, e->stream));
+  if (e->use_persistent) {
+    if (int rc = launch_persistent(e, n_steps, period, e->host_seq)) return rc;
+  } else {
+    for (int i = 0; i < n_steps; ++i) {
+      if (period > 0 && i > 0 && i % period == 0)
+        CK(cudaMemcpyAsync(&e->st->seq_len, &e->h_st->fwd_token, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+      CK(cudaGraphLaunch(e->g_step, e->stream));
+    }
   }
   CK(cudaEventRecord(b, e->stream));
   CK(cudaEventSynchronize(b));
@@ -1206,6 +1418,26 @@ int c2s_bench_decode_timed(c2s_engine *e, int n_steps, float penalty, int window
   cudaEventDestroy(a);
   cudaEventDestroy(b);
   return read_status(e);
+}
+
+int c2s_trace_decode(c2s_engine *e, int n_steps, float penalty, int window, uint64_t *trace_out, int *nphase_out) {
+  if (!e || !trace_out || !nphase_out) return fail(C2S_ERR_ARG, "null argument");
+  if (!e->use_persistent) return fail(C2S_ERR_STATE, "persistent decode kernel not in use");
+  if (n_steps <= 0 || n_steps > e->d.max_tokens - e->host_seq) return fail(C2S_ERR_ARG, "n_steps out of range");
+  DeviceGuard g(e->device);
+  if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
+  const size_t n = static_cast<size_t>(n_steps) * e->nphase * 4 * 2;
+  unsigned long long *dtr = nullptr;
+  CK(cudaMalloc(&dtr, n * 8));
+  CK(cudaMemsetAsync(dtr, 0, n * 8, e->stream));
+  int rc = launch_persistent(e, n_steps, 0, 0, dtr);
+  if (rc == C2S_OK) {
+    cudaMemcpyAsync(trace_out, dtr, n * 8, cudaMemcpyDeviceToHost, e->stream);
+    rc = read_status(e);
+  }
+  cudaFree(dtr);
+  *nphase_out = e->nphase;
+  return rc;
 }
 
 int c2s_profile_step(c2s_engine *e, int n_steps, float penalty, int window, float *stage_ms, int *stage_launches) {

@@ -57,7 +57,7 @@ struct MatParams {
   int need_f32, need_q8k;
   int32_t *dbg;        // optional int32 partials (K-quants)
   int ybuf_rows;
-  int off_bars, off_xn, off_xt, off_q8, off_y, smem_bytes;
+  int off_bars, off_nw, off_bias, off_xn, off_xt, off_q8, off_y, smem_bytes;
   int check_halt;      // engine kernels honour DevState::halted
 };
 
@@ -99,110 +99,223 @@ __device__ __forceinline__ void issue_chunk(const MatParams &P, const ChunkRef &
   bulk_g2s(stage, reinterpret_cast<const void *>(a0), bytes, bar);
 }
 
-// Dot products of the rows in one staged chunk; results to y[0..nr).
-// Warp/row mapping: wpr warps per row, lanes over units; partials reduced in
-// a fixed order (deterministic).
-__device__ __forceinline__ void compute_chunk(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
-                                              int grow0, const float *xt, int nbx, const Q8KView &q8,
-                                              float *y, float (*red)[kWarps]) {
+// ---------------------------------------------------------------------------
+// Row dot products over one staged chunk.
+// ---------------------------------------------------------------------------
+// float(b) for a byte b of `w` via the exponent trick: 0x4B0000bb = 2^23 + b.
+__device__ __forceinline__ float byte_as_f(uint32_t w, int e) {
+  return __int_as_float(static_cast<int>(__byte_perm(w, 0x4B000000u, 0x7440u | static_cast<uint32_t>(e))));
+}
+
+// Q8_0 block . f32 x held in registers (lane owns the block).
+__device__ __forceinline__ float blockdot_q8_0_reg(const uint8_t *blk, const float (&xr)[32]) {
+  const float d = h2f(ld16(blk));
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const uint32_t w = ld32u(blk + 2 + 4 * t) ^ 0x80808080u;  // int8 -> uint8 + 128
+    a0 = fmaf(byte_as_f(w, 0) - 8388736.0f, xr[4 * t + 0], a0);  // 2^23 + 128
+    a1 = fmaf(byte_as_f(w, 1) - 8388736.0f, xr[4 * t + 1], a1);
+    a2 = fmaf(byte_as_f(w, 2) - 8388736.0f, xr[4 * t + 2], a2);
+    a3 = fmaf(byte_as_f(w, 3) - 8388736.0f, xr[4 * t + 3], a3);
+  }
+  return d * ((a0 + a1) + (a2 + a3));
+}
+
+// Q5_0 block . f32 x held in registers: q = (nibble | hbit<<4) - 16.
+__device__ __forceinline__ float blockdot_q5_0_reg(const uint8_t *blk, const float (&xr)[32]) {
+  const float d = h2f(ld16(blk));
+  const uint32_t qh = static_cast<uint32_t>(ld16(blk + 2)) | (static_cast<uint32_t>(ld16(blk + 4)) << 16);
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint32_t w = ld32u(blk + 6 + 4 * t);
+    const uint32_t lo = (w & 0x0F0F0F0Fu) | (spread4((qh >> (4 * t)) & 0xFu) << 4);
+    const uint32_t hi = ((w >> 4) & 0x0F0F0F0Fu) | (spread4((qh >> (16 + 4 * t)) & 0xFu) << 4);
+    a0 = fmaf(byte_as_f(lo, 0) - 8388624.0f, xr[4 * t + 0], a0);  // 2^23 + 16
+    a1 = fmaf(byte_as_f(lo, 1) - 8388624.0f, xr[4 * t + 1], a1);
+    a2 = fmaf(byte_as_f(lo, 2) - 8388624.0f, xr[4 * t + 2], a2);
+    a3 = fmaf(byte_as_f(lo, 3) - 8388624.0f, xr[4 * t + 3], a3);
+    a0 = fmaf(byte_as_f(hi, 0) - 8388624.0f, xr[16 + 4 * t + 0], a0);
+    a1 = fmaf(byte_as_f(hi, 1) - 8388624.0f, xr[16 + 4 * t + 1], a1);
+    a2 = fmaf(byte_as_f(hi, 2) - 8388624.0f, xr[16 + 4 * t + 2], a2);
+    a3 = fmaf(byte_as_f(hi, 3) - 8388624.0f, xr[16 + 4 * t + 3], a3);
+  }
+  return d * ((a0 + a1) + (a2 + a3));
+}
+
+// One warp's partial over units u = u0 + lane + k*ustep of one row (K-quants
+// and the generic f32 path).  All lanes must call it (Q6_K shuffles).
+template <int TYPE>
+__device__ __forceinline__ float row_units(const MatParams &P, const uint8_t *row, int grow, bool rowok, int u0,
+                                           int ustep, int U, const float *xt, int nbx, const Q8KView &q8) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (int ub = u0; ub < U; ub += ustep) {
+    const int u = ub + lane;
+    const bool ok = rowok && u < U;
+    if (TYPE == T_Q4_K) {
+      if (ok) {
+        int lo, hi;
+        const int sbi = u >> 2, j = u & 3;
+        acc += unit_q4k(row + sbi * 144, sbi, j, q8, lo, hi);
+        if (P.dbg) {
+          int32_t *dst = P.dbg + (static_cast<size_t>(grow) * (U >> 2) + sbi) * 8 + 2 * j;
+          dst[0] = lo;
+          dst[1] = hi;
+        }
+      }
+    } else if (TYPE == T_Q6_K) {
+      int is = 0;
+      const int sbi = u >> 2;
+      if (ok) is = unit_q6k_isum(row + sbi * 210, sbi, (u >> 1) & 1, u & 1, q8);
+      is += __shfl_xor_sync(0xffffffffu, is, 1);
+      is += __shfl_xor_sync(0xffffffffu, is, 2);
+      if (ok && (u & 3) == 0) {
+        const float d6 = h2f(ld16(row + sbi * 210 + 208));
+        acc += __fmul_rn(static_cast<float>(is), __fmul_rn(d6, q8.d[sbi]));
+        if (P.dbg) P.dbg[static_cast<size_t>(grow) * (U >> 2) + sbi] = is;
+      }
+    } else if (TYPE == T_Q5_0) {
+      if (ok) acc += unit_q5_0(row + u * 22, xt + u, nbx);
+    } else if (TYPE == T_Q8_0) {
+      if (ok) acc += unit_q8_0(row + u * 34, xt + u, nbx);
+    }
+  }
+  return acc;
+}
+
+// Rows of one staged chunk -> y[0..nr).  Few wide rows: several warps per
+// row, partials combined in a fixed order.  Otherwise one warp per row with
+// no block-level barrier.  f32-activation types with <= 32 blocks per row use
+// the x values each lane holds in registers (xr, block = lane).
+template <int TYPE>
+__device__ __forceinline__ void compute_chunk_t(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
+                                                int grow0, const float *xt, int nbx, const Q8KView &q8, float *y,
+                                                float (*red)[kWarps], const float (&xr)[32], bool xreg) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int U = S.units;
-  int wpr = 1;  // warps per row: spread few wide rows over several warps
+  if ((TYPE == T_Q5_0 || TYPE == T_Q8_0) && xreg) {
+    for (int r = warp; r < nr; r += kWarps) {
+      const uint8_t *row = rows_smem + static_cast<size_t>(r) * S.row_bytes;
+      float acc = 0.f;
+      if (lane < U) {
+        if (TYPE == T_Q8_0) acc = blockdot_q8_0_reg(row + lane * 34, xr);
+        else acc = blockdot_q5_0_reg(row + lane * 22, xr);
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) y[r] = acc;
+    }
+    return;
+  }
+  int wpr = 1;
   if (nr < kWarps) {
     const int want = kWarps / nr;
     const int cap = (U + 31) / 32;
     while (wpr * 2 <= want && wpr * 2 <= cap) wpr *= 2;
   }
+  if (wpr == 1) {
+    for (int r = warp; r < nr; r += kWarps) {
+      const uint8_t *row = rows_smem + static_cast<size_t>(r) * S.row_bytes;
+      float acc = row_units<TYPE>(P, row, grow0 + r, true, 0, 32, U, xt, nbx, q8);
+      acc = warp_sum(acc);
+      if (lane == 0) y[r] = acc;
+    }
+    return;
+  }
   const int rows_per_pass = kWarps / wpr;
   const int sub = warp % wpr;
-  const int iters = (U + wpr * 32 - 1) / (wpr * 32);
   for (int rb = 0; rb < nr; rb += rows_per_pass) {
     const int r = rb + warp / wpr;
     const bool rowok = r < nr;
     const uint8_t *row = rows_smem + static_cast<size_t>(rowok ? r : 0) * S.row_bytes;
-    float acc = 0.f;
-    for (int it = 0; it < iters; ++it) {
-      const int u = it * wpr * 32 + sub * 32 + lane;
-      const bool ok = rowok && u < U;
-      if (S.type == T_Q4_K) {
-        if (ok) {
-          int lo, hi;
-          const int sbi = u >> 2, j = u & 3;
-          acc += unit_q4k(row + sbi * 144, sbi, j, q8, lo, hi);
-          if (P.dbg) {
-            const int nsb = U >> 2;
-            int32_t *dst = P.dbg + (static_cast<size_t>(grow0 + r) * nsb + sbi) * 8 + 2 * j;
-            dst[0] = lo;
-            dst[1] = hi;
-          }
-        }
-      } else if (S.type == T_Q6_K) {
-        int is = 0;
-        const int sbi = u >> 2;
-        if (ok) is = unit_q6k_isum(row + sbi * 210, sbi, (u >> 1) & 1, u & 1, q8);
-        is += __shfl_xor_sync(0xffffffffu, is, 1);
-        is += __shfl_xor_sync(0xffffffffu, is, 2);
-        if (ok && (u & 3) == 0) {
-          const float d6 = h2f(ld16(row + sbi * 210 + 208));
-          acc += __fmul_rn(static_cast<float>(is), __fmul_rn(d6, q8.d[sbi]));
-          if (P.dbg) P.dbg[static_cast<size_t>(grow0 + r) * (U >> 2) + sbi] = is;
-        }
-      } else if (S.type == T_Q5_0) {
-        if (ok) acc += unit_q5_0(row + u * 22, xt + u, nbx);
-      } else if (S.type == T_Q8_0) {
-        if (ok) acc += unit_q8_0(row + u * 34, xt + u, nbx);
-      }
-    }
+    float acc = row_units<TYPE>(P, row, grow0 + r, rowok, sub * 32, wpr * 32, U, xt, nbx, q8);
     acc = warp_sum(acc);
     if (lane == 0 && rowok) red[r - rb][sub] = acc;
-    __syncthreads();
+    csync();
     if (threadIdx.x < rows_per_pass && rb + static_cast<int>(threadIdx.x) < nr) {
       const int rr = rb + threadIdx.x;
-      float s = 0.f;
-      for (int k = 0; k < wpr; ++k) s += red[rr - rb][k];
-      y[rr] = s;
+      float sum = 0.f;
+      for (int k = 0; k < wpr; ++k) sum += red[rr - rb][k];
+      y[rr] = sum;
     }
-    __syncthreads();
+    csync();
   }
 }
 
-// RMSNorm of a shared-memory vector in place (tensor/ops.go:207-218):
-// inv = float32(1/sqrt(float64(sumsq/n + eps))); out = (x*inv)*w.
-__device__ __forceinline__ void rmsnorm_smem(float *x, const float *w, int n, float eps, float *scratch) {
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
-  ss = block_sum(ss, scratch);
-  const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps);
-  const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(mean)));
-  for (int i = threadIdx.x; i < n; i += blockDim.x) x[i] = __fmul_rn(__fmul_rn(x[i], inv), __ldg(w + i));
-  __syncthreads();
+__device__ __forceinline__ void compute_chunk(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
+                                              int grow0, const float *xt, int nbx, const Q8KView &q8, float *y,
+                                              float (*red)[kWarps], const float (&xr)[32], bool xreg) {
+  switch (S.type) {
+    case T_Q4_K: compute_chunk_t<T_Q4_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
+    case T_Q6_K: compute_chunk_t<T_Q6_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
+    case T_Q5_0: compute_chunk_t<T_Q5_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
+    case T_Q8_0: compute_chunk_t<T_Q8_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
+    default: break;
+  }
 }
 
-// Builds the Q8_K activation in shared memory from a vector `src` (global or
-// shared), one warp per superblock.
-template <bool kGlobal>
+// Loads n floats (n % 4 == 0, 16-B aligned) from global into shared memory,
+// every thread's loads in flight before its first store.
+__device__ __forceinline__ void load_vec_to_smem(float *dst, const float *src, int n) {
+  const int n4 = n >> 2;
+  const float4 *s4 = reinterpret_cast<const float4 *>(src);
+  float4 *d4 = reinterpret_cast<float4 *>(dst);
+  int i = threadIdx.x;
+  for (; i + 3 * kThreads < n4; i += 4 * kThreads) {
+    const float4 a = __ldcg(s4 + i), b = __ldcg(s4 + i + kThreads), c = __ldcg(s4 + i + 2 * kThreads),
+                 d = __ldcg(s4 + i + 3 * kThreads);
+    d4[i] = a;
+    d4[i + kThreads] = b;
+    d4[i + 2 * kThreads] = c;
+    d4[i + 3 * kThreads] = d;
+  }
+  for (; i < n4; i += kThreads) d4[i] = __ldcg(s4 + i);
+}
+
+// Same for read-only constants (norm weights): the read-only data path.
+__device__ __forceinline__ void load_const_to_smem(float *dst, const float *src, int n) {
+  const int n4 = n >> 2;
+  const float4 *s4 = reinterpret_cast<const float4 *>(src);
+  float4 *d4 = reinterpret_cast<float4 *>(dst);
+  for (int i = threadIdx.x; i < n4; i += kThreads) d4[i] = __ldg(s4 + i);
+}
+
+// RMSNorm of a shared-memory vector in place (tensor/ops.go:207-218):
+// inv = float32(1/sqrt(float64(sumsq/n + eps))); out = (x*inv)*w, w in smem.
+__device__ __forceinline__ void rmsnorm_smem(float *x, const float *w, int n, float eps, float *scratch) {
+  float ss0 = 0.f, ss1 = 0.f;
+  int i = threadIdx.x;
+  for (; i + kThreads < n; i += 2 * kThreads) {
+    ss0 = fmaf(x[i], x[i], ss0);
+    ss1 = fmaf(x[i + kThreads], x[i + kThreads], ss1);
+  }
+  if (i < n) ss0 = fmaf(x[i], x[i], ss0);
+  const float ss = block_sum(ss0 + ss1, scratch);
+  const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps);
+  const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(mean)));
+  for (int k = threadIdx.x; k < n; k += kThreads) x[k] = __fmul_rn(__fmul_rn(x[k], inv), w[k]);
+  csync();
+}
+
+// Builds the Q8_K activation in shared memory from a shared-memory vector,
+// one warp per superblock.
 __device__ __forceinline__ void build_q8k(const float *src, int cols, int8_t *qs, float *d, int32_t *bsum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsb = cols / 256;
   for (int sb = warp; sb < nsb; sb += kWarps) {
     float x[8];
-    const float *p = src + sb * 256 + lane * 8;
-    if (kGlobal) {
-      const float4 a = __ldcg(reinterpret_cast<const float4 *>(p));
-      const float4 b = __ldcg(reinterpret_cast<const float4 *>(p + 4));
-      x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = p[i];
-    }
+    const float4 a = *reinterpret_cast<const float4 *>(src + sb * 256 + lane * 8);
+    const float4 b = *reinterpret_cast<const float4 *>(src + sb * 256 + lane * 8 + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
     quantize_sb_warp(x, d + sb, bsum + sb * 16, [&](int ln, const int (&q)[8]) {
       const int e0 = sb * 256 + ln * 8;
       int8_t *dst = qs + q8_pad_index(e0);
       uint32_t w0 = 0, w1 = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        w0 |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
-        w1 |= (static_cast<uint32_t>(q[4 + i]) & 0xFFu) << (8 * i);
+      for (int k = 0; k < 4; ++k) {
+        w0 |= (static_cast<uint32_t>(q[k]) & 0xFFu) << (8 * k);
+        w1 |= (static_cast<uint32_t>(q[4 + k]) & 0xFFu) << (8 * k);
       }
       *reinterpret_cast<uint2 *>(dst) = make_uint2(w0, w1);
     });
@@ -232,11 +345,20 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
     fence_mbar_init();
   }
   __syncthreads();
-  // Weights do not depend on earlier kernels: stream them before the wait.
+  // Weights and constants do not depend on earlier kernels: fetch them
+  // before the wait.
   if (tid == 0) {
     for (int i = 0; i < nchunks && i < kStages; ++i)
       issue_chunk(P, chunk_at(P, my0, my1, i), smem + i * kStageAlloc, &bars[i]);
   }
+  float *nw = reinterpret_cast<float *>(smem + P.off_nw);
+  float *ybias = reinterpret_cast<float *>(smem + P.off_bias);
+  const bool normed = P.kind == K_QKV || P.kind == K_FFN_UP || P.kind == K_NORM ||
+                      (P.kind == K_LOGITS && P.x_in == nullptr);
+  if (normed) load_const_to_smem(nw, P.norm_w, P.cols);
+  for (int s = 0; s < P.nseg; ++s)
+    if (P.seg[s].bias)
+      for (int r = my0[s] + tid; r < my1[s]; r += kThreads) ybias[s * P.ybuf_rows + (r - my0[s])] = __ldg(P.seg[s].bias + r);
   pdl_trigger();
   pdl_wait();
 
@@ -244,6 +366,16 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
   unsigned *err = &st->err;
   bool skip = false;
   if (P.check_halt) skip = (*reinterpret_cast<volatile int *>(&st->halted)) != 0;
+  if (skip) {  // halted step: drain the copies already issued, then leave
+    if (tid == 0)
+      for (int i = 0; i < nchunks && i < kStages; ++i) mbar_wait_bounded(&bars[i], 0, err);
+    __syncthreads();
+    return;
+  }
+  // residual rows of this CTA, fetched early (used by the epilogue)
+  float xres = 0.f;
+  const bool residual = P.kind == K_OPROJ || P.kind == K_FFN_DOWN;
+  if (residual && my0[0] + tid < my1[0]) xres = __ldcg(P.X + my0[0] + tid);
 
   float *xn = reinterpret_cast<float *>(smem + P.off_xn);
   float *xt = reinterpret_cast<float *>(smem + P.off_xt);
@@ -256,44 +388,41 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
   q8.bsum = q8bs;
   const int nbx = P.cols / 32;
 
-  if (!skip) {
-    // ---- input vector
-    const bool normed = P.kind == K_QKV || P.kind == K_FFN_UP || P.kind == K_NORM ||
-                        (P.kind == K_LOGITS && P.x_in == nullptr);
-    if (normed) {
-      if (P.kind == K_QKV && P.do_embed) {
-        int tok = st->fwd_token;
-        if (tok < 0 || tok >= st->vocab) tok = 0;  // engine/model.go:222-224
-        dequant_row_cta(P.embd_type, P.embd_w + static_cast<size_t>(tok) * P.embd_row_bytes, xn, P.cols);
-        __syncthreads();
-        if (c == 0)
-          for (int i = tid; i < P.cols; i += kThreads) P.X[i] = xn[i];
-      } else {
-        for (int i = tid; i < P.cols; i += kThreads) xn[i] = __ldcg(P.X + i);
-        __syncthreads();
-      }
-      rmsnorm_smem(xn, P.norm_w, P.cols, P.eps, scratch);
-      if ((P.kind == K_LOGITS || P.kind == K_NORM) && c == 0 && P.normx_out)
-        for (int i = tid; i < P.cols; i += kThreads) P.normx_out[i] = xn[i];
-      if (P.need_f32)
-        for (int i = tid; i < P.cols; i += kThreads) xt[(i & 31) * nbx + (i >> 5)] = xn[i];
-      if (P.need_q8k) build_q8k<false>(xn, P.cols, q8qs, q8d, q8bs);
+  // ---- input vector
+  if (normed) {
+    if (P.kind == K_QKV && P.do_embed) {
+      int tok = st->fwd_token;
+      if (tok < 0 || tok >= st->vocab) tok = 0;  // engine/model.go:222-224
+      dequant_row_cta(P.embd_type, P.embd_w + static_cast<size_t>(tok) * P.embd_row_bytes, xn, P.cols);
+      __syncthreads();
+      if (c == 0)
+        for (int i = tid; i < P.cols; i += kThreads) P.X[i] = xn[i];
     } else {
-      if (P.need_f32)
-        for (int i = tid; i < P.cols; i += kThreads) xt[(i & 31) * nbx + (i >> 5)] = __ldcg(P.x_in + i);
-      if (P.need_q8k) build_q8k<true>(P.x_in, P.cols, q8qs, q8d, q8bs);
+      load_vec_to_smem(xn, P.X, P.cols);
+      __syncthreads();
     }
+    rmsnorm_smem(xn, nw, P.cols, P.eps, scratch);
+    if ((P.kind == K_LOGITS || P.kind == K_NORM) && c == 0 && P.normx_out)
+      for (int i = tid; i < P.cols; i += kThreads) P.normx_out[i] = xn[i];
+  } else {
+    load_vec_to_smem(xn, P.x_in, P.cols);
     __syncthreads();
+  }
+  if (P.need_f32)
+    for (int i = tid; i < P.cols; i += kThreads) xt[(i & 31) * nbx + (i >> 5)] = xn[i];
+  if (P.need_q8k) build_q8k(xn, P.cols, q8qs, q8d, q8bs);
+  __syncthreads();
+  // f32 x of this lane's block in registers (types with <= 32 blocks per row)
+  float xr[32];
+  const bool xreg = P.need_f32 && nbx <= 32;
+  if (xreg) {
+    const int lane = tid & 31;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) xr[k] = lane < nbx ? xt[k * nbx + lane] : 0.f;
   }
 
   // ---- stream the chunks
   float *ybuf = reinterpret_cast<float *>(smem + P.off_y);
-  if (skip) {  // halted step: drain the copies already issued, then leave
-    if (tid == 0)
-      for (int i = 0; i < nchunks && i < kStages; ++i) mbar_wait_bounded(&bars[i], 0, err);
-    __syncthreads();
-    return;
-  }
   bool failed = false;
   int consumed = 0;
   for (int i = 0; i < nchunks; ++i) {
@@ -311,7 +440,7 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
       const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
       const uint8_t *rows = smem + sidx * kStageAlloc + (src & 15);
       compute_chunk(P, S, rows, ch.r1 - ch.r0, ch.r0, xt, nbx, q8,
-                    ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]), red);
+                    ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]), red, xr, xreg);
     }
     __syncthreads();
     if (tid == 0 && i + kStages < nchunks)
@@ -333,11 +462,12 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
     for (int s = 0; s < P.nseg; ++s)
       for (int r = my0[s] + tid; r < my1[s]; r += kThreads) {
         float v = ybuf[s * P.ybuf_rows + (r - my0[s])];
-        if (P.seg[s].bias) v = __fadd_rn(v, __ldg(P.seg[s].bias + r));
+        if (P.seg[s].bias) v = __fadd_rn(v, ybias[s * P.ybuf_rows + (r - my0[s])]);
         P.seg[s].out[r] = v;
       }
-  } else if (P.kind == K_OPROJ || P.kind == K_FFN_DOWN) {
-    for (int r = my0[0] + tid; r < my1[0]; r += kThreads)
+  } else if (residual) {
+    if (my0[0] + tid < my1[0]) P.X[my0[0] + tid] = __fadd_rn(xres, ybuf[tid]);
+    for (int r = my0[0] + tid + kThreads; r < my1[0]; r += kThreads)
       P.X[r] = __fadd_rn(__ldcg(P.X + r), ybuf[r - my0[0]]);
     if (P.kind == K_FFN_DOWN && P.commit_here && c == 0 && tid == 0 && st->commit) {
       const int pos = st->fwd_pos;
@@ -486,17 +616,27 @@ __host__ __device__ inline int attn_nsplit(int n, int max_splits) {
   return ns > max_splits ? max_splits : ns;
 }
 
+// positions per staged sub-chunk: K and V tiles of 16 KB each
+__host__ __device__ inline int attn_sub(int hd) { return 4096 / hd; }
+
 __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
-  extern __shared__ __align__(16) float asmem[];
+  extern __shared__ __align__(128) float asmem[];
+  __shared__ __align__(8) uint64_t bars[2];
   __shared__ int s_last;
-  __shared__ float s_red[kWarps][8];
+  __shared__ float s_m[8], s_l[8], s_scale[8];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_trigger();
   pdl_wait();
   DevState *st = A.st;
   if (A.check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
-  const int g = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  const int hd = A.hd, qpk = A.n_heads / A.n_kv;
+  const int g = blockIdx.x, s = blockIdx.y;
+  const int hd = A.hd, qpk = A.n_heads / A.n_kv, SUB = attn_sub(hd);
   const int pos = st->fwd_pos;
   if (pos < 0 || pos >= A.max_tokens) {
     if (tid == 0 && s == 0 && g == 0) atomicOr(&st->err, kErrPos);
@@ -506,17 +646,49 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   const int nsplit = attn_nsplit(n, A.max_splits);
   const int chunk = (n + nsplit - 1) / nsplit;
   if (s >= nsplit) return;
-  const int p0 = s * chunk, p1 = min(n, p0 + chunk);
-  const int len = p1 - p0;
+  const int p0 = min(n, s * chunk), p1 = min(n, p0 + chunk);
 
-  float *qs = asmem;            // [qpk][hd]
-  float *knew = qs + qpk * hd;  // [hd]
-  float *vnew = knew + hd;      // [hd]
-  float *sc = vnew + hd;        // [qpk][chunk_cap]
+  // KV layout [L][KVH][max_tokens][hd] per plane (engine/kvcache.go:127-140)
+  const size_t head_stride = static_cast<size_t>(A.max_tokens) * hd;
+  const size_t layer_stride = static_cast<size_t>(A.n_kv) * head_stride;
+  float *kc = A.kcache + static_cast<size_t>(A.layer) * layer_stride + g * head_stride;
+  float *vc = A.vcache + static_cast<size_t>(A.layer) * layer_stride + g * head_stride;
+
+  float *kbuf = asmem;                        // [2][SUB][hd]
+  float *vbuf = kbuf + 2 * SUB * hd;          // [2][SUB][hd]
+  float *qs = vbuf + 2 * SUB * hd;            // [qpk][hd]
+  float *knew = qs + qpk * hd;                // [hd]
+  float *vnew = knew + hd;                    // [hd]
+  float *sc = vnew + hd;                      // [qpk][SUB]
+  float *acc = sc + qpk * SUB;                // [qpk][hd]
+
+  // stage the cached rows of sub-chunk it into buffer it&1 (positions < pos)
+  auto issue = [&](int it) {
+    const int a = p0 + it * SUB, b = min(p1, a + SUB);
+    const int cached = max(0, min(b, pos) - a);
+    if (cached > 0) {
+      const uint32_t bytes = static_cast<uint32_t>(cached) * hd * 4;
+      uint64_t *bar = &bars[it & 1];
+      mbar_arrive_expect_tx(bar, 2 * bytes);
+      bulk_g2s(kbuf + (it & 1) * SUB * hd, kc + static_cast<size_t>(a) * hd, bytes, bar);
+      bulk_g2s(vbuf + (it & 1) * SUB * hd, vc + static_cast<size_t>(a) * hd, bytes, bar);
+    }
+  };
+  const int n_sub = (p1 - p0 + SUB - 1) / SUB;
+  if (tid == 0) {
+    issue(0);
+    if (n_sub > 1) issue(1);
+  }
+  // projections (bias already added by the QKV kernel), QK-norm, RoPE
   for (int i = tid; i < qpk * hd; i += kThreads) qs[i] = __ldcg(A.q + g * qpk * hd + i);
   for (int i = tid; i < hd; i += kThreads) {
     knew[i] = __ldcg(A.k + g * hd + i);
     vnew[i] = __ldcg(A.v + g * hd + i);
+  }
+  for (int i = tid; i < qpk * hd; i += kThreads) acc[i] = 0.f;
+  if (tid < 8) {
+    s_m[tid] = -INFINITY;
+    s_l[tid] = 0.f;
   }
   __syncthreads();
   if (A.q_norm)  // Qwen3 per-head QK-norm (engine/forward.go:80-91)
@@ -530,108 +702,106 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
     rope_rotate(knew, hd, cs, sn, tid, kThreads);
   }
   __syncthreads();
-  // KV layout [L][KVH][max_tokens][hd] per plane (engine/kvcache.go:127-140)
-  const size_t head_stride = static_cast<size_t>(A.max_tokens) * hd;
-  const size_t layer_stride = static_cast<size_t>(A.n_kv) * head_stride;
-  float *kc = A.kcache + static_cast<size_t>(A.layer) * layer_stride + g * head_stride;
-  float *vc = A.vcache + static_cast<size_t>(A.layer) * layer_stride + g * head_stride;
   if (pos >= p0 && pos < p1)  // KVCache.StoreKV (engine/kvcache.go:143-158)
     for (int i = tid; i < hd; i += kThreads) {
       kc[static_cast<size_t>(pos) * hd + i] = knew[i];
       vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
     }
-
-  // scores: s_p = (sum_d q_d k_pd) * scale, d in order, no FMA
-  // (internal/simd/c2_tensor_attn_nosimd_gen.go:7-24)
-  for (int t = tid; t < len; t += kThreads) {
-    const int p = p0 + t;
-    const float *kp = (p == pos) ? knew : kc + static_cast<size_t>(p) * hd;
-    float acc[8];
+  // q of every head of the group in registers: lane holds d = lane*E .. +E-1
+  const int E = hd / 32;  // 2 (hd 64) or 4 (hd 128)
+  float qr[8][4];
 #pragma unroll
-    for (int h = 0; h < 8; ++h) acc[h] = 0.f;
-    for (int d = 0; d < hd; d += 4) {
-      float4 kv4;
-      if (p == pos) kv4 = make_float4(kp[d], kp[d + 1], kp[d + 2], kp[d + 3]);
-      else kv4 = __ldcg(reinterpret_cast<const float4 *>(kp + d));
+  for (int h = 0; h < 8; ++h)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qr[h][j] = (h < qpk && j < E) ? qs[h * hd + lane * E + j] : 0.f;
+
+  bool ok_all = true;
+  for (int it = 0; it < n_sub; ++it) {
+    const int a = p0 + it * SUB, b = min(p1, a + SUB), len = b - a;
+    const int cached = max(0, min(b, pos) - a);
+    if (cached > 0) ok_all = mbar_wait_bounded(&bars[it & 1], (it >> 1) & 1, &st->err) && ok_all;
+    const float *kb = kbuf + (it & 1) * SUB * hd;
+    const float *vb = vbuf + (it & 1) * SUB * hd;
+    // scores: one warp per position, lanes over d
+    for (int t = warp; t < len; t += kWarps) {
+      const float *kp = (a + t == pos) ? knew : kb + t * hd;
+      float kv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = j < E ? kp[lane * E + j] : 0.f;
+      float dot[8];
 #pragma unroll
       for (int h = 0; h < 8; ++h) {
-        if (h < qpk) {
-          const float *qh = qs + h * hd + d;
-          acc[h] = __fadd_rn(acc[h], __fmul_rn(qh[0], kv4.x));
-          acc[h] = __fadd_rn(acc[h], __fmul_rn(qh[1], kv4.y));
-          acc[h] = __fadd_rn(acc[h], __fmul_rn(qh[2], kv4.z));
-          acc[h] = __fadd_rn(acc[h], __fmul_rn(qh[3], kv4.w));
-        }
+        float d0 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
+        dot[h] = d0;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int h = 0; h < 8; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
+      if (lane < qpk && lane < 8) {
+        float v = dot[0];
+#pragma unroll
+        for (int h = 1; h < 8; ++h) v = (lane == h) ? dot[h] : v;
+        sc[lane * SUB + t] = __fmul_rn(v, A.scale);
       }
     }
-    for (int h = 0; h < qpk && h < 8; ++h) sc[h * A.chunk_cap + t] = __fmul_rn(acc[h], A.scale);
-    for (int h = 8; h < qpk; ++h) {  // GQA groups wider than 8 heads
-      const float *qh = qs + h * hd;
-      float a = 0.f;
-      for (int d = 0; d < hd; ++d) a = __fadd_rn(a, __fmul_rn(qh[d], kp[d]));
-      sc[h * A.chunk_cap + t] = __fmul_rn(a, A.scale);
-    }
-  }
-  __syncthreads();
-  // per-head max over the split
-  for (int h0 = 0; h0 < qpk; h0 += 8) {
-    float m[8];
-#pragma unroll
-    for (int h = 0; h < 8; ++h) m[h] = -INFINITY;
-    for (int t = tid; t < len; t += kThreads)
-#pragma unroll
-      for (int h = 0; h < 8; ++h)
-        if (h0 + h < qpk) m[h] = fmaxf(m[h], sc[(h0 + h) * A.chunk_cap + t]);
-#pragma unroll
-    for (int h = 0; h < 8; ++h) m[h] = warp_max(m[h]);
-    if (lane == 0)
-#pragma unroll
-      for (int h = 0; h < 8; ++h) s_red[warp][h] = m[h];
     __syncthreads();
-    if (tid < 8 && h0 + tid < qpk) {
-      float mm = -INFINITY;
-      for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, s_red[w][tid]);
-      s_red[0][tid] = mm;
-    }
-    __syncthreads();
-    float mh[8];
-#pragma unroll
-    for (int h = 0; h < 8; ++h) mh[h] = s_red[0][h];
-    __syncthreads();
-    // e = float32(exp(float64(s - max)))  (tensor/ops.go:329-333)
-    for (int t = tid; t < len; t += kThreads)
-#pragma unroll
-      for (int h = 0; h < 8; ++h)
-        if (h0 + h < qpk) {
-          float &e = sc[(h0 + h) * A.chunk_cap + t];
-          e = static_cast<float>(exp(static_cast<double>(__fsub_rn(e, mh[h]))));
-        }
-    if (tid < 8 && h0 + tid < qpk) s_red[1][tid] = mh[tid];  // keep the max
-    __syncthreads();
-    if (tid < 8 && h0 + tid < qpk) {
+    // online softmax per head: warp h owns head h (e = exp in float64)
+    for (int h = warp; h < qpk; h += kWarps) {
+      float m = -INFINITY;
+      for (int t = lane; t < len; t += 32) m = fmaxf(m, sc[h * SUB + t]);
+      m = warp_max(m);
+      const float m_new = fmaxf(s_m[h], m);
       float l = 0.f;
-      for (int t = 0; t < len; ++t) l = __fadd_rn(l, sc[(h0 + tid) * A.chunk_cap + t]);
-      const int h = g * qpk + h0 + tid;
-      float *pp = A.part + (static_cast<size_t>(h) * A.max_splits + s) * (hd + 2);
-      pp[0] = s_red[1][tid];
-      pp[1] = l;
+      for (int t = lane; t < len; t += 32) {
+        const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sc[h * SUB + t], m_new))));
+        sc[h * SUB + t] = e;
+        l += e;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        const float scale = static_cast<float>(exp(static_cast<double>(s_m[h] - m_new)));
+        s_scale[h] = scale;
+        s_l[h] = s_l[h] * scale + l;
+        s_m[h] = m_new;
+      }
     }
     __syncthreads();
-  }
-  // acc_d = sum_p e_p v_pd (p in order)
-  for (int i = tid; i < qpk * hd; i += kThreads) {
-    const int h = i / hd, d = i - h * hd;
-    const float *e = sc + h * A.chunk_cap;
-    float a = 0.f;
-    for (int t = 0; t < len; ++t) {
-      const int p = p0 + t;
-      const float vv = (p == pos) ? vnew[d] : __ldcg(vc + static_cast<size_t>(p) * hd + d);
-      a = __fadd_rn(a, __fmul_rn(e[t], vv));
+    // acc[h][d] = acc*scale + sum_t e[h][t] v[t][d]
+    for (int i = tid; i < qpk * hd; i += kThreads) {
+      const int h = i / hd, d = i - h * hd;
+      const float *e = sc + h * SUB;
+      float a0 = 0.f, a1 = 0.f;
+      int t = 0;
+      for (; t + 1 < len; t += 2) {
+        const float v0 = (a + t == pos) ? vnew[d] : vb[t * hd + d];
+        const float v1 = (a + t + 1 == pos) ? vnew[d] : vb[(t + 1) * hd + d];
+        a0 = fmaf(e[t], v0, a0);
+        a1 = fmaf(e[t + 1], v1, a1);
+      }
+      if (t < len) a0 = fmaf(e[t], (a + t == pos) ? vnew[d] : vb[t * hd + d], a0);
+      acc[i] = acc[i] * s_scale[h] + (a0 + a1);
     }
-    float *pp = A.part + (static_cast<size_t>(g * qpk + h) * A.max_splits + s) * (hd + 2);
-    pp[2 + d] = a;
+    __syncthreads();
+    if (tid == 0 && it + 2 < n_sub) issue(it + 2);
   }
-  // the last split of this kv head combines (flash-decoding rescale)
+  (void)ok_all;
+  const int h0 = g * qpk;
+  if (nsplit == 1) {  // single split: normalise and write the heads directly
+    for (int i = tid; i < qpk * hd; i += kThreads) {
+      const int h = i / hd;
+      A.out[(h0 + h) * hd + (i - h * hd)] = acc[i] / s_l[h];
+    }
+    return;
+  }
+  // partial (m, l, acc) of this split; the last split of the group combines
+  for (int i = tid; i < qpk * (hd + 2); i += kThreads) {
+    const int h = i / (hd + 2), k = i - h * (hd + 2);
+    float *pp = A.part + (static_cast<size_t>(h0 + h) * A.max_splits + s) * (hd + 2);
+    pp[k] = k == 0 ? s_m[h] : (k == 1 ? s_l[h] : acc[h * hd + k - 2]);
+  }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -642,7 +812,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   if (!s_last) return;
   __threadfence();
   for (int i = tid; i < qpk * hd; i += kThreads) {
-    const int h = g * qpk + i / hd, d = i % hd;
+    const int h = h0 + i / hd, d = i % hd;
     const float *base = A.part + static_cast<size_t>(h) * A.max_splits * (hd + 2);
     float M = -INFINITY;
     for (int k = 0; k < nsplit; ++k) M = fmaxf(M, __ldcg(base + static_cast<size_t>(k) * (hd + 2)));
@@ -650,10 +820,10 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
     for (int k = 0; k < nsplit; ++k) {
       const float *pk = base + static_cast<size_t>(k) * (hd + 2);
       const float w = static_cast<float>(exp(static_cast<double>(__fsub_rn(__ldcg(pk), M))));
-      L = __fadd_rn(L, __fmul_rn(w, __ldcg(pk + 1)));
-      O = __fadd_rn(O, __fmul_rn(w, __ldcg(pk + 2 + d)));
+      L = fmaf(w, __ldcg(pk + 1), L);
+      O = fmaf(w, __ldcg(pk + 2 + d), O);
     }
-    A.out[h * hd + d] = __fmul_rn(O, __fdiv_rn(1.f, L));
+    A.out[h * hd + d] = O / L;
   }
   if (tid == 0) st->attn_counter[g] = 0;
 }
@@ -751,7 +921,8 @@ __global__ void __launch_bounds__(kThreads) k_dot_rows_f32x(int type, const uint
           const uint32_t qh = static_cast<uint32_t>(ld16(b + 2)) | (static_cast<uint32_t>(ld16(b + 4)) << 16);
           const int k = e & 15;
           const int nib = e < 16 ? (b[6 + k] & 15) : (b[6 + k] >> 4);
-          q = static_cast<float>((nib | (((qh >> (e < 16 ? k : k + 16)) & 1) << 4)) - 16);
+          const int hb = static_cast<int>((qh >> (e < 16 ? k : k + 16)) & 1u);
+          q = static_cast<float>((nib | (hb << 4)) - 16);
         }
         v = __fadd_rn(v, __fmul_rn(q, x[bi * 32 + e]));
       }

@@ -47,6 +47,7 @@ SIGNATURES = {
     "c2s_kernels_per_step": (I, [P]),
     "c2s_bench_decode_timed": (I, [P, I, F, I, I, C.POINTER(F)]),
     "c2s_profile_step": (I, [P, I, F, I, P, P]),
+    "c2s_trace_decode": (I, [P, I, F, I, P, C.POINTER(I)]),
     "c2s_quantize_row_q8_k": (I, [P, P, I]),
     "c2s_gemv": (I, [I, P, P, P, I, I]),
     "c2s_gemv_device": (I, [I, I, P, P, P, I, I]),
@@ -368,6 +369,14 @@ class Engine:
         cnt = np.zeros(8, np.int32)
         _check(load_library().c2s_profile_step(self._h, n_steps, penalty, window, _ptr(ms), _ptr(cnt)))
         return {name: {"ms": float(ms[k]), "launches": int(cnt[k])} for k, name in self.STAGES.items()}
+
+    def trace_decode(self, n_steps: int, penalty: float = 1.15, window: int = 64) -> np.ndarray:
+        """Per-phase start/end stamps (ns) of the persistent decode kernel for
+        CTAs 0..3: array [n_steps, nphase, 4, 2]."""
+        nph = C.c_int(0)
+        buf = np.zeros(n_steps * 4 * 2 * (5 * self.desc.n_layers + 1), np.uint64)
+        _check(load_library().c2s_trace_decode(self._h, n_steps, penalty, window, _ptr(buf), C.byref(nph)))
+        return buf.reshape(n_steps, nph.value, 4, 2)
 
     @property
     def kernels_per_step(self) -> int:

@@ -153,6 +153,12 @@ int c2s_bench_decode_timed(c2s_engine *e, int n_steps, float penalty, int window
  * 7 = attention(+QK-norm, RoPE, KV append). */
 int c2s_profile_step(c2s_engine *e, int n_steps, float penalty, int window, float *stage_ms,
                      int *stage_launches);
+/* Phase trace of the persistent decode kernel: runs n_steps decode steps and
+ * returns %globaltimer stamps [step][phase][cta 0..3][start, end] (ns) in
+ * trace_out (n_steps * nphase * 8 values); *nphase_out = phases per step
+ * (1 logits phase, then 5 per layer: qkv, attention, o-proj, gate/up, down). */
+int c2s_trace_decode(c2s_engine *e, int n_steps, float penalty, int window, uint64_t *trace_out,
+                     int *nphase_out);
 /* Number of kernels one decode step launches (for the bench's launch count). */
 int c2s_kernels_per_step(const c2s_engine *e);
 

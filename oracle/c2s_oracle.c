@@ -526,6 +526,87 @@ void c2o_attn_av(const float *scores, const float *vbase, int pos, int stride,
 }
 
 /* ------------------------------------------------------------------------ */
+/* The reference's AVX2 build (GOEXPERIMENT=simd) evaluates three kernels of  */
+/* the 0.5B path in a different float order than the scalar twins above:     */
+/* attention QK and AV use fused multiply-add, SwiGLU uses a polynomial exp.  */
+/* Restated here so the scalar and SIMD builds of the reference can be        */
+/* compared with each other.                                                  */
+/* ------------------------------------------------------------------------ */
+/* internal/simd/c2_tensor_attn_gen.go:9-58 (AVX2 branch; hd % 8 == 0) */
+void c2o_attn_qk_simd(const float *q, const float *kbase, int pos, int stride, float scale,
+                      float *scores, int hd) {
+    for (int p = 0; p <= pos; p++) {
+        const float *k = kbase + (size_t)p * stride;
+        float a[8] = {0}, b[8] = {0};
+        int d = 0;
+        for (; d + 16 <= hd; d += 16)
+            for (int i = 0; i < 8; i++) {
+                a[i] = fmaf(q[d + i], k[d + i], a[i]);
+                b[i] = fmaf(q[d + 8 + i], k[d + 8 + i], b[i]);
+            }
+        for (; d + 8 <= hd; d += 8)
+            for (int i = 0; i < 8; i++) a[i] = fmaf(q[d + i], k[d + i], a[i]);
+        float v[8];
+        for (int i = 0; i < 8; i++) v[i] = a[i] + b[i];
+        float acc = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+        for (; d < hd; d++) acc += q[d] * k[d];
+        scores[p] = acc * scale;
+    }
+}
+
+/* internal/simd/c2_tensor_attn_gen.go:68-112 (AVX2 branch): per output
+ * element, sequential over positions with fused multiply-add. */
+void c2o_attn_av_simd(const float *scores, const float *vbase, int pos, int stride,
+                      float *out, int hd) {
+    const int dv = hd - hd % 8;  /* 8-wide vector columns; the rest is scalar */
+    for (int d = 0; d < hd; d++) {
+        float acc = 0;
+        if (d < dv)
+            for (int p = 0; p <= pos; p++) acc = fmaf(scores[p], vbase[(size_t)p * stride + d], acc);
+        else
+            for (int p = 0; p <= pos; p++) acc += scores[p] * vbase[(size_t)p * stride + d];
+        out[d] = acc;
+    }
+}
+
+/* internal/simd/c2_tensor_swiglu_gen.go:11-57 (AVX2 branch, 8 at a time;
+ * tail in float64 like the scalar twin).  Truncating float->int conversion. */
+static float bitsf(uint32_t u) { return f32_from_bits(u); }
+void c2o_swiglu_simd(float *out, const float *gate, const float *up, int n) {
+    const float half = bitsf(0x3f000000u), one = bitsf(0x3f800000u);
+    const float inv_ln2 = bitsf(0x3fb8aa3bu), ln2 = bitsf(0x3f317218u);
+    const float c5 = bitsf(0x3c088888u), c4 = bitsf(0x3d2aaaabu), c3 = bitsf(0x3e2aaaabu);
+    const int nv = n - n % 8;  /* 8-wide vector part; the tail is scalar */
+    int i = 0;
+    for (; i < nv; i++) {
+        float x = gate[i];
+        float nx = -x;
+        float nf = nx * inv_ln2;
+        /* x86 cvttps2dq returns INT32_MIN for out-of-range input */
+        float fp = nf + half, fn = nf - half;
+        int npos = (fp >= -2147483648.0f && fp < 2147483648.0f) ? (int)fp : INT32_MIN;
+        int nneg = (fn >= -2147483648.0f && fn < 2147483648.0f) ? (int)fn : INT32_MIN;
+        int ni = nf >= 0.0f ? npos : nneg;
+        if (ni < -126) ni = -126;
+        if (ni > 127) ni = 127;
+        float nif = (float)ni;
+        float r = nx - nif * ln2;
+        float p = ((((c5 * r + c4) * r + c3) * r + half) * r + one) * r + one;
+        float scl = f32_from_bits((uint32_t)(ni + 127) << 23);
+        float ev = p * scl;
+        float den = one + ev;
+        float sig = one / den;
+        float silu = x * sig;
+        out[i] = silu * up[i];
+    }
+    for (; i < n; i++) {
+        double g = (double)gate[i];
+        float silu = (float)(g / (1.0 + exp(-g)));
+        out[i] = silu * up[i];
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Worker pool: engine/pool.go:16-154,180-208.                              */
 /* n persistent workers; the caller publishes a task and waits.              */
 /* ------------------------------------------------------------------------ */
@@ -761,6 +842,7 @@ struct c2o_model {
     float *attn_scratch; /* per worker scores for parallel heads */
     c2o_pool *pool;
     int nthreads;
+    int simd_order;      /* 1: restate the reference's AVX2 build */
 };
 
 static void set_err(char *err, int errlen, const char *fmt, ...) {
@@ -1090,9 +1172,11 @@ static void attention_head(c2o_model *m, int layer, int pos, int h, float scale,
     const float *q = m->Q + h * m->hd;
     const float *kb = m->kv + kv_off(m, 0, layer, kvh, 0);
     const float *vb = m->kv + kv_off(m, 1, layer, kvh, 0);
-    c2o_attn_qk(q, kb, pos, m->hd, scale, scores, m->hd);
+    if (m->simd_order) c2o_attn_qk_simd(q, kb, pos, m->hd, scale, scores, m->hd);
+    else c2o_attn_qk(q, kb, pos, m->hd, scale, scores, m->hd);
     c2o_softmax(scores, pos + 1);
-    c2o_attn_av(scores, vb, pos, m->hd, m->AttnOut + h * m->hd, m->hd);
+    if (m->simd_order) c2o_attn_av_simd(scores, vb, pos, m->hd, m->AttnOut + h * m->hd, m->hd);
+    else c2o_attn_av(scores, vb, pos, m->hd, m->AttnOut + h * m->hd, m->hd);
 }
 
 static void attn_worker(void *arg, int wid, int nw) {  /* engine/pool.go:159-175 */
@@ -1145,7 +1229,8 @@ void c2o_forward(c2o_model *m, int32_t token, int pos, float *normx_out) {
         c2o_rmsnorm(m->NormX, m->X, m->layers[l].ffn_norm, H, m->eps);
         gemv_t(m, m->Gate, m->layers[l].gate, m->NormX, m->ffn, H);
         gemv_t(m, m->Up, m->layers[l].up, m->NormX, m->ffn, H);
-        c2o_swiglu(m->Gate, m->Gate, m->Up, m->ffn);
+        if (m->simd_order) c2o_swiglu_simd(m->Gate, m->Gate, m->Up, m->ffn);
+        else c2o_swiglu(m->Gate, m->Gate, m->Up, m->ffn);
         gemv_t(m, m->Down, m->layers[l].down, m->Gate, H, m->ffn);
         for (int i = 0; i < H; i++) m->X[i] += m->Down[i];
     }
@@ -1196,6 +1281,8 @@ int32_t c2o_select(c2o_model *m, float *logits, int cur_pos, float penalty, int 
         if (logits[id] > bv) { bv = logits[id]; best = id; }
     return best;
 }
+
+void c2o_model_set_simd_order(c2o_model *m, int on) { m->simd_order = on ? 1 : 0; }
 
 int c2o_kv_seq_len(const c2o_model *m) { return m->seq_len; }
 void c2o_kv_set_seq_len(c2o_model *m, int n) { m->seq_len = n; }

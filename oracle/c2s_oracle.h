@@ -88,6 +88,14 @@ void  c2o_attn_qk(const float *q, const float *kbase, int pos, int stride, float
 void  c2o_attn_av(const float *scores, const float *vbase, int pos, int stride,
                   float *out, int hd);
 
+/* The reference's AVX2 build (GOEXPERIMENT=simd): the kernels whose float
+ * order differs from the scalar twins on the Q5_0/Q4_K/Q6_K/Q8_0 path. */
+void  c2o_attn_qk_simd(const float *q, const float *kbase, int pos, int stride, float scale,
+                       float *scores, int hd);
+void  c2o_attn_av_simd(const float *scores, const float *vbase, int pos, int stride,
+                       float *out, int hd);
+void  c2o_swiglu_simd(float *out, const float *gate, const float *up, int n);
+
 /* ---- model ------------------------------------------------------------- */
 typedef struct c2o_model c2o_model;
 
@@ -106,6 +114,8 @@ c2o_model *c2o_model_open(const char *path, int max_tokens, int nthreads,
                           char *err, int errlen);
 void  c2o_model_close(c2o_model *m);
 void  c2o_model_get_info(const c2o_model *m, c2o_model_info *info);
+/* 1: evaluate attention and SwiGLU in the AVX2 build's order (default 0). */
+void  c2o_model_set_simd_order(c2o_model *m, int on);
 
 /* engine.Forward (engine/forward.go:54-138); writes NormX (embd floats). */
 void  c2o_forward(c2o_model *m, int32_t token, int pos, float *normx_out);

@@ -73,6 +73,10 @@ def _declare(L: C.CDLL) -> None:
         "c2o_model_open": (P, [C.c_char_p, I, I, C.c_char_p, I]),
         "c2o_model_close": (None, [P]),
         "c2o_model_get_info": (None, [P, P]),
+        "c2o_model_set_simd_order": (None, [P, I]),
+        "c2o_attn_qk_simd": (None, [P, P, I, I, F, P, I]),
+        "c2o_attn_av_simd": (None, [P, P, I, I, P, I]),
+        "c2o_swiglu_simd": (None, [P, P, P, I]),
         "c2o_forward": (None, [P, C.c_int32, I, P]),
         "c2o_compute_logits": (None, [P, P, P, P, I]),
         "c2o_select": (C.c_int32, [P, P, I, F, I]),
@@ -212,24 +216,26 @@ def softmax(x) -> np.ndarray:
     return v
 
 
-def swiglu(g, u) -> np.ndarray:
+def swiglu(g, u, simd: bool = False) -> np.ndarray:
     g, u = _f32(g), _f32(u)
     out = np.zeros_like(g)
-    lib().c2o_swiglu(_p(out), _p(g), _p(u), g.size)
+    (lib().c2o_swiglu_simd if simd else lib().c2o_swiglu)(_p(out), _p(g), _p(u), g.size)
     return out
 
 
-def attn_qk(q, kbase, pos: int, stride: int, scale: float, hd: int) -> np.ndarray:
+def attn_qk(q, kbase, pos: int, stride: int, scale: float, hd: int, simd: bool = False) -> np.ndarray:
     q, kbase = _f32(q), _f32(kbase)
     s = np.zeros(pos + 1, np.float32)
-    lib().c2o_attn_qk(_p(q), _p(kbase), pos, stride, scale, _p(s), hd)
+    fn = lib().c2o_attn_qk_simd if simd else lib().c2o_attn_qk
+    fn(_p(q), _p(kbase), pos, stride, scale, _p(s), hd)
     return s
 
 
-def attn_av(scores, vbase, pos: int, stride: int, hd: int) -> np.ndarray:
+def attn_av(scores, vbase, pos: int, stride: int, hd: int, simd: bool = False) -> np.ndarray:
     scores, vbase = _f32(scores), _f32(vbase)
     out = np.zeros(hd, np.float32)
-    lib().c2o_attn_av(_p(scores), _p(vbase), pos, stride, _p(out), hd)
+    fn = lib().c2o_attn_av_simd if simd else lib().c2o_attn_av
+    fn(_p(scores), _p(vbase), pos, stride, _p(out), hd)
     return out
 
 
@@ -245,7 +251,7 @@ class ModelInfo(C.Structure):
 class OracleModel:
     """engine.Model + KVCache + Arena on the CPU (engine/model.go:58, kvcache.go:49)."""
 
-    def __init__(self, path: str, max_tokens: int = 16384, nthreads: int = 1):
+    def __init__(self, path: str, max_tokens: int = 16384, nthreads: int = 1, simd_order: bool = False):
         err = C.create_string_buffer(512)
         self._h = lib().c2o_model_open(path.encode(), max_tokens, nthreads, err, 512)
         if not self._h:
@@ -253,6 +259,8 @@ class OracleModel:
         info = ModelInfo()
         lib().c2o_model_get_info(self._h, C.byref(info))
         self.info = info
+        if simd_order:  # evaluate like the reference's AVX2 build
+            lib().c2o_model_set_simd_order(self._h, 1)
 
     def close(self):
         if self._h:
