@@ -65,13 +65,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait: gives up after ~2 s of wall time, sets *err and returns false.
+// Wait budget for every bounded spin: ~2 s at the B200's ~2 GHz SM clock,
+// measured with the SM-local cycle counter (cheap to read, unlike
+// %globaltimer).
+constexpr long long kSpinCycles = 4000000000LL;
+
+// Bounded wait: gives up after kSpinCycles, sets *err and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, unsigned *err) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   for (uint32_t it = 0; it < (1u << 30); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) break;
+    if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) break;
   }
   atomicOr(err, kErrMbarTimeout);
   return false;

@@ -732,13 +732,30 @@ int persistent_setup(c2s_engine *e) {
   off = (off + 127) & ~size_t(127);
   P.off_act = static_cast<int>(off);
   e->p_smem = off + act;
-  // parameters
+  // parameters: the layer table travels in the kernel's parameter space
+  if (L > kMaxLayers) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: more than %d layers", kMaxLayers);
+  if (H > 16 * kThreads) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: embd above %d", 16 * kThreads);
+  static_assert(sizeof(PParams) < 32000, "kernel parameter space");
+  for (int l = 0; l < L; ++l) {
+    const LayerDev &Ld = e->layers[l];
+    PLayer &y = P.layers[l];
+    y.q = Ld.q; y.k = Ld.k; y.v = Ld.v; y.o = Ld.o; y.gate = Ld.gate; y.up = Ld.up; y.down = Ld.down;
+    y.attn_norm = Ld.attn_norm; y.ffn_norm = Ld.ffn_norm;
+    y.qb = Ld.qb; y.kb = Ld.kb; y.vb = Ld.vb; y.qn = Ld.qn; y.kn = Ld.kn;
+    y.tq = static_cast<int8_t>(Ld.tq); y.tk = static_cast<int8_t>(Ld.tk); y.tv = static_cast<int8_t>(Ld.tv);
+    y.to = static_cast<int8_t>(Ld.to); y.tg = static_cast<int8_t>(Ld.tgate); y.tu = static_cast<int8_t>(Ld.tup);
+    y.td = static_cast<int8_t>(Ld.tdown);
+  }
+  P.out_w = e->output;
+  P.out_norm = e->out_norm;
+  P.out_type = e->out_type;
+  P.n_layers = L;
+  P.F = F;
+  P.kvd = kvd;
+  P.vocab = d.vocab;
   e->nphase = static_cast<int>(ph.size());
-  CK(cudaMalloc(&e->d_phases, sizeof(PPhase) * ph.size()));
-  CK(cudaMemcpy(e->d_phases, ph.data(), sizeof(PPhase) * ph.size(), cudaMemcpyHostToDevice));
-  CK(cudaMalloc(&e->gbar, 64));
-  CK(cudaMemset(e->gbar, 0, 64));
-  P.phases = e->d_phases;
+  CK(cudaMalloc(&e->gbar, 4 * static_cast<size_t>(G) + 64));
+  CK(cudaMemset(e->gbar, 0, 4 * static_cast<size_t>(G) + 64));
   P.nphase = e->nphase;
   P.H = H;
   P.n_heads = d.n_heads;
@@ -787,7 +804,7 @@ int launch_persistent(c2s_engine *e, int n_steps, int rewind_period, int rewind_
   P.n_steps = n_steps;
   P.rewind_period = rewind_period;
   P.rewind_base = rewind_base;
-  CK(cudaMemsetAsync(e->gbar, 0, sizeof(unsigned), e->stream));
+  CK(cudaMemsetAsync(e->gbar, 0, 4 * static_cast<size_t>(e->num_sms), e->stream));
   void *args[] = {&P};
   CK(cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(k_persistent), dim3(e->num_sms), dim3(kPThreads),
                                  args, e->p_smem, e->stream));
@@ -1015,7 +1032,7 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->part), static_cast<void *>(e->amax_part), static_cast<void *>(e->token_ids),
                   static_cast<void *>(e->out_tokens), static_cast<void *>(e->rows_idx),
                   static_cast<void *>(e->scratch_x), static_cast<void *>(e->st),
-                  static_cast<void *>(e->d_phases), static_cast<void *>(e->gbar)})
+                  static_cast<void *>(e->gbar)})
     if (p) cudaFree(p);
   for (void *p : {static_cast<void *>(e->h_in), static_cast<void *>(e->h_buf), static_cast<void *>(e->h_st),
                   static_cast<void *>(e->h_tokens)})
@@ -1426,7 +1443,7 @@ int c2s_trace_decode(c2s_engine *e, int n_steps, float penalty, int window, uint
   if (n_steps <= 0 || n_steps > e->d.max_tokens - e->host_seq) return fail(C2S_ERR_ARG, "n_steps out of range");
   DeviceGuard g(e->device);
   if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
-  const size_t n = static_cast<size_t>(n_steps) * e->nphase * 4 * 2;
+  const size_t n = static_cast<size_t>(n_steps) * e->nphase * e->num_sms * c2s::kTraceFields;
   unsigned long long *dtr = nullptr;
   CK(cudaMalloc(&dtr, n * 8));
   CK(cudaMemsetAsync(dtr, 0, n * 8, e->stream));

@@ -144,6 +144,84 @@ __device__ __forceinline__ float blockdot_q5_0_reg(const uint8_t *blk, const flo
   return d * ((a0 + a1) + (a2 + a3));
 }
 
+// ---------------------------------------------------------------------------
+// f32 activation of one 32-value block split into three int8 limbs:
+//   x = s * (a + b/254 + c/254^2),  s = max|x|/127,  a, b, c in [-127, 127]
+// (reconstruction error <= ~6.2e-8 * max|x|).  A Q8_0 / Q5_0 block dot is
+// then three int8 dp4a chains and one f32 combine.
+// ---------------------------------------------------------------------------
+struct XLimbs {
+  int a[8], b[8], c[8];
+  float s;
+};
+
+__device__ __forceinline__ void make_limbs(const float (&x)[32], XLimbs &L) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
+  L.s = amax / 127.f;
+  const float inv = amax > 0.f ? 127.f / amax : 0.f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    uint32_t wa = 0, wb = 0, wc = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float y = x[4 * t + e] * inv;
+      const float a = rintf(y);
+      const float r1 = __fmul_rn(y - a, 254.f);
+      const float b = rintf(r1);
+      const float c = rintf(__fmul_rn(r1 - b, 254.f));
+      wa |= (static_cast<uint32_t>(static_cast<int>(a)) & 0xFFu) << (8 * e);
+      wb |= (static_cast<uint32_t>(static_cast<int>(b)) & 0xFFu) << (8 * e);
+      wc |= (static_cast<uint32_t>(static_cast<int>(c)) & 0xFFu) << (8 * e);
+    }
+    L.a[t] = static_cast<int>(wa);
+    L.b[t] = static_cast<int>(wb);
+    L.c[t] = static_cast<int>(wc);
+  }
+}
+
+__device__ __forceinline__ float limbs_combine(int A, int B, int C, float s) {
+  const float k = 1.f / 254.f;
+  return s * fmaf(fmaf(static_cast<float>(C), k, static_cast<float>(B)), k, static_cast<float>(A));
+}
+
+// Q8_0 block (int8 weights) . limb-split x
+__device__ __forceinline__ float blockdot_q8_0_limbs(const uint8_t *blk, const XLimbs &L) {
+  const float d = h2f(ld16(blk));
+  int A = 0, B = 0, C = 0;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const int w = static_cast<int>(ld32u(blk + 2 + 4 * t));
+    A = __dp4a(w, L.a[t], A);
+    B = __dp4a(w, L.b[t], B);
+    C = __dp4a(w, L.c[t], C);
+  }
+  return d * limbs_combine(A, B, C, L.s);
+}
+
+// Q5_0 block . limb-split x: int8(u - 16) = nibble | (hbit ? 0 : 0xF0)
+__device__ __forceinline__ float blockdot_q5_0_limbs(const uint8_t *blk, const XLimbs &L) {
+  const float d = h2f(ld16(blk));
+  const uint32_t qh = static_cast<uint32_t>(ld16(blk + 2)) | (static_cast<uint32_t>(ld16(blk + 4)) << 16);
+  int A = 0, B = 0, C = 0;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint32_t w = ld32u(blk + 6 + 4 * t);
+    const uint32_t hl = spread4((qh >> (4 * t)) & 0xFu) ^ 0x01010101u;
+    const uint32_t hh = spread4((qh >> (16 + 4 * t)) & 0xFu) ^ 0x01010101u;
+    const int lo = static_cast<int>((w & 0x0F0F0F0Fu) | (hl * 0xF0u));
+    const int hi = static_cast<int>(((w >> 4) & 0x0F0F0F0Fu) | (hh * 0xF0u));
+    A = __dp4a(lo, L.a[t], A);
+    B = __dp4a(lo, L.b[t], B);
+    C = __dp4a(lo, L.c[t], C);
+    A = __dp4a(hi, L.a[4 + t], A);
+    B = __dp4a(hi, L.b[4 + t], B);
+    C = __dp4a(hi, L.c[4 + t], C);
+  }
+  return d * limbs_combine(A, B, C, L.s);
+}
+
 // One warp's partial over units u = u0 + lane + k*ustep of one row (K-quants
 // and the generic f32 path).  All lanes must call it (Q6_K shuffles).
 template <int TYPE>
@@ -192,19 +270,37 @@ __device__ __forceinline__ float row_units(const MatParams &P, const uint8_t *ro
 template <int TYPE>
 __device__ __forceinline__ void compute_chunk_t(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
                                                 int grow0, const float *xt, int nbx, const Q8KView &q8, float *y,
-                                                float (*red)[kWarps], const float (&xr)[32], bool xreg) {
+                                                float (*red)[kWarps], const XLimbs &xl, bool xreg) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int U = S.units;
   if ((TYPE == T_Q5_0 || TYPE == T_Q8_0) && xreg) {
-    for (int r = warp; r < nr; r += kWarps) {
-      const uint8_t *row = rows_smem + static_cast<size_t>(r) * S.row_bytes;
-      float acc = 0.f;
+    // lane = block; two rows per round for instruction-level parallelism
+    const int bsz = TYPE == T_Q8_0 ? 34 : 22;
+    int r = warp;
+    for (; r + kWarps < nr; r += 2 * kWarps) {
+      const uint8_t *r0 = rows_smem + static_cast<size_t>(r) * S.row_bytes + lane * bsz;
+      const uint8_t *r1 = r0 + static_cast<size_t>(kWarps) * S.row_bytes;
+      float a0 = 0.f, a1 = 0.f;
       if (lane < U) {
-        if (TYPE == T_Q8_0) acc = blockdot_q8_0_reg(row + lane * 34, xr);
-        else acc = blockdot_q5_0_reg(row + lane * 22, xr);
+        a0 = TYPE == T_Q8_0 ? blockdot_q8_0_limbs(r0, xl) : blockdot_q5_0_limbs(r0, xl);
+        a1 = TYPE == T_Q8_0 ? blockdot_q8_0_limbs(r1, xl) : blockdot_q5_0_limbs(r1, xl);
       }
-      acc = warp_sum(acc);
-      if (lane == 0) y[r] = acc;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+      }
+      if (lane == 0) {
+        y[r] = a0;
+        y[r + kWarps] = a1;
+      }
+    }
+    if (r < nr) {
+      const uint8_t *r0 = rows_smem + static_cast<size_t>(r) * S.row_bytes + lane * bsz;
+      float a0 = 0.f;
+      if (lane < U) a0 = TYPE == T_Q8_0 ? blockdot_q8_0_limbs(r0, xl) : blockdot_q5_0_limbs(r0, xl);
+      a0 = warp_sum(a0);
+      if (lane == 0) y[r] = a0;
     }
     return;
   }
@@ -245,14 +341,23 @@ __device__ __forceinline__ void compute_chunk_t(const MatParams &P, const Seg &S
 
 __device__ __forceinline__ void compute_chunk(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
                                               int grow0, const float *xt, int nbx, const Q8KView &q8, float *y,
-                                              float (*red)[kWarps], const float (&xr)[32], bool xreg) {
+                                              float (*red)[kWarps], const XLimbs &xl, bool xreg) {
   switch (S.type) {
-    case T_Q4_K: compute_chunk_t<T_Q4_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
-    case T_Q6_K: compute_chunk_t<T_Q6_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
-    case T_Q5_0: compute_chunk_t<T_Q5_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
-    case T_Q8_0: compute_chunk_t<T_Q8_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xr, xreg); break;
+    case T_Q4_K: compute_chunk_t<T_Q4_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
+    case T_Q6_K: compute_chunk_t<T_Q6_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
+    case T_Q5_0: compute_chunk_t<T_Q5_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
+    case T_Q8_0: compute_chunk_t<T_Q8_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
     default: break;
   }
+}
+
+// this lane's block (block = lane) of the transposed f32 activation -> limbs
+__device__ __forceinline__ void lane_limbs(const float *xt, int nbx, XLimbs &xl) {
+  const int lane = threadIdx.x & 31;
+  float xr[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) xr[k] = lane < nbx ? xt[k * nbx + lane] : 0.f;
+  make_limbs(xr, xl);
 }
 
 // Loads n floats (n % 4 == 0, 16-B aligned) from global into shared memory,
@@ -412,14 +517,10 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
     for (int i = tid; i < P.cols; i += kThreads) xt[(i & 31) * nbx + (i >> 5)] = xn[i];
   if (P.need_q8k) build_q8k(xn, P.cols, q8qs, q8d, q8bs);
   __syncthreads();
-  // f32 x of this lane's block in registers (types with <= 32 blocks per row)
-  float xr[32];
+  // this lane's block of x as int8 limbs in registers (rows of <= 32 blocks)
+  XLimbs xl;
   const bool xreg = P.need_f32 && nbx <= 32;
-  if (xreg) {
-    const int lane = tid & 31;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) xr[k] = lane < nbx ? xt[k * nbx + lane] : 0.f;
-  }
+  if (xreg) lane_limbs(xt, nbx, xl);
 
   // ---- stream the chunks
   float *ybuf = reinterpret_cast<float *>(smem + P.off_y);
@@ -440,7 +541,7 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
       const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
       const uint8_t *rows = smem + sidx * kStageAlloc + (src & 15);
       compute_chunk(P, S, rows, ch.r1 - ch.r0, ch.r0, xt, nbx, q8,
-                    ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]), red, xr, xreg);
+                    ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]), red, xl, xreg);
     }
     __syncthreads();
     if (tid == 0 && i + kStages < nchunks)

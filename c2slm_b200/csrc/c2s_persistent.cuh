@@ -30,8 +30,22 @@ struct PPhase {
   int do_embed, commit_here, need_f32, need_q8k;
 };
 
+constexpr int kMaxLayers = 32;
+
+// One layer's tensors, as the persistent kernel needs them.  The whole table
+// travels in the kernel's parameter space (constant bank), so building a
+// phase descriptor costs no global-memory round trip.
+struct PLayer {
+  const uint8_t *q, *k, *v, *o, *gate, *up, *down;
+  const float *attn_norm, *ffn_norm, *qb, *kb, *vb, *qn, *kn;
+  int8_t tq, tk, tv, to, tg, tu, td, pad;
+};
+
 struct PParams {
-  const PPhase *phases;
+  PLayer layers[kMaxLayers];
+  const uint8_t *out_w;
+  const float *out_norm;
+  int out_type, n_layers, F, kvd, vocab;
   int nphase, n_steps;
   int nslot;
   int off_full, off_empty, off_abar, off_act;
@@ -46,11 +60,40 @@ struct PParams {
   int embd_type, embd_row_bytes;
   DevState *st;
   int *token_ids, *out_tokens;
-  unsigned *gbar;       // grid barrier counter, zero at launch
+  unsigned *gbar;       // grid barrier arrival counter, zero at launch
   int rewind_period;    // > 0: SeqLen returns to rewind_base every period steps
   int rewind_base;
-  unsigned long long *trace;  // optional: [step][phase][cta<4][start, end] globaltimer ns
+  unsigned long long *trace;  // optional: [step][phase][cta][kTraceFields], see k_persistent
 };
+
+// trace record per (step, phase, CTA): globaltimer ns at phase start (after
+// the grid barrier), inputs ready, chunks done and end; then SM cycles thread
+// 0 spent waiting for weight chunks, in the grid barrier before the phase, in
+// the chunk loop, and the cycle counter at phase start.
+constexpr int kTraceFields = 8;
+
+__host__ __device__ inline int qrow_bytes(int type, int cols) {
+  return type == T_Q5_0 ? (cols / 32) * 22
+         : type == T_Q8_0 ? (cols / 32) * 34
+         : type == T_Q4_K ? (cols / 256) * 144
+         : type == T_Q6_K ? (cols / 256) * 210 : cols * 4;
+}
+
+__device__ __forceinline__ Seg pseg(const uint8_t *w, int type, int rows, int cols, const float *bias, float *out) {
+  Seg s;
+  s.w = w;
+  s.type = type;
+  s.rows = rows;
+  s.row_bytes = qrow_bytes(type, cols);
+  s.units = (type == T_Q4_K || type == T_Q6_K) ? (cols / 256) * 4 : cols / 32;
+  s.rows_per_chunk = max(1, kStageBytes / s.row_bytes);
+  s.bias = bias;
+  s.out = out;
+  return s;
+}
+
+struct PParams;
+__device__ void build_phase(const PParams &P, int pi, PPhase &ph);
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
   unsigned v;
@@ -68,27 +111,25 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-// Grid-wide barrier of the compute warps: every CTA adds 1, all wait until the
-// counter reaches `target`.  Bounded (~2 s): on expiry sets the error flag and
-// returns false (the caller stops).
-__device__ __forceinline__ bool grid_barrier(unsigned *gbar, unsigned target, unsigned *err, int *s_ok) {
+// Grid-wide barrier of the compute warps: one monotonically increasing
+// arrival counter (zeroed at launch).  Thread 0 of each CTA arrives with a
+// release add, then polls with acquire loads until all G CTAs of barrier
+// number `seq` have arrived.  Bounded (~2 s): on expiry sets the error flag
+// and returns false (the caller stops).
+__device__ __forceinline__ bool grid_barrier(unsigned *counter, unsigned seq, unsigned *err, int *s_ok) {
   csync();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(gbar, 1u);
+    const unsigned target = seq * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
     int ok = 1;
-    if (ld_acquire_u32(gbar) < target) {
-      const uint64_t t0 = globaltimer_ns();
-      for (uint32_t it = 0;; ++it) {
-        if (ld_acquire_u32(gbar) >= target) break;
-        if ((it & 255u) == 255u && globaltimer_ns() - t0 > 2000000000ull) {
-          atomicOr(err, kErrCounter);
-          ok = 0;
-          break;
-        }
+    const long long t0 = clock64();
+    for (uint32_t it = 0; ld_acquire_u32(counter) < target; ++it) {
+      if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+        atomicOr(err, kErrCounter);
+        ok = 0;
+        break;
       }
     }
-    __threadfence();
     *s_ok = ok;
   }
   csync();
@@ -168,6 +209,80 @@ __device__ __forceinline__ void build_q8k_global(const float *src, int cols, int
       });
     }
   }
+}
+
+// phase pi of a decode step: 0 = logits, then per layer qkv, attn, o-proj,
+// gate/up, down
+__device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
+  auto needs = [&]() {
+    ph.need_f32 = 0;
+    ph.need_q8k = 0;
+    for (int s = 0; s < ph.nseg; ++s) {
+      const int t = ph.seg[s].type;
+      if (t == T_Q5_0 || t == T_Q8_0) ph.need_f32 = 1;
+      if (t == T_Q4_K || t == T_Q6_K) ph.need_q8k = 1;
+    }
+  };
+  ph.x_in = nullptr;
+  ph.norm_w = nullptr;
+  ph.q_norm = ph.k_norm = nullptr;
+  ph.do_embed = ph.commit_here = 0;
+  ph.nseg = 0;
+  if (pi == 0) {
+    ph.kind = K_LOGITS;
+    ph.layer = -1;
+    ph.nseg = 1;
+    ph.cols = P.H;
+    ph.seg[0] = pseg(P.out_w, P.out_type, P.vocab, P.H, nullptr, P.logits);
+    ph.norm_w = P.out_norm;
+    needs();
+    return;
+  }
+  const int l = (pi - 1) / 5, r = (pi - 1) % 5;
+  const PLayer &L = P.layers[l];
+  ph.layer = l;
+  switch (r) {
+    case 0:
+      ph.kind = K_QKV;
+      ph.nseg = 3;
+      ph.cols = P.H;
+      ph.seg[0] = pseg(L.q, L.tq, P.H, P.H, L.qb, P.q);
+      ph.seg[1] = pseg(L.k, L.tk, P.kvd, P.H, L.kb, P.k);
+      ph.seg[2] = pseg(L.v, L.tv, P.kvd, P.H, L.vb, P.v);
+      ph.norm_w = L.attn_norm;
+      ph.do_embed = (l == 0);
+      break;
+    case 1:
+      ph.kind = K_ATTN;
+      ph.cols = 0;
+      ph.q_norm = L.qn;
+      ph.k_norm = L.kn;
+      break;
+    case 2:
+      ph.kind = K_OPROJ;
+      ph.nseg = 1;
+      ph.cols = P.H;
+      ph.seg[0] = pseg(L.o, L.to, P.H, P.H, nullptr, P.X);
+      ph.x_in = P.attn_out;
+      break;
+    case 3:
+      ph.kind = K_FFN_UP;
+      ph.nseg = 2;
+      ph.cols = P.H;
+      ph.seg[0] = pseg(L.gate, L.tg, P.F, P.H, nullptr, nullptr);
+      ph.seg[1] = pseg(L.up, L.tu, P.F, P.H, nullptr, nullptr);
+      ph.norm_w = L.ffn_norm;
+      break;
+    default:
+      ph.kind = K_FFN_DOWN;
+      ph.nseg = 1;
+      ph.cols = P.F;
+      ph.seg[0] = pseg(L.down, L.td, P.H, P.F, nullptr, P.X);
+      ph.x_in = P.h;
+      ph.commit_here = (l == P.n_layers - 1);
+      break;
+  }
+  needs();
 }
 
 // ---------------------------------------------------------------------------
@@ -368,7 +483,7 @@ __device__ void p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
 // one matvec phase on the compute warps; weights arrive through the ring
 // ---------------------------------------------------------------------------
 __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint32_t &k_ring, float (*red)[kWarps],
-                         float *scratch, int *s_flag) {
+                         float *scratch, int *s_flag, unsigned long long *tr) {
   const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
   DevState *st = P.st;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
@@ -393,6 +508,13 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   const int nbx = ph.cols / 32;
   // ---- input vector
   if (normed) {
+    // norm weights of this thread's elements, requested with the activation
+    float nwr[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int e = tid + k * kThreads;
+      nwr[k] = e < ph.cols ? __ldg(ph.norm_w + e) : 0.f;
+    }
     if (ph.kind == K_QKV && ph.do_embed) {
       int tok = ldst(&st->fwd_token);
       if (tok < 0 || tok >= st->vocab) tok = 0;  // engine/model.go:222-224
@@ -404,7 +526,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       load_vec_to_smem(xn, P.X, ph.cols);
       csync();
     }
-    // norm weights straight from L2 (tensor/ops.go:207-218)
+    // RMSNorm (tensor/ops.go:207-218); norm weights come from L2
     float ss0 = 0.f, ss1 = 0.f;
     int i = tid;
     for (; i + kThreads < ph.cols; i += 2 * kThreads) {
@@ -415,7 +537,11 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     const float ss = block_sum(ss0 + ss1, scratch);
     const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(ph.cols)), P.eps);
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(mean)));
-    for (int kk = tid; kk < ph.cols; kk += kThreads) xn[kk] = __fmul_rn(__fmul_rn(xn[kk], inv), __ldg(ph.norm_w + kk));
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int e = tid + k * kThreads;
+      if (e < ph.cols) xn[e] = __fmul_rn(__fmul_rn(xn[e], inv), nwr[k]);
+    }
     csync();
     if (ph.kind == K_LOGITS && c == 0)
       for (int kk = tid; kk < ph.cols; kk += kThreads) P.normx[kk] = xn[kk];
@@ -431,18 +557,21 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     if (ph.need_q8k) build_q8k_global(ph.x_in, ph.cols, q8qs, q8d, q8bs);
   }
   csync();
-  float xr[32];
+  XLimbs xl;
   const bool xreg = ph.need_f32 && nbx <= 32;
-  if (xreg) {
-    const int lane = tid & 31;
-#pragma unroll
-    for (int kk = 0; kk < 32; ++kk) xr[kk] = lane < nbx ? xt[kk * nbx + lane] : 0.f;
-  }
+  if (xreg) lane_limbs(xt, nbx, xl);
+  if (tr) tr[1] = globaltimer_ns();
   // ---- chunks from the ring
+  long long wait_cyc = 0;
+  const long long loop_t0 = tr ? clock64() : 0;
   for (int i = 0; i < nchunks; ++i, ++k_ring) {
     const int slot = static_cast<int>(k_ring % static_cast<uint32_t>(P.nslot));
     const uint32_t parity = (k_ring / static_cast<uint32_t>(P.nslot)) & 1u;
-    if (tid == 0) *s_flag = mbar_wait_bounded(&full[slot], parity, &st->err) ? 1 : 0;
+    if (tid == 0) {
+      const long long w0 = tr ? clock64() : 0;
+      *s_flag = mbar_wait_bounded(&full[slot], parity, &st->err) ? 1 : 0;
+      if (tr) wait_cyc += clock64() - w0;
+    }
     csync();
     if (!*s_flag) return false;
     const ChunkRef ch = phase_chunk_at(ph, my0, my1, i);
@@ -451,9 +580,14 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     const uint8_t *rows = smem + static_cast<size_t>(slot) * kStageAlloc + (src & 15);
     MatParams dummy{};
     compute_chunk(dummy, S, rows, ch.r1 - ch.r0, ch.r0, xt, nbx, q8,
-                  ybuf + ch.seg * P.yrows + (ch.r0 - my0[ch.seg]), red, xr, xreg);
+                  ybuf + ch.seg * P.yrows + (ch.r0 - my0[ch.seg]), red, xl, xreg);
     csync();
     if (tid == 0) mbar_arrive(&empty[slot]);
+  }
+  if (tr) {
+    tr[2] = globaltimer_ns();
+    tr[4] = static_cast<unsigned long long>(wait_cyc);
+    tr[6] = static_cast<unsigned long long>(clock64() - loop_t0);
   }
   // ---- epilogue
   if (ph.kind == K_QKV) {
@@ -481,14 +615,20 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   } else if (ph.kind == K_LOGITS) {
     const int n = my1[0] - my0[0];
     for (int r = tid; r < n; r += kThreads) P.logits[my0[0] + r] = ybuf[r];
+    // the penalty window's ids, fetched in parallel
+    __shared__ int win[kThreads];
+    const int wpos = ldst(&st->seq_len);
+    const int wlen = max(0, min(st->window, wpos));
+    if (tid < wlen) win[tid] = ldst(P.token_ids + wpos - wlen + tid);
     csync();
     if (tid == 0) {  // repetition penalty on this CTA's rows (c2slm.go:156-170)
-      const int pos = ldst(&st->seq_len);
+      const int pos = wpos;
       int start = pos - st->window;
       if (start < 0) start = 0;
       const float pen = st->penalty;
       for (int p = start; p < pos; ++p) {
-        const int tok = ldst(P.token_ids + p);
+        const int k = p - (pos - wlen);
+        const int tok = k < kThreads ? win[k] : ldst(P.token_ids + p);
         if (tok >= 0 && tok < st->vocab && tok != st->im_end && tok != st->eos && tok >= my0[0] && tok < my1[0]) {
           float &v = ybuf[tok - my0[0]];
           v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
@@ -534,17 +674,43 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       *s_flag = (t == static_cast<unsigned>(G - 1)) ? 1 : 0;
     }
     csync();
-    if (*s_flag && tid == 0) {
+    if (*s_flag) {  // the last CTA reduces the G partials (ties: lowest id)
       __threadfence();
       float best_v = -INFINITY;
       int best_i = 0x7fffffff;
-      for (int kk = 0; kk < G; ++kk) {
+      for (int kk = tid; kk < G; kk += kThreads) {
         const float2 pv = __ldcg(P.amax_part + kk);
         const int pi = __float_as_int(pv.y);
-        if (pi == 0x7fffffff) continue;
-        if (best_i == 0x7fffffff || pv.x > best_v || (pv.x == best_v && pi < best_i)) {
+        if (pi != 0x7fffffff && (pv.x > best_v || (pv.x == best_v && pi < best_i) || best_i == 0x7fffffff)) {
           best_v = pv.x;
           best_i = pi;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (oi != 0x7fffffff && (best_i == 0x7fffffff || ov > best_v || (ov == best_v && oi < best_i))) {
+          best_v = ov;
+          best_i = oi;
+        }
+      }
+      csync();
+      if ((tid & 31) == 0) {
+        red[0][tid >> 5] = best_v;
+        red[1][tid >> 5] = __int_as_float(best_i);
+      }
+      csync();
+    }
+    if (*s_flag && tid == 0) {
+      float best_v = red[0][0];
+      int best_i = __float_as_int(red[1][0]);
+      for (int w = 1; w < kWarps; ++w) {
+        const float v = red[0][w];
+        const int ix = __float_as_int(red[1][w]);
+        if (ix != 0x7fffffff && (best_i == 0x7fffffff || v > best_v || (v == best_v && ix < best_i))) {
+          best_v = v;
+          best_i = ix;
         }
       }
       if (best_i == 0x7fffffff) best_i = 0;
@@ -567,6 +733,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   __shared__ float scratch[kWarps];
   __shared__ int s_flag, s_ok;
   __shared__ volatile int s_stop;
+  __shared__ PPhase s_ph, s_pph;  // current phase: compute side / producer side
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + P.off_empty);
   uint64_t *abar = reinterpret_cast<uint64_t *>(smem + P.off_abar);
@@ -591,7 +758,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
     bool stopped = false;
     for (int step = 0; step < P.n_steps && !stopped; ++step) {
       for (int pi = 0; pi < P.nphase && !stopped; ++pi) {
-        const PPhase &ph = P.phases[pi];
+        build_phase(P, pi, s_pph);
+        const PPhase &ph = s_pph;
         if (ph.kind == K_ATTN) continue;
         int my0[kMaxSegs], my1[kMaxSegs];
         const int nch = phase_chunks(ph, c, G, my0, my1);
@@ -601,11 +769,11 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
           if (use > 0) {  // wait until the compute warps released the slot
             const uint32_t par = (use - 1) & 1u;
             bool ok = mbar_try_wait(&empty[slot], par);
-            const uint64_t t0 = globaltimer_ns();
+            const long long t0 = clock64();
             for (uint32_t it = 0; !ok; ++it) {
               if (s_stop) { stopped = true; break; }
               ok = mbar_try_wait(&empty[slot], par);
-              if (!ok && (it & 63u) == 63u && globaltimer_ns() - t0 > 2000000000ull) {
+              if (!ok && (it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
                 atomicOr(&st->err, kErrMbarTimeout);
                 stopped = true;
                 break;
@@ -621,9 +789,9 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
     // drain: wait (bounded) for the compute side to stop, then for every copy
     // issued but not consumed, before the CTA exits
     {
-      const uint64_t t0 = globaltimer_ns();
+      const long long t0 = clock64();
       for (uint32_t it = 0; !s_stop; ++it)
-        if ((it & 255u) == 255u && globaltimer_ns() - t0 > 4000000000ull) {
+        if ((it & 255u) == 255u && clock64() - t0 > 2 * kSpinCycles) {
           atomicOr(&st->err, kErrMbarTimeout);
           break;
         }
@@ -642,23 +810,32 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   bool ok = true;
   for (int step = 0; step < P.n_steps && ok; ++step) {
     for (int pi = 0; pi < P.nphase && ok; ++pi) {
-      const PPhase &ph = P.phases[pi];
+      if (tid == 0) build_phase(P, pi, s_ph);
+      csync();
+      const PPhase &ph = s_ph;
+      const long long b0 = P.trace ? clock64() : 0;
       if (step > 0 || pi > 0) {
-        bar_target += G;
+        bar_target += 1;
         if (!grid_barrier(P.gbar, bar_target, &st->err, &s_ok)) { ok = false; break; }
       }
       if (pi == 0 && ldst(&st->halted)) { ok = false; break; }
-      unsigned long long *tr = (P.trace && c < 4 && tid == 0)
-                                   ? P.trace + ((static_cast<size_t>(step) * P.nphase + pi) * 4 + c) * 2
-                                   : nullptr;
-      if (tr) tr[0] = globaltimer_ns();
+      unsigned long long *tr =
+          (P.trace && tid == 0)
+              ? P.trace + ((static_cast<size_t>(step) * P.nphase + pi) * G + c) * kTraceFields
+              : nullptr;
+      if (tr) {
+        const long long b1 = clock64();
+        tr[0] = globaltimer_ns();
+        tr[5] = static_cast<unsigned long long>(b1 - b0);
+        tr[7] = static_cast<unsigned long long>(b1);
+      }
       if (ph.kind == K_ATTN) {
         p_attention(P, ph, reinterpret_cast<float *>(smem + P.off_act), abar, abar_uses, c);
       } else {
-        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag)) { ok = false; break; }
+        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag, tr)) { ok = false; break; }
       }
       csync();
-      if (tr) tr[1] = globaltimer_ns();
+      if (tr) tr[3] = globaltimer_ns();
       // bench rewind: the down phase of the last layer set SeqLen = pos + 1
       if (ph.kind == K_FFN_DOWN && ph.commit_here && P.rewind_period > 0 && c == 0 && tid == 0 &&
           (step + 1) % P.rewind_period == 0)

@@ -370,13 +370,17 @@ class Engine:
         _check(load_library().c2s_profile_step(self._h, n_steps, penalty, window, _ptr(ms), _ptr(cnt)))
         return {name: {"ms": float(ms[k]), "launches": int(cnt[k])} for k, name in self.STAGES.items()}
 
-    def trace_decode(self, n_steps: int, penalty: float = 1.15, window: int = 64) -> np.ndarray:
-        """Per-phase start/end stamps (ns) of the persistent decode kernel for
-        CTAs 0..3: array [n_steps, nphase, 4, 2]."""
+    def trace_decode(self, n_steps: int, penalty: float = 1.15, window: int = 64, n_sms: int | None = None):
+        """Per-phase stamps (ns) of the persistent decode kernel for every CTA:
+        array [n_steps, nphase, n_sms, 8]: ns stamps (start, inputs ready,
+        chunks done, end), then SM cycles (weight waits, grid barrier, chunk
+        loop, cycle counter at start)."""
+        import torch
+        n_sms = n_sms or torch.cuda.get_device_properties(self.device).multi_processor_count
         nph = C.c_int(0)
-        buf = np.zeros(n_steps * 4 * 2 * (5 * self.desc.n_layers + 1), np.uint64)
+        buf = np.zeros(n_steps * n_sms * 8 * (5 * self.desc.n_layers + 1), np.uint64)
         _check(load_library().c2s_trace_decode(self._h, n_steps, penalty, window, _ptr(buf), C.byref(nph)))
-        return buf.reshape(n_steps, nph.value, 4, 2)
+        return buf.reshape(n_steps, nph.value, n_sms, 8)
 
     @property
     def kernels_per_step(self) -> int:

@@ -154,9 +154,13 @@ int c2s_bench_decode_timed(c2s_engine *e, int n_steps, float penalty, int window
 int c2s_profile_step(c2s_engine *e, int n_steps, float penalty, int window, float *stage_ms,
                      int *stage_launches);
 /* Phase trace of the persistent decode kernel: runs n_steps decode steps and
- * returns %globaltimer stamps [step][phase][cta 0..3][start, end] (ns) in
- * trace_out (n_steps * nphase * 8 values); *nphase_out = phases per step
- * (1 logits phase, then 5 per layer: qkv, attention, o-proj, gate/up, down). */
+ * returns 8 values per [step][phase][cta] in trace_out (n_steps * nphase *
+ * n_sms * 8 values): %globaltimer ns at phase start (after the grid barrier),
+ * inputs ready, chunks done and end; then SM cycles spent waiting for weight
+ * chunks, in the grid barrier before the phase, in the chunk loop, and the
+ * cycle counter at phase start.  Values 1, 2, 4 and 6 are 0 for attention
+ * phases.  *nphase_out = phases per step (1 logits phase, then 5 per layer:
+ * qkv, attention, o-proj, gate/up, down). */
 int c2s_trace_decode(c2s_engine *e, int n_steps, float penalty, int window, uint64_t *trace_out,
                      int *nphase_out);
 /* Number of kernels one decode step launches (for the bench's launch count). */
