@@ -12,7 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libc2slm_b200.so")
 SOURCES = [os.path.join(HERE, "csrc", "c2s_engine.cu")]
-DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in ("c2s_device.cuh", "c2s_kernels.cuh", "c2s_persistent.cuh")] + \
+DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in ("c2s_device.cuh", "c2s_rows.cuh", "c2s_kernels.cuh", "c2s_persistent.cuh")] + \
     [os.path.join(ROOT, "include", "c2slm_b200.h")]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

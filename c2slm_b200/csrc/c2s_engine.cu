@@ -66,6 +66,7 @@ int check_matrix(int type, int64_t rows, int64_t cols, const char *what) {
   if (!(is_kquant(type) || is_f32x(type)))
     return fail(C2S_ERR_UNSUPPORTED, "%s: GGML type %d is not a supported matrix type", what, type);
   if (rows <= 0 || cols <= 0) return fail(C2S_ERR_ARG, "%s: bad shape %lld x %lld", what, (long long)rows, (long long)cols);
+  if (rows > (1 << 24)) return fail(C2S_ERR_UNSUPPORTED, "%s: more than 2^24 rows", what);  // 32-bit row split
   if (is_kquant(type) && cols % 256) return fail(C2S_ERR_UNSUPPORTED, "%s: K-quant needs cols %% 256 == 0 (cols=%lld)", what, (long long)cols);
   if (is_f32x(type) && cols % 32) return fail(C2S_ERR_UNSUPPORTED, "%s: cols %% 32 != 0", what);
   if (row_bytes_of(type, cols) > static_cast<size_t>(kStageBytes))
@@ -118,12 +119,12 @@ void layout_matvec(MatParams &P, int grid) {
   if (bias) off += a16(static_cast<size_t>(P.nseg) * yr * 4);
   P.off_xn = static_cast<int>(off);
   off += a16(static_cast<size_t>(P.cols) * 4);
-  P.off_xt = static_cast<int>(off);
-  if (P.need_f32) off += a16(static_cast<size_t>(P.cols) * 4);
+  P.off_xt = static_cast<int>(off);  // limbs of the f32 activation (25 words per 32-value block)
+  if (P.need_f32) off += a16(static_cast<size_t>(P.cols / 32) * 25 * 4);
   P.off_q8 = static_cast<int>(off);
   if (P.need_q8k) {
     const int nsb = P.cols / 256;
-    off += a16(static_cast<size_t>(q8_qs_bytes(P.cols)) + 4 * nsb + 64 * nsb);
+    off += a16(static_cast<size_t>(q8_qs_bytes(P.cols))) + a16(4 * static_cast<size_t>(nsb)) + 64 * nsb;
   }
   P.off_y = static_cast<int>(off);
   off += static_cast<size_t>(std::max(P.nseg, 1)) * yr * 4;
@@ -368,7 +369,7 @@ struct c2s_engine {
   DevState *h_st = nullptr;
   int *h_tokens = nullptr;
   int host_seq = 0;
-  int max_splits = 1, chunk_cap = 32;
+  int max_splits = 1, split_len = 256;
   size_t attn_smem = 0;
   int kernels_per_step = 0;
   cudaGraphExec_t g_forward = nullptr, g_step = nullptr, g_logits = nullptr, g_fwd_select = nullptr;
@@ -487,7 +488,7 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     A.out = e->attn_out;
     A.st = e->st;
     A.check_halt = check_halt;
-    A.chunk_cap = e->chunk_cap;
+    A.split_len = e->split_len;
     if ((err = mark(tm, s, -1))) break;
     err = launch(k_attention, dim3(e->d.n_kv_heads, e->max_splits), dim3(kThreads), e->attn_smem, s, A);
     if (err || (err = mark(tm, s, 7))) break;
@@ -690,7 +691,7 @@ int persistent_setup(c2s_engine *e) {
   // shared memory: weight ring | mbarriers | activation region (union of the
   // matvec and attention working sets)
   auto a16 = [](size_t v) { return (v + 15) & ~size_t(15); };
-  int xn_cap = H, xt_cap = 0, q8_cap = 0, yrows = 1;
+  int limb_cap = 0, q8_cap = 0, yrows = 1;
   for (auto &p : ph) {
     if (p.kind == K_ATTN) continue;
     for (int s = 0; s < p.nseg; ++s) {
@@ -699,30 +700,42 @@ int persistent_setup(c2s_engine *e) {
       if (p.kind != K_LOGITS && per > kThreads)
         return fail(C2S_ERR_UNSUPPORTED, "persistent decode: more than %d rows per CTA", kThreads);
     }
-    if (p.need_f32) {
-      xt_cap = std::max(xt_cap, p.cols);
-      xn_cap = std::max(xn_cap, p.cols);
-    }
+    if (p.need_f32) limb_cap = std::max(limb_cap, p.cols);
     if (p.need_q8k) q8_cap = std::max(q8_cap, p.cols);
   }
   PParams &P = e->pp;
-  P.off_xn = 0;
-  P.off_xt = static_cast<int>(a16(static_cast<size_t>(xn_cap) * 4));
-  P.off_q8 = P.off_xt + static_cast<int>(a16(static_cast<size_t>(xt_cap) * 4));
-  const size_t q8b = q8_cap ? a16(static_cast<size_t>(q8_qs_bytes(q8_cap)) + 4 * (q8_cap / 256) + 64 * (q8_cap / 256)) : 0;
-  P.off_y = P.off_q8 + static_cast<int>(q8b);
+  P.off_xn = 0;  // f32 input vector (embedding row, normalised x for Q8_K)
+  P.off_limbs = static_cast<int>(a16(static_cast<size_t>(H) * 4));
+  P.off_q8 = P.off_limbs + static_cast<int>(a16(static_cast<size_t>(limb_cap / 32) * 25 * 4));
+  const size_t q8b = q8_cap ? a16(static_cast<size_t>(q8_qs_bytes(q8_cap))) + a16(4 * static_cast<size_t>(q8_cap / 256)) +
+                                  64 * static_cast<size_t>(q8_cap / 256)
+                            : 0;
+  P.off_y = P.off_q8 + static_cast<int>(a16(q8b));
   P.yrows = yrows;
   const size_t mv_act = static_cast<size_t>(P.off_y) + static_cast<size_t>(kMaxSegs) * yrows * 4;
   const int qpk = d.n_heads / d.n_kv_heads, SUB = attn_sub(hd);
   const size_t at_act = (static_cast<size_t>(4) * SUB * hd + 2 * static_cast<size_t>(qpk) * hd + 2 * hd +
                          static_cast<size_t>(qpk) * SUB) * 4;
   const size_t act = a16(std::max(mv_act, at_act));
-  const size_t budget = 227 * 1024 - 2048;  // dynamic smem; static smem of the kernel is < 2 KB
-  int nslot = static_cast<int>((budget - act - 64 * 8) / kStageAlloc);
-  nslot = std::min(nslot, 12);
+  const size_t budget = 227 * 1024 - 4096;  // dynamic smem; static smem of the kernel is < 4 KB
+  // weight ring: a few large slots (each warp consumes many rows per slot)
+  int slot_kb = 48;
+  if (const char *sk = getenv("C2S_SLOT_KB")) slot_kb = std::max(8, std::min(96, atoi(sk)));
+  size_t max_row = 0;
+  for (auto &p : ph)
+    for (int s = 0; s < p.nseg; ++s) max_row = std::max(max_row, static_cast<size_t>(p.seg[s].row_bytes));
+  if (budget < act + 1024) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: activation set too large for shared memory");
+  const size_t ring = budget - act - 1024;
+  size_t slot_bytes = static_cast<size_t>(slot_kb) * 1024;
+  while (slot_bytes > 16384 && ring / (slot_bytes + 64) < 3) slot_bytes -= 8192;
+  if (slot_bytes < max_row) slot_bytes = (max_row + 1023) & ~size_t(1023);
+  int nslot = static_cast<int>(ring / (slot_bytes + 64));
+  nslot = std::min(nslot, 8);
   if (nslot < 2) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: activation set too large for shared memory");
   P.nslot = nslot;
-  size_t off = static_cast<size_t>(nslot) * kStageAlloc;
+  P.slot_bytes = static_cast<int>(slot_bytes);
+  P.slot_alloc = static_cast<int>(slot_bytes + 64);
+  size_t off = static_cast<size_t>(nslot) * P.slot_alloc;
   P.off_full = static_cast<int>(off);
   off += 8 * nslot;
   P.off_empty = static_cast<int>(off);
@@ -763,6 +776,7 @@ int persistent_setup(c2s_engine *e) {
   P.hd = hd;
   P.max_tokens = d.max_tokens;
   P.max_splits = e->max_splits;
+  P.split_len = e->split_len;
   P.rope_len = kMaxContext;
   P.eps = d.eps;
   P.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
@@ -948,9 +962,10 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   if (cudaMalloc(&e->kv, kvn * 4) != cudaSuccess) return fail(C2S_ERR_OOM, "KV cache: cudaMalloc(%zu) failed", kvn * 4);
   CK(cudaMemset(e->kv, 0, kvn * 4));
   e->max_splits = std::max(1, std::min(kMaxSplits, e->num_sms / d.n_kv_heads));
-  // largest split over n <= max_tokens: <= kMinSplitLen while the split count
-  // grows, ceil(n / max_splits) once it saturates
-  e->chunk_cap = std::max(kMinSplitLen, (d.max_tokens + e->max_splits - 1) / e->max_splits);
+  // positions per attention split, fixed for the engine so that position p
+  // always belongs to split p / split_len: at least 64 KB of K per split, and
+  // few enough splits for max_tokens
+  e->split_len = std::max(16384 / hd, (d.max_tokens + e->max_splits - 1) / e->max_splits);
   const int qpk = d.n_heads / d.n_kv_heads;
   if (qpk > 8) return fail(C2S_ERR_UNSUPPORTED, "more than 8 query heads per kv head");
   if (hd != 64 && hd != 128) return fail(C2S_ERR_UNSUPPORTED, "head_dim must be 64 or 128");

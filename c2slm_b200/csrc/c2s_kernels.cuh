@@ -9,7 +9,7 @@
 // launch).  Activations are tiny (<= 76 KB) and are re-read from L2 by every
 // CTA after the wait.
 #pragma once
-#include "c2s_device.cuh"
+#include "c2s_rows.cuh"
 
 namespace c2s {
 
@@ -61,9 +61,11 @@ struct MatParams {
   int check_halt;      // engine kernels honour DevState::halted
 };
 
+// rows [r0, r1) of CTA c of G (32-bit: (c + 1) * rows < 2^32 for every
+// matrix the engine accepts)
 __device__ __forceinline__ void seg_rows(int rows, int c, int G, int &r0, int &r1) {
-  r0 = static_cast<int>((static_cast<long long>(c) * rows) / G);
-  r1 = static_cast<int>((static_cast<long long>(c + 1) * rows) / G);
+  r0 = static_cast<int>((static_cast<unsigned>(c) * static_cast<unsigned>(rows)) / static_cast<unsigned>(G));
+  r1 = static_cast<int>((static_cast<unsigned>(c + 1) * static_cast<unsigned>(rows)) / static_cast<unsigned>(G));
 }
 
 struct ChunkRef {
@@ -142,48 +144,6 @@ __device__ __forceinline__ float blockdot_q5_0_reg(const uint8_t *blk, const flo
     a3 = fmaf(byte_as_f(hi, 3) - 8388624.0f, xr[16 + 4 * t + 3], a3);
   }
   return d * ((a0 + a1) + (a2 + a3));
-}
-
-// ---------------------------------------------------------------------------
-// f32 activation of one 32-value block split into three int8 limbs:
-//   x = s * (a + b/254 + c/254^2),  s = max|x|/127,  a, b, c in [-127, 127]
-// (reconstruction error <= ~6.2e-8 * max|x|).  A Q8_0 / Q5_0 block dot is
-// then three int8 dp4a chains and one f32 combine.
-// ---------------------------------------------------------------------------
-struct XLimbs {
-  int a[8], b[8], c[8];
-  float s;
-};
-
-__device__ __forceinline__ void make_limbs(const float (&x)[32], XLimbs &L) {
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[i]));
-  L.s = amax / 127.f;
-  const float inv = amax > 0.f ? 127.f / amax : 0.f;
-#pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    uint32_t wa = 0, wb = 0, wc = 0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float y = x[4 * t + e] * inv;
-      const float a = rintf(y);
-      const float r1 = __fmul_rn(y - a, 254.f);
-      const float b = rintf(r1);
-      const float c = rintf(__fmul_rn(r1 - b, 254.f));
-      wa |= (static_cast<uint32_t>(static_cast<int>(a)) & 0xFFu) << (8 * e);
-      wb |= (static_cast<uint32_t>(static_cast<int>(b)) & 0xFFu) << (8 * e);
-      wc |= (static_cast<uint32_t>(static_cast<int>(c)) & 0xFFu) << (8 * e);
-    }
-    L.a[t] = static_cast<int>(wa);
-    L.b[t] = static_cast<int>(wb);
-    L.c[t] = static_cast<int>(wc);
-  }
-}
-
-__device__ __forceinline__ float limbs_combine(int A, int B, int C, float s) {
-  const float k = 1.f / 254.f;
-  return s * fmaf(fmaf(static_cast<float>(C), k, static_cast<float>(B)), k, static_cast<float>(A));
 }
 
 // Q8_0 block (int8 weights) . limb-split x
@@ -388,15 +348,19 @@ __device__ __forceinline__ void load_const_to_smem(float *dst, const float *src,
 
 // RMSNorm of a shared-memory vector in place (tensor/ops.go:207-218):
 // inv = float32(1/sqrt(float64(sumsq/n + eps))); out = (x*inv)*w, w in smem.
+// Sum of squares: thread t accumulates float4 t, t + kThreads, ... in order
+// (x, y, z, w), then a fixed block tree -- the persistent kernel's prologue
+// sums in the same order.
 __device__ __forceinline__ void rmsnorm_smem(float *x, const float *w, int n, float eps, float *scratch) {
-  float ss0 = 0.f, ss1 = 0.f;
-  int i = threadIdx.x;
-  for (; i + kThreads < n; i += 2 * kThreads) {
-    ss0 = fmaf(x[i], x[i], ss0);
-    ss1 = fmaf(x[i + kThreads], x[i + kThreads], ss1);
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < (n >> 2); i += kThreads) {
+    const float4 v = reinterpret_cast<const float4 *>(x)[i];
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
   }
-  if (i < n) ss0 = fmaf(x[i], x[i], ss0);
-  const float ss = block_sum(ss0 + ss1, scratch);
+  ss = block_sum(ss, scratch);
   const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(n)), eps);
   const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(mean)));
   for (int k = threadIdx.x; k < n; k += kThreads) x[k] = __fmul_rn(__fmul_rn(x[k], inv), w[k]);
@@ -483,15 +447,18 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
   if (residual && my0[0] + tid < my1[0]) xres = __ldcg(P.X + my0[0] + tid);
 
   float *xn = reinterpret_cast<float *>(smem + P.off_xn);
-  float *xt = reinterpret_cast<float *>(smem + P.off_xt);
+  const int nbx = P.cols / 32;
+  int *la = reinterpret_cast<int *>(smem + P.off_xt);
+  int *lb = la + 8 * nbx, *lc = lb + 8 * nbx;
+  float *ls = reinterpret_cast<float *>(lc + 8 * nbx);
+  const LimbsView LV{la, lb, lc, ls, nbx};
   Q8KView q8{};
   int8_t *q8qs = reinterpret_cast<int8_t *>(smem + P.off_q8);
   float *q8d = reinterpret_cast<float *>(smem + P.off_q8 + q8_qs_bytes(P.cols));
-  int32_t *q8bs = reinterpret_cast<int32_t *>(smem + P.off_q8 + q8_qs_bytes(P.cols) + 4 * (P.cols / 256));
+  int32_t *q8bs = reinterpret_cast<int32_t *>(smem + P.off_q8 + q8_qs_bytes(P.cols) + ((4 * (P.cols / 256) + 15) & ~15));
   q8.qs = q8qs;
   q8.d = q8d;
   q8.bsum = q8bs;
-  const int nbx = P.cols / 32;
 
   // ---- input vector
   if (normed) {
@@ -513,14 +480,16 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
     load_vec_to_smem(xn, P.x_in, P.cols);
     __syncthreads();
   }
-  if (P.need_f32)
-    for (int i = tid; i < P.cols; i += kThreads) xt[(i & 31) * nbx + (i >> 5)] = xn[i];
+  if (P.need_f32) {  // int8 limbs of x, from the float4 each thread reads
+    const int n4 = P.cols >> 2;
+    for (int i0 = 0; i0 < n4; i0 += kThreads) {
+      const int i = i0 + tid;
+      const float4 v = i < n4 ? reinterpret_cast<const float4 *>(xn)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      put_limbs(v, i, i < n4, la, lb, lc, ls, nbx);
+    }
+  }
   if (P.need_q8k) build_q8k(xn, P.cols, q8qs, q8d, q8bs);
   __syncthreads();
-  // this lane's block of x as int8 limbs in registers (rows of <= 32 blocks)
-  XLimbs xl;
-  const bool xreg = P.need_f32 && nbx <= 32;
-  if (xreg) lane_limbs(xt, nbx, xl);
 
   // ---- stream the chunks
   float *ybuf = reinterpret_cast<float *>(smem + P.off_y);
@@ -540,8 +509,21 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
     {
       const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
       const uint8_t *rows = smem + sidx * kStageAlloc + (src & 15);
-      compute_chunk(P, S, rows, ch.r1 - ch.r0, ch.r0, xt, nbx, q8,
-                    ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]), red, xl, xreg);
+      float *y = ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]);
+      const int nr = ch.r1 - ch.r0, warp = tid >> 5;
+      if (P.dbg) {  // integer partials of the K-quant dots (bit-exact contract)
+        XLimbs none{};
+        compute_chunk(P, S, rows, nr, ch.r0, nullptr, nbx, q8, y, red, none, false);
+      } else if (warp < nr) {
+        const int cnt = (nr - warp + kWarps - 1) / kWarps;
+        switch (S.type) {
+          case T_Q8_0: warp_rows<T_Q8_0>(rows, S.row_bytes, S.units, warp, cnt, LV, q8, y); break;
+          case T_Q5_0: warp_rows<T_Q5_0>(rows, S.row_bytes, S.units, warp, cnt, LV, q8, y); break;
+          case T_Q4_K: warp_rows<T_Q4_K>(rows, S.row_bytes, S.units, warp, cnt, LV, q8, y); break;
+          case T_Q6_K: warp_rows<T_Q6_K>(rows, S.row_bytes, S.units, warp, cnt, LV, q8, y); break;
+          default: break;
+        }
+      }
     }
     __syncthreads();
     if (tid == 0 && i + kStages < nchunks)
@@ -687,18 +669,8 @@ struct AttnParams {
   float *out;   // [n_heads * hd]
   DevState *st;
   int check_halt;
-  int chunk_cap;  // positions per split the shared memory was sized for
+  int split_len;  // positions per split: position p is always in split p / split_len
 };
-
-__device__ __forceinline__ void rope_rotate(float *v, int hd, const float *cs, const float *sn, int tid, int nthr) {
-  const int half = hd / 2;
-  for (int i = tid; i < half; i += nthr) {
-    const float x0 = v[i], x1 = v[i + half];
-    const float c = cs[i], s = sn[i];
-    v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-    v[i + half] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-  }
-}
 
 __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int hd, float eps) {
   const int lane = threadIdx.x & 31;
@@ -712,144 +684,149 @@ __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int 
   __syncwarp();
 }
 
-__host__ __device__ inline int attn_nsplit(int n, int max_splits) {
-  int ns = (n + kMinSplitLen - 1) / kMinSplitLen;
-  return ns > max_splits ? max_splits : ns;
-}
-
-// positions per staged sub-chunk: K and V tiles of 16 KB each
 __host__ __device__ inline int attn_sub(int hd) { return 4096 / hd; }
 
-__global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
-  extern __shared__ __align__(128) float asmem[];
-  __shared__ __align__(8) uint64_t bars[2];
-  __shared__ int s_last;
-  __shared__ float s_m[8], s_l[8], s_scale[8];
+// Scores of positions a .. a+len-1 for the qpk (<= 8) heads of a group: one
+// warp per position, lane l holds d = l*E .. l*E+E-1 of q and k.
+template <int E>
+__device__ __forceinline__ void attn_scores(const float *qs, const float *knew, const float *kb, int a, int len,
+                                            int pos, int qpk, float scale, float *sc, int SUB) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, hd = 32 * E;
+  float qr[8][E];
+#pragma unroll
+  for (int h = 0; h < 8; ++h)
+#pragma unroll
+    for (int j = 0; j < E; ++j) qr[h][j] = h < qpk ? qs[h * hd + lane * E + j] : 0.f;
+  for (int t = warp; t < len; t += kWarps) {
+    const float *kp = (a + t == pos) ? knew : kb + t * hd;
+    float kv[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) kv[j] = kp[lane * E + j];
+    float dot[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+      float d0 = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
+      dot[h] = d0;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int h = 0; h < 8; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
+    if (lane < qpk) {
+      float v = dot[0];
+#pragma unroll
+      for (int h = 1; h < 8; ++h) v = (lane == h) ? dot[h] : v;
+      sc[lane * SUB + t] = __fmul_rn(v, scale);
+    }
+  }
+}
+
+// One attention work item: kv head g, split s of the positions [0, pos]
+// (decode of one token at pos).  Shared by the per-phase kernel and the
+// persistent kernel, so both evaluate the same float operations in the same
+// order.
+struct AttnJob {
+  const float *q, *k, *v;          // projections of this token (bias added)
+  const float *q_norm, *k_norm;    // Qwen3 per-head norms, or null
+  float *kc, *vc;                  // cache planes of this layer and kv head: row p at [p * hd]
+  const float *rope_cs, *rope_sn;  // RoPE row of pos (hd/2 each), or null outside the table
+  float *out, *part;
+  unsigned *counter;               // arrivals of the group's splits (last one combines)
+  int g, s, nsplit, p0, p1, pos;
+  int hd, qpk, max_splits;
+  float eps, scale;
+};
+
+// Shared memory: asmem holds [2][SUB][hd] K, [2][SUB][hd] V, [qpk][hd] q,
+// [hd] k, [hd] v, [qpk][SUB] scores, [qpk][hd] accumulators.  bars[2] are the
+// staging barriers; uses[2] counts their completed phases (kept by the
+// caller across items).  Returns false if a bounded wait expired.
+__device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[2], unsigned *err) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_trigger();
-  pdl_wait();
-  DevState *st = A.st;
-  if (A.check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
-  const int g = blockIdx.x, s = blockIdx.y;
-  const int hd = A.hd, qpk = A.n_heads / A.n_kv, SUB = attn_sub(hd);
-  const int pos = st->fwd_pos;
-  if (pos < 0 || pos >= A.max_tokens) {
-    if (tid == 0 && s == 0 && g == 0) atomicOr(&st->err, kErrPos);
-    return;
-  }
-  const int n = pos + 1;
-  const int nsplit = attn_nsplit(n, A.max_splits);
-  const int chunk = (n + nsplit - 1) / nsplit;
-  if (s >= nsplit) return;
-  const int p0 = min(n, s * chunk), p1 = min(n, p0 + chunk);
-
-  // KV layout [L][KVH][max_tokens][hd] per plane (engine/kvcache.go:127-140)
-  const size_t head_stride = static_cast<size_t>(A.max_tokens) * hd;
-  const size_t layer_stride = static_cast<size_t>(A.n_kv) * head_stride;
-  float *kc = A.kcache + static_cast<size_t>(A.layer) * layer_stride + g * head_stride;
-  float *vc = A.vcache + static_cast<size_t>(A.layer) * layer_stride + g * head_stride;
-
-  float *kbuf = asmem;                        // [2][SUB][hd]
-  float *vbuf = kbuf + 2 * SUB * hd;          // [2][SUB][hd]
-  float *qs = vbuf + 2 * SUB * hd;            // [qpk][hd]
-  float *knew = qs + qpk * hd;                // [hd]
-  float *vnew = knew + hd;                    // [hd]
-  float *sc = vnew + hd;                      // [qpk][SUB]
-  float *acc = sc + qpk * SUB;                // [qpk][hd]
-
-  // stage the cached rows of sub-chunk it into buffer it&1 (positions < pos)
-  auto issue = [&](int it) {
+  const int hd = J.hd, qpk = J.qpk, SUB = attn_sub(hd), pos = J.pos, p0 = J.p0, p1 = J.p1;
+  float *kbuf = asmem, *vbuf = kbuf + 2 * SUB * hd, *qs = vbuf + 2 * SUB * hd;
+  float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd, *acc = sc + qpk * SUB;
+  __shared__ float s_m[8], s_l[8], s_scale[8];
+  __shared__ int s_last;
+  const int n_sub = (p1 - p0 + SUB - 1) / SUB;
+  // stage the cached rows (positions < pos) of sub-chunk it into buffer it&1
+  auto cached_rows = [&](int it) {
     const int a = p0 + it * SUB, b = min(p1, a + SUB);
-    const int cached = max(0, min(b, pos) - a);
+    return max(0, min(b, pos) - a);
+  };
+  auto issue = [&](int it) {
+    const int cached = cached_rows(it);
     if (cached > 0) {
+      const int a = p0 + it * SUB;
       const uint32_t bytes = static_cast<uint32_t>(cached) * hd * 4;
       uint64_t *bar = &bars[it & 1];
       mbar_arrive_expect_tx(bar, 2 * bytes);
-      bulk_g2s(kbuf + (it & 1) * SUB * hd, kc + static_cast<size_t>(a) * hd, bytes, bar);
-      bulk_g2s(vbuf + (it & 1) * SUB * hd, vc + static_cast<size_t>(a) * hd, bytes, bar);
+      bulk_g2s(kbuf + (it & 1) * SUB * hd, J.kc + static_cast<size_t>(a) * hd, bytes, bar);
+      bulk_g2s(vbuf + (it & 1) * SUB * hd, J.vc + static_cast<size_t>(a) * hd, bytes, bar);
     }
   };
-  const int n_sub = (p1 - p0 + SUB - 1) / SUB;
   if (tid == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // cache rows stored earlier by this CTA
     issue(0);
     if (n_sub > 1) issue(1);
   }
-  // projections (bias already added by the QKV kernel), QK-norm, RoPE
-  for (int i = tid; i < qpk * hd; i += kThreads) qs[i] = __ldcg(A.q + g * qpk * hd + i);
-  for (int i = tid; i < hd; i += kThreads) {
-    knew[i] = __ldcg(A.k + g * hd + i);
-    vnew[i] = __ldcg(A.v + g * hd + i);
+  // projections: every load in flight at once
+  for (int i = tid; i < qpk * hd; i += kThreads) {
+    qs[i] = __ldcg(J.q + i);
+    acc[i] = 0.f;
   }
-  for (int i = tid; i < qpk * hd; i += kThreads) acc[i] = 0.f;
+  for (int i = tid; i < hd; i += kThreads) {
+    knew[i] = __ldcg(J.k + i);
+    vnew[i] = __ldcg(J.v + i);
+  }
   if (tid < 8) {
     s_m[tid] = -INFINITY;
     s_l[tid] = 0.f;
   }
-  __syncthreads();
-  if (A.q_norm)  // Qwen3 per-head QK-norm (engine/forward.go:80-91)
-    for (int h = warp; h < qpk; h += kWarps) head_rmsnorm_warp(qs + h * hd, A.q_norm, hd, A.eps);
-  if (A.k_norm && warp == kWarps - 1) head_rmsnorm_warp(knew, A.k_norm, hd, A.eps);
-  __syncthreads();
-  if (pos < A.rope_len) {  // RoPETable.Apply rejects pos outside the table (tensor/ops.go:263)
-    const float *cs = A.rope_cos + static_cast<size_t>(pos) * (hd / 2);
-    const float *sn = A.rope_sin + static_cast<size_t>(pos) * (hd / 2);
-    for (int h = 0; h < qpk; ++h) rope_rotate(qs + h * hd, hd, cs, sn, tid, kThreads);
-    rope_rotate(knew, hd, cs, sn, tid, kThreads);
+  csync();
+  if (J.q_norm || J.k_norm) {  // Qwen3 per-head QK-norm (engine/forward.go:80-91)
+    if (J.q_norm)
+      for (int h = warp; h < qpk; h += kWarps) head_rmsnorm_warp(qs + h * hd, J.q_norm, hd, J.eps);
+    if (J.k_norm && warp == kWarps - 1) head_rmsnorm_warp(knew, J.k_norm, hd, J.eps);
+    csync();
   }
-  __syncthreads();
-  if (pos >= p0 && pos < p1)  // KVCache.StoreKV (engine/kvcache.go:143-158)
-    for (int i = tid; i < hd; i += kThreads) {
-      kc[static_cast<size_t>(pos) * hd + i] = knew[i];
-      vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
+  if (J.rope_cs) {  // NeoX RoPE of every q head and k: one thread per (head, pair)
+    const int half = hd / 2;
+    for (int t = tid; t < (qpk + 1) * half; t += kThreads) {
+      const int h = t / half, i = t - h * half;
+      float *v = h < qpk ? qs + h * hd : knew;
+      const float x0 = v[i], x1 = v[i + half];
+      const float c = J.rope_cs[i], sn = J.rope_sn[i];
+      v[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+      v[i + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
     }
-  // q of every head of the group in registers: lane holds d = lane*E .. +E-1
-  const int E = hd / 32;  // 2 (hd 64) or 4 (hd 128)
-  float qr[8][4];
-#pragma unroll
-  for (int h = 0; h < 8; ++h)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) qr[h][j] = (h < qpk && j < E) ? qs[h * hd + lane * E + j] : 0.f;
-
-  bool ok_all = true;
+    csync();
+  }
+  if (pos >= p0 && pos < p1) {  // KVCache.StoreKV (engine/kvcache.go:143-158)
+    for (int i = tid; i < hd; i += kThreads) {
+      J.kc[static_cast<size_t>(pos) * hd + i] = knew[i];
+      J.vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // later staged reads of this row see it
+  }
+  bool ok = true;
   for (int it = 0; it < n_sub; ++it) {
     const int a = p0 + it * SUB, b = min(p1, a + SUB), len = b - a;
-    const int cached = max(0, min(b, pos) - a);
-    if (cached > 0) ok_all = mbar_wait_bounded(&bars[it & 1], (it >> 1) & 1, &st->err) && ok_all;
+    if (cached_rows(it) > 0) {  // completions of a buffer's barrier alternate parity
+      ok = mbar_wait_bounded(&bars[it & 1], uses[it & 1] & 1u, err) && ok;
+      uses[it & 1] += 1;
+    }
     const float *kb = kbuf + (it & 1) * SUB * hd;
     const float *vb = vbuf + (it & 1) * SUB * hd;
-    // scores: one warp per position, lanes over d
-    for (int t = warp; t < len; t += kWarps) {
-      const float *kp = (a + t == pos) ? knew : kb + t * hd;
-      float kv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kv[j] = j < E ? kp[lane * E + j] : 0.f;
-      float dot[8];
-#pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        float d0 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
-        dot[h] = d0;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int h = 0; h < 8; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
-      if (lane < qpk && lane < 8) {
-        float v = dot[0];
-#pragma unroll
-        for (int h = 1; h < 8; ++h) v = (lane == h) ? dot[h] : v;
-        sc[lane * SUB + t] = __fmul_rn(v, A.scale);
-      }
+    switch (hd / 32) {
+      case 2: attn_scores<2>(qs, knew, kb, a, len, pos, qpk, J.scale, sc, SUB); break;
+      case 4: attn_scores<4>(qs, knew, kb, a, len, pos, qpk, J.scale, sc, SUB); break;
+      default: attn_scores<8>(qs, knew, kb, a, len, pos, qpk, J.scale, sc, SUB); break;
     }
-    __syncthreads();
-    // online softmax per head: warp h owns head h (e = exp in float64)
+    csync();
+    // online softmax per head: warp h owns head h (exp in float64)
     for (int h = warp; h < qpk; h += kWarps) {
       float m = -INFINITY;
       for (int t = lane; t < len; t += 32) m = fmaxf(m, sc[h * SUB + t]);
@@ -869,7 +846,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
         s_m[h] = m_new;
       }
     }
-    __syncthreads();
+    csync();
     // acc[h][d] = acc*scale + sum_t e[h][t] v[t][d]
     for (int i = tid; i < qpk * hd; i += kThreads) {
       const int h = i / hd, d = i - h * hd;
@@ -885,48 +862,103 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
       if (t < len) a0 = fmaf(e[t], (a + t == pos) ? vnew[d] : vb[t * hd + d], a0);
       acc[i] = acc[i] * s_scale[h] + (a0 + a1);
     }
-    __syncthreads();
+    csync();
     if (tid == 0 && it + 2 < n_sub) issue(it + 2);
   }
-  (void)ok_all;
-  const int h0 = g * qpk;
-  if (nsplit == 1) {  // single split: normalise and write the heads directly
+  const int h0 = J.g * qpk;
+  if (J.nsplit == 1) {  // single split: normalise and write the heads directly
     for (int i = tid; i < qpk * hd; i += kThreads) {
       const int h = i / hd;
-      A.out[(h0 + h) * hd + (i - h * hd)] = acc[i] / s_l[h];
+      J.out[(h0 + h) * hd + (i - h * hd)] = acc[i] / s_l[h];
     }
-    return;
+    return ok;
   }
   // partial (m, l, acc) of this split; the last split of the group combines
   for (int i = tid; i < qpk * (hd + 2); i += kThreads) {
     const int h = i / (hd + 2), k = i - h * (hd + 2);
-    float *pp = A.part + (static_cast<size_t>(h0 + h) * A.max_splits + s) * (hd + 2);
+    float *pp = J.part + (static_cast<size_t>(h0 + h) * J.max_splits + J.s) * (hd + 2);
     pp[k] = k == 0 ? s_m[h] : (k == 1 ? s_l[h] : acc[h * hd + k - 2]);
   }
   __threadfence();
-  __syncthreads();
+  csync();
   if (tid == 0) {
-    const unsigned t = atomicAdd(&st->attn_counter[g], 1u);
-    s_last = (t == static_cast<unsigned>(nsplit - 1)) ? 1 : 0;
+    const unsigned t = atomicAdd(J.counter, 1u);
+    s_last = (t == static_cast<unsigned>(J.nsplit - 1)) ? 1 : 0;
   }
-  __syncthreads();
-  if (!s_last) return;
+  csync();
+  if (!s_last) return ok;
   __threadfence();
   for (int i = tid; i < qpk * hd; i += kThreads) {
     const int h = h0 + i / hd, d = i % hd;
-    const float *base = A.part + static_cast<size_t>(h) * A.max_splits * (hd + 2);
+    const float *base = J.part + static_cast<size_t>(h) * J.max_splits * (hd + 2);
     float M = -INFINITY;
-    for (int k = 0; k < nsplit; ++k) M = fmaxf(M, __ldcg(base + static_cast<size_t>(k) * (hd + 2)));
+    for (int k = 0; k < J.nsplit; ++k) M = fmaxf(M, __ldcg(base + static_cast<size_t>(k) * (hd + 2)));
     float L = 0.f, O = 0.f;
-    for (int k = 0; k < nsplit; ++k) {
+    for (int k = 0; k < J.nsplit; ++k) {
       const float *pk = base + static_cast<size_t>(k) * (hd + 2);
       const float w = static_cast<float>(exp(static_cast<double>(__fsub_rn(__ldcg(pk), M))));
       L = fmaf(w, __ldcg(pk + 1), L);
       O = fmaf(w, __ldcg(pk + 2 + d), O);
     }
-    A.out[h * hd + d] = O / L;
+    J.out[h * hd + d] = O / L;
   }
-  if (tid == 0) st->attn_counter[g] = 0;
+  if (tid == 0) *J.counter = 0;
+  return ok;
+}
+
+__global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
+  extern __shared__ __align__(128) float asmem[];
+  __shared__ __align__(8) uint64_t bars[2];
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+  pdl_wait();
+  DevState *st = A.st;
+  if (A.check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
+  const int g = blockIdx.x, s = blockIdx.y;
+  const int pos = st->fwd_pos;
+  if (pos < 0 || pos >= A.max_tokens) {
+    if (tid == 0 && s == 0 && g == 0) atomicOr(&st->err, kErrPos);
+    return;
+  }
+  const int n = pos + 1, hd = A.hd;
+  const int nsplit = (n + A.split_len - 1) / A.split_len;
+  if (s >= nsplit) return;
+  // KV layout [L][KVH][max_tokens][hd] per plane (engine/kvcache.go:127-140)
+  const size_t head_stride = static_cast<size_t>(A.max_tokens) * hd;
+  const size_t off = static_cast<size_t>(A.layer) * A.n_kv * head_stride + g * head_stride;
+  AttnJob J;
+  J.qpk = A.n_heads / A.n_kv;
+  J.q = A.q + g * J.qpk * hd;
+  J.k = A.k + g * hd;
+  J.v = A.v + g * hd;
+  J.q_norm = A.q_norm;
+  J.k_norm = A.k_norm;
+  J.kc = A.kcache + off;
+  J.vc = A.vcache + off;
+  // RoPETable.Apply rejects pos outside the table (tensor/ops.go:263)
+  J.rope_cs = pos < A.rope_len ? A.rope_cos + static_cast<size_t>(pos) * (hd / 2) : nullptr;
+  J.rope_sn = pos < A.rope_len ? A.rope_sin + static_cast<size_t>(pos) * (hd / 2) : nullptr;
+  J.out = A.out;
+  J.part = A.part;
+  J.counter = &st->attn_counter[g];
+  J.g = g;
+  J.s = s;
+  J.nsplit = nsplit;
+  J.p0 = s * A.split_len;
+  J.p1 = min(n, J.p0 + A.split_len);
+  J.pos = pos;
+  J.hd = hd;
+  J.max_splits = A.max_splits;
+  J.eps = A.eps;
+  J.scale = A.scale;
+  uint32_t uses[2] = {0, 0};
+  attend(J, asmem, bars, uses, &st->err);
 }
 
 // ---------------------------------------------------------------------------

@@ -49,8 +49,9 @@ struct PParams {
   int nphase, n_steps;
   int nslot;
   int off_full, off_empty, off_abar, off_act;
-  int off_xn, off_xt, off_q8, off_y, yrows;  // relative to off_act
-  int H, n_heads, n_kv, hd, max_tokens, max_splits, rope_len;
+  int off_xn, off_limbs, off_q8, off_y, yrows;  // relative to off_act
+  int slot_bytes, slot_alloc;  // weight ring: payload per slot, slot stride
+  int H, n_heads, n_kv, hd, max_tokens, max_splits, split_len, rope_len;
   float eps, scale;
   float *X, *normx, *q, *k, *v, *attn_out, *h, *logits, *part;
   float2 *amax_part;
@@ -79,14 +80,15 @@ __host__ __device__ inline int qrow_bytes(int type, int cols) {
          : type == T_Q6_K ? (cols / 256) * 210 : cols * 4;
 }
 
-__device__ __forceinline__ Seg pseg(const uint8_t *w, int type, int rows, int cols, const float *bias, float *out) {
+__device__ __forceinline__ Seg pseg(const uint8_t *w, int type, int rows, int cols, const float *bias, float *out,
+                                    int slot_bytes) {
   Seg s;
   s.w = w;
   s.type = type;
   s.rows = rows;
   s.row_bytes = qrow_bytes(type, cols);
   s.units = (type == T_Q4_K || type == T_Q6_K) ? (cols / 256) * 4 : cols / 32;
-  s.rows_per_chunk = max(1, kStageBytes / s.row_bytes);
+  s.rows_per_chunk = max(1, slot_bytes / s.row_bytes);
   s.bias = bias;
   s.out = out;
   return s;
@@ -136,67 +138,29 @@ __device__ __forceinline__ bool grid_barrier(unsigned *counter, unsigned seq, un
   return *s_ok != 0;
 }
 
-// chunk enumeration of one phase for CTA c (same on both sides of the ring)
-__device__ __forceinline__ int phase_chunks(const PPhase &ph, int c, int G, int (&my0)[kMaxSegs],
-                                            int (&my1)[kMaxSegs]) {
-  int n = 0;
-  for (int s = 0; s < kMaxSegs; ++s) {
-    my0[s] = my1[s] = 0;
-    if (s < ph.nseg) {
-      seg_rows(ph.seg[s].rows, c, G, my0[s], my1[s]);
-      const int cpr = ph.seg[s].rows_per_chunk;
-      n += (my1[s] - my0[s] + cpr - 1) / cpr;
-    }
-  }
-  return n;
-}
-
-__device__ __forceinline__ ChunkRef phase_chunk_at(const PPhase &ph, const int (&my0)[kMaxSegs],
-                                                   const int (&my1)[kMaxSegs], int i) {
-  ChunkRef c{0, 0, 0};
-  for (int s = 0; s < ph.nseg; ++s) {
-    const int cpr = ph.seg[s].rows_per_chunk;
-    const int nch = (my1[s] - my0[s] + cpr - 1) / cpr;
-    if (i < nch) {
-      c.seg = s;
-      c.r0 = my0[s] + i * cpr;
-      c.r1 = min(my1[s], c.r0 + cpr);
-      return c;
-    }
-    i -= nch;
-  }
-  return c;
-}
-
-__device__ __forceinline__ void issue_rows(const Seg &S, const ChunkRef &c, uint8_t *slot, uint64_t *bar) {
-  const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(c.r0) * S.row_bytes;
-  const uintptr_t end = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(c.r1) * S.row_bytes;
-  const uintptr_t a0 = src & ~uintptr_t(15);
-  const uintptr_t a1 = (end + 15) & ~uintptr_t(15);
-  const uint32_t bytes = static_cast<uint32_t>(a1 - a0);
-  mbar_arrive_expect_tx(bar, bytes);
-  bulk_g2s(slot, reinterpret_cast<const void *>(a0), bytes, bar);
-}
-
-// Q8_K of a global vector straight into shared memory: each warp takes 2
-// superblocks per round with all their loads in flight.
+// Q8_K of a global vector straight into shared memory: warp w quantises
+// superblocks w, w + kWarps, ... with all of its loads in flight first
+// (cols <= 4 * kWarps * 256 per call round).
 __device__ __forceinline__ void build_q8k_global(const float *src, int cols, int8_t *qs, float *d, int32_t *bsum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsb = cols / 256;
-  for (int sb0 = warp; sb0 < nsb; sb0 += 2 * kWarps) {
-    const int sb1 = sb0 + kWarps;
-    float4 a0 = make_float4(0, 0, 0, 0), b0 = a0, a1 = a0, b1 = a0;
-    a0 = __ldcg(reinterpret_cast<const float4 *>(src + sb0 * 256 + lane * 8));
-    b0 = __ldcg(reinterpret_cast<const float4 *>(src + sb0 * 256 + lane * 8 + 4));
-    if (sb1 < nsb) {
-      a1 = __ldcg(reinterpret_cast<const float4 *>(src + sb1 * 256 + lane * 8));
-      b1 = __ldcg(reinterpret_cast<const float4 *>(src + sb1 * 256 + lane * 8 + 4));
+  constexpr int kPer = 4;  // superblocks per warp per round
+  for (int base = 0; base < nsb; base += kPer * kWarps) {
+    float4 a[kPer], b[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int sb = base + warp + k * kWarps;
+      a[k] = b[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (sb < nsb) {
+        a[k] = __ldcg(reinterpret_cast<const float4 *>(src + sb * 256 + lane * 8));
+        b[k] = __ldcg(reinterpret_cast<const float4 *>(src + sb * 256 + lane * 8 + 4));
+      }
     }
-    for (int k = 0; k < 2; ++k) {
-      const int sb = k ? sb1 : sb0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int sb = base + warp + k * kWarps;
       if (sb >= nsb) break;
-      const float4 a = k ? a1 : a0, b = k ? b1 : b0;
-      float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      float x[8] = {a[k].x, a[k].y, a[k].z, a[k].w, b[k].x, b[k].y, b[k].z, b[k].w};
       quantize_sb_warp(x, d + sb, bsum + sb * 16, [&](int ln, const int (&q)[8]) {
         int8_t *dst = qs + q8_pad_index(sb * 256 + ln * 8);
         uint32_t w0 = 0, w1 = 0;
@@ -233,7 +197,7 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
     ph.layer = -1;
     ph.nseg = 1;
     ph.cols = P.H;
-    ph.seg[0] = pseg(P.out_w, P.out_type, P.vocab, P.H, nullptr, P.logits);
+    ph.seg[0] = pseg(P.out_w, P.out_type, P.vocab, P.H, nullptr, P.logits, P.slot_bytes);
     ph.norm_w = P.out_norm;
     needs();
     return;
@@ -246,9 +210,9 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
       ph.kind = K_QKV;
       ph.nseg = 3;
       ph.cols = P.H;
-      ph.seg[0] = pseg(L.q, L.tq, P.H, P.H, L.qb, P.q);
-      ph.seg[1] = pseg(L.k, L.tk, P.kvd, P.H, L.kb, P.k);
-      ph.seg[2] = pseg(L.v, L.tv, P.kvd, P.H, L.vb, P.v);
+      ph.seg[0] = pseg(L.q, L.tq, P.H, P.H, L.qb, P.q, P.slot_bytes);
+      ph.seg[1] = pseg(L.k, L.tk, P.kvd, P.H, L.kb, P.k, P.slot_bytes);
+      ph.seg[2] = pseg(L.v, L.tv, P.kvd, P.H, L.vb, P.v, P.slot_bytes);
       ph.norm_w = L.attn_norm;
       ph.do_embed = (l == 0);
       break;
@@ -262,22 +226,22 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
       ph.kind = K_OPROJ;
       ph.nseg = 1;
       ph.cols = P.H;
-      ph.seg[0] = pseg(L.o, L.to, P.H, P.H, nullptr, P.X);
+      ph.seg[0] = pseg(L.o, L.to, P.H, P.H, nullptr, P.X, P.slot_bytes);
       ph.x_in = P.attn_out;
       break;
     case 3:
       ph.kind = K_FFN_UP;
       ph.nseg = 2;
       ph.cols = P.H;
-      ph.seg[0] = pseg(L.gate, L.tg, P.F, P.H, nullptr, nullptr);
-      ph.seg[1] = pseg(L.up, L.tu, P.F, P.H, nullptr, nullptr);
+      ph.seg[0] = pseg(L.gate, L.tg, P.F, P.H, nullptr, nullptr, P.slot_bytes);
+      ph.seg[1] = pseg(L.up, L.tu, P.F, P.H, nullptr, nullptr, P.slot_bytes);
       ph.norm_w = L.ffn_norm;
       break;
     default:
       ph.kind = K_FFN_DOWN;
       ph.nseg = 1;
       ph.cols = P.F;
-      ph.seg[0] = pseg(L.down, L.td, P.H, P.F, nullptr, P.X);
+      ph.seg[0] = pseg(L.down, L.td, P.H, P.F, nullptr, P.X, P.slot_bytes);
       ph.x_in = P.h;
       ph.commit_here = (l == P.n_layers - 1);
       break;
@@ -286,304 +250,272 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
 }
 
 // ---------------------------------------------------------------------------
-// attention item (kv head g, split s) of the current position; the last
-// split of a group combines.  Shared memory: the activation region.
+// attention: CTA c takes item c = (kv head g, split s) of the step's position
+// (read, with its RoPE row, during the logits phase).  Splits are fixed
+// position ranges, so the CTA that stores a cache row is the one that reads
+// it in later steps.
 // ---------------------------------------------------------------------------
-__device__ void p_attention(const PParams &P, const PPhase &ph, float *asmem, uint64_t *abar, uint32_t (&uses)[2],
-                            int item) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+__device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, uint64_t *abar, uint32_t (&uses)[2],
+                            int item, int pos, const float *rope_row) {
   DevState *st = P.st;
-  const int hd = P.hd, qpk = P.n_heads / P.n_kv, SUB = attn_sub(hd);
-  const int pos = ldst(&st->fwd_pos);
   if (pos < 0 || pos >= P.max_tokens) {
-    if (tid == 0 && item == 0) atomicOr(&st->err, kErrPos);
-    return;
+    if (threadIdx.x == 0 && item == 0) atomicOr(&st->err, kErrPos);
+    return true;
   }
-  const int n = pos + 1;
-  const int nsplit = attn_nsplit(n, P.max_splits);
-  if (item >= P.n_kv * nsplit) return;
+  const int n = pos + 1, hd = P.hd;
+  const int nsplit = (n + P.split_len - 1) / P.split_len;
+  if (item >= P.n_kv * nsplit) return true;
   const int g = item / nsplit, s = item % nsplit;
-  const int chunk = (n + nsplit - 1) / nsplit;
-  const int p0 = min(n, s * chunk), p1 = min(n, p0 + chunk);
   const size_t head_stride = static_cast<size_t>(P.max_tokens) * hd;
-  const size_t layer_stride = static_cast<size_t>(P.n_kv) * head_stride;
-  float *kc = P.kcache + static_cast<size_t>(ph.layer) * layer_stride + g * head_stride;
-  float *vc = P.vcache + static_cast<size_t>(ph.layer) * layer_stride + g * head_stride;
-  float *kbuf = asmem, *vbuf = kbuf + 2 * SUB * hd, *qs = vbuf + 2 * SUB * hd;
-  float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd, *acc = sc + qpk * SUB;
-  __shared__ float s_m[8], s_l[8], s_scale[8];
-  __shared__ int s_last;
-  const int n_sub = (p1 - p0 + SUB - 1) / SUB;
-  auto issue = [&](int it) {
-    const int a = p0 + it * SUB, b = min(p1, a + SUB);
-    const int cached = max(0, min(b, pos) - a);
-    if (cached > 0) {
-      const uint32_t bytes = static_cast<uint32_t>(cached) * hd * 4;
-      uint64_t *bar = &abar[it & 1];
-      mbar_arrive_expect_tx(bar, 2 * bytes);
-      bulk_g2s(kbuf + (it & 1) * SUB * hd, kc + static_cast<size_t>(a) * hd, bytes, bar);
-      bulk_g2s(vbuf + (it & 1) * SUB * hd, vc + static_cast<size_t>(a) * hd, bytes, bar);
-    }
-  };
-  // sub-chunks whose cached part is non-empty use (and advance) their buffer's barrier
-  auto uses_bar = [&](int it) {
-    const int a = p0 + it * SUB, b = min(p1, a + SUB);
-    return min(b, pos) - a > 0;
-  };
-  if (tid == 0) {
-    fence_proxy_async();
-    issue(0);
-    if (n_sub > 1) issue(1);
-  }
-  for (int i = tid; i < qpk * hd; i += kThreads) {
-    qs[i] = __ldcg(P.q + g * qpk * hd + i);
-    acc[i] = 0.f;
-  }
-  for (int i = tid; i < hd; i += kThreads) {
-    knew[i] = __ldcg(P.k + g * hd + i);
-    vnew[i] = __ldcg(P.v + g * hd + i);
-  }
-  if (tid < 8) {
-    s_m[tid] = -INFINITY;
-    s_l[tid] = 0.f;
-  }
-  csync();
-  if (ph.q_norm)
-    for (int h = warp; h < qpk; h += kWarps) head_rmsnorm_warp(qs + h * hd, ph.q_norm, hd, P.eps);
-  if (ph.k_norm && warp == kWarps - 1) head_rmsnorm_warp(knew, ph.k_norm, hd, P.eps);
-  csync();
-  if (pos < P.rope_len) {
-    const float *cs = P.rope_cos + static_cast<size_t>(pos) * (hd / 2);
-    const float *sn = P.rope_sin + static_cast<size_t>(pos) * (hd / 2);
-    for (int h = 0; h < qpk; ++h) rope_rotate(qs + h * hd, hd, cs, sn, tid, kThreads);
-    rope_rotate(knew, hd, cs, sn, tid, kThreads);
-  }
-  csync();
-  if (pos >= p0 && pos < p1) {
-    for (int i = tid; i < hd; i += kThreads) {
-      kc[static_cast<size_t>(pos) * hd + i] = knew[i];
-      vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
-    }
-    fence_proxy_async();  // later TMA reads of this row see it
-  }
-  const int E = hd / 32;
-  float qr[8][4];
-#pragma unroll
-  for (int h = 0; h < 8; ++h)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) qr[h][j] = (h < qpk && j < E) ? qs[h * hd + lane * E + j] : 0.f;
-  for (int it = 0; it < n_sub; ++it) {
-    const int a = p0 + it * SUB, b = min(p1, a + SUB), len = b - a;
-    if (uses_bar(it)) {  // completions of a buffer's barrier alternate parity
-      mbar_wait_bounded(&abar[it & 1], uses[it & 1] & 1u, &st->err);
-      uses[it & 1] += 1;
-    }
-    const float *kb = kbuf + (it & 1) * SUB * hd;
-    const float *vb = vbuf + (it & 1) * SUB * hd;
-    for (int t = warp; t < len; t += kWarps) {
-      const float *kp = (a + t == pos) ? knew : kb + t * hd;
-      float kv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) kv[j] = j < E ? kp[lane * E + j] : 0.f;
-      float dot[8];
-#pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        float d0 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
-        dot[h] = d0;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int h = 0; h < 8; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
-      if (lane < qpk) {
-        float v = dot[0];
-#pragma unroll
-        for (int h = 1; h < 8; ++h) v = (lane == h) ? dot[h] : v;
-        sc[lane * SUB + t] = __fmul_rn(v, P.scale);
-      }
-    }
-    csync();
-    for (int h = warp; h < qpk; h += kWarps) {
-      float m = -INFINITY;
-      for (int t = lane; t < len; t += 32) m = fmaxf(m, sc[h * SUB + t]);
-      m = warp_max(m);
-      const float m_new = fmaxf(s_m[h], m);
-      float l = 0.f;
-      for (int t = lane; t < len; t += 32) {
-        const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sc[h * SUB + t], m_new))));
-        sc[h * SUB + t] = e;
-        l += e;
-      }
-      l = warp_sum(l);
-      if (lane == 0) {
-        const float scl = static_cast<float>(exp(static_cast<double>(s_m[h] - m_new)));
-        s_scale[h] = scl;
-        s_l[h] = s_l[h] * scl + l;
-        s_m[h] = m_new;
-      }
-    }
-    csync();
-    for (int i = tid; i < qpk * hd; i += kThreads) {
-      const int h = i / hd, d = i - h * hd;
-      const float *e = sc + h * SUB;
-      float a0 = 0.f, a1 = 0.f;
-      int t = 0;
-      for (; t + 1 < len; t += 2) {
-        a0 = fmaf(e[t], (a + t == pos) ? vnew[d] : vb[t * hd + d], a0);
-        a1 = fmaf(e[t + 1], (a + t + 1 == pos) ? vnew[d] : vb[(t + 1) * hd + d], a1);
-      }
-      if (t < len) a0 = fmaf(e[t], (a + t == pos) ? vnew[d] : vb[t * hd + d], a0);
-      acc[i] = acc[i] * s_scale[h] + (a0 + a1);
-    }
-    csync();
-    if (tid == 0 && it + 2 < n_sub) issue(it + 2);
-  }
-  const int h0 = g * qpk;
-  if (nsplit == 1) {
-    for (int i = tid; i < qpk * hd; i += kThreads) {
-      const int h = i / hd;
-      P.attn_out[(h0 + h) * hd + (i - h * hd)] = acc[i] / s_l[h];
-    }
-    return;
-  }
-  for (int i = tid; i < qpk * (hd + 2); i += kThreads) {
-    const int h = i / (hd + 2), kk = i - h * (hd + 2);
-    float *pp = P.part + (static_cast<size_t>(h0 + h) * P.max_splits + s) * (hd + 2);
-    pp[kk] = kk == 0 ? s_m[h] : (kk == 1 ? s_l[h] : acc[h * hd + kk - 2]);
-  }
-  __threadfence();
-  csync();
-  if (tid == 0) {
-    const unsigned t = atomicAdd(&st->attn_counter[g], 1u);
-    s_last = (t == static_cast<unsigned>(nsplit - 1)) ? 1 : 0;
-  }
-  csync();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < qpk * hd; i += kThreads) {
-    const int h = h0 + i / hd, d = i % hd;
-    const float *base = P.part + static_cast<size_t>(h) * P.max_splits * (hd + 2);
-    float M = -INFINITY;
-    for (int kk = 0; kk < nsplit; ++kk) M = fmaxf(M, __ldcg(base + static_cast<size_t>(kk) * (hd + 2)));
-    float L = 0.f, O = 0.f;
-    for (int kk = 0; kk < nsplit; ++kk) {
-      const float *pk = base + static_cast<size_t>(kk) * (hd + 2);
-      const float w = static_cast<float>(exp(static_cast<double>(__fsub_rn(__ldcg(pk), M))));
-      L = fmaf(w, __ldcg(pk + 1), L);
-      O = fmaf(w, __ldcg(pk + 2 + d), O);
-    }
-    P.attn_out[h * hd + d] = O / L;
-  }
-  if (tid == 0) st->attn_counter[g] = 0;
+  const size_t off = (static_cast<size_t>(ph.layer) * P.n_kv + g) * head_stride;
+  AttnJob J;
+  J.qpk = P.n_heads / P.n_kv;
+  J.q = P.q + g * J.qpk * hd;
+  J.k = P.k + g * hd;
+  J.v = P.v + g * hd;
+  J.q_norm = ph.q_norm;
+  J.k_norm = ph.k_norm;
+  J.kc = P.kcache + off;
+  J.vc = P.vcache + off;
+  J.rope_cs = pos < P.rope_len ? rope_row : nullptr;
+  J.rope_sn = pos < P.rope_len ? rope_row + hd / 2 : nullptr;
+  J.out = P.attn_out;
+  J.part = P.part;
+  J.counter = &st->attn_counter[g];
+  J.g = g;
+  J.s = s;
+  J.nsplit = nsplit;
+  J.p0 = s * P.split_len;
+  J.p1 = min(n, J.p0 + P.split_len);
+  J.pos = pos;
+  J.hd = hd;
+  J.max_splits = P.max_splits;
+  J.eps = P.eps;
+  J.scale = P.scale;
+  return attend(J, asmem, abar, uses, &st->err);
 }
 
 // ---------------------------------------------------------------------------
 // one matvec phase on the compute warps; weights arrive through the ring
 // ---------------------------------------------------------------------------
+struct PhaseRows {
+  int r0[kMaxSegs], r1[kMaxSegs];
+};
+
+// chunk i of the phase for this CTA: segment, first row, row count, offset
+// of the first row in the CTA's rows of that segment (same enumeration on
+// both sides of the ring)
+struct PChunk {
+  int seg, r0, nr, lr0;
+};
+
+__device__ __forceinline__ int phase_rows(const PPhase &ph, int c, int G, PhaseRows &R) {
+  int n = 0;
+#pragma unroll
+  for (int s = 0; s < kMaxSegs; ++s) {
+    R.r0[s] = R.r1[s] = 0;
+    if (s < ph.nseg) {
+      seg_rows(ph.seg[s].rows, c, G, R.r0[s], R.r1[s]);
+      const int cpr = ph.seg[s].rows_per_chunk;
+      n += (R.r1[s] - R.r0[s] + cpr - 1) / cpr;
+    }
+  }
+  return n;
+}
+
+__device__ __forceinline__ PChunk phase_chunk(const PPhase &ph, const PhaseRows &R, int i) {
+  PChunk c{0, 0, 0, 0};
+  bool found = false;
+#pragma unroll
+  for (int s = 0; s < kMaxSegs; ++s) {
+    if (!found && s < ph.nseg) {
+      const int cpr = ph.seg[s].rows_per_chunk;
+      const int nch = (R.r1[s] - R.r0[s] + cpr - 1) / cpr;
+      if (i < nch) {
+        c.seg = s;
+        c.lr0 = i * cpr;
+        c.r0 = R.r0[s] + c.lr0;
+        c.nr = min(R.r1[s], c.r0 + cpr) - c.r0;
+        found = true;
+      } else {
+        i -= nch;
+      }
+    }
+  }
+  return c;
+}
+
+__device__ __forceinline__ void issue_chunk_rows(const Seg &S, const PChunk &c, uint8_t *slot, uint64_t *bar) {
+  const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(c.r0) * S.row_bytes;
+  const uintptr_t end = src + static_cast<uintptr_t>(c.nr) * S.row_bytes;
+  const uintptr_t a0 = src & ~uintptr_t(15);
+  const uintptr_t a1 = (end + 15) & ~uintptr_t(15);
+  const uint32_t bytes = static_cast<uint32_t>(a1 - a0);
+  mbar_arrive_expect_tx(bar, bytes);
+  bulk_g2s(slot, reinterpret_cast<const void *>(a0), bytes, bar);
+}
+
+// bounded wait of one warp on a ring slot; false on timeout (error flag set)
+__device__ __forceinline__ bool warp_wait_full(uint64_t *bar, uint32_t parity, unsigned *err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint32_t &k_ring, float (*red)[kWarps],
-                         float *scratch, int *s_flag, unsigned long long *tr) {
-  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+                         float *scratch, int *s_flag, int *s_pos, float *s_rope, unsigned long long *tr) {
+  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   DevState *st = P.st;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + P.off_empty);
   uint8_t *act = smem + P.off_act;
+  const int cols = ph.cols, nb = cols / 32, nsb = cols / 256;
   float *xn = reinterpret_cast<float *>(act + P.off_xn);
-  float *xt = reinterpret_cast<float *>(act + P.off_xt);
+  int *la = reinterpret_cast<int *>(act + P.off_limbs);
+  int *lb = la + 8 * nb, *lc = lb + 8 * nb;
+  float *ls = reinterpret_cast<float *>(lc + 8 * nb);
   int8_t *q8qs = reinterpret_cast<int8_t *>(act + P.off_q8);
-  float *q8d = reinterpret_cast<float *>(act + P.off_q8 + q8_qs_bytes(ph.cols));
-  int32_t *q8bs = reinterpret_cast<int32_t *>(act + P.off_q8 + q8_qs_bytes(ph.cols) + 4 * (ph.cols / 256));
+  float *q8d = reinterpret_cast<float *>(act + P.off_q8 + q8_qs_bytes(cols));
+  int32_t *q8bs = reinterpret_cast<int32_t *>(act + P.off_q8 + q8_qs_bytes(cols) + ((4 * nsb + 15) & ~15));
   float *ybuf = reinterpret_cast<float *>(act + P.off_y);
-  Q8KView q8{q8qs, q8d, q8bs};
-  int my0[kMaxSegs], my1[kMaxSegs];
-  const int nchunks = phase_chunks(ph, c, G, my0, my1);
+  const LimbsView LV{la, lb, lc, ls, nb};
+  const Q8KView q8{q8qs, q8d, q8bs};
+  PhaseRows R;
+  const int nchunks = phase_rows(ph, c, G, R);
   const bool residual = ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN;
   const bool normed = ph.kind == K_QKV || ph.kind == K_FFN_UP || ph.kind == K_LOGITS;
-  // values the epilogue needs, requested first
+  // ---- loads the epilogue needs, requested first
   float xres = 0.f, bias[kMaxSegs] = {0.f, 0.f, 0.f};
-  if (residual && my0[0] + tid < my1[0]) xres = __ldcg(P.X + my0[0] + tid);
-  for (int s = 0; s < ph.nseg; ++s)
-    if (ph.seg[s].bias && my0[s] + tid < my1[s]) bias[s] = __ldg(ph.seg[s].bias + my0[s] + tid);
-  const int nbx = ph.cols / 32;
-  // ---- input vector
-  if (normed) {
-    // norm weights of this thread's elements, requested with the activation
-    float nwr[16];
+  if (residual && R.r0[0] + tid < R.r1[0]) xres = __ldcg(P.X + R.r0[0] + tid);
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int e = tid + k * kThreads;
-      nwr[k] = e < ph.cols ? __ldg(ph.norm_w + e) : 0.f;
-    }
-    if (ph.kind == K_QKV && ph.do_embed) {
+  for (int s = 0; s < kMaxSegs; ++s)
+    if (s < ph.nseg && ph.seg[s].bias && R.r0[s] + tid < R.r1[s]) bias[s] = __ldg(ph.seg[s].bias + R.r0[s] + tid);
+  __shared__ int win[kThreads];
+  __shared__ int s_fail;
+  if (ph.kind == K_LOGITS) {
+    // SeqLen = the position this step forwards; the penalty window's ids and
+    // the RoPE row of that position (kept in shared memory for the step)
+    const int wpos = ldst(&st->seq_len);
+    const int wlen = max(0, min(st->window, wpos));
+    if (tid < wlen) win[tid] = ldst(P.token_ids + wpos - wlen + tid);
+    if (tid == 0) *s_pos = wpos;
+    const int half = P.hd / 2;
+    if (wpos >= 0 && wpos < P.rope_len && tid < P.hd)
+      s_rope[tid] = __ldg((tid < half ? P.rope_cos : P.rope_sin) + static_cast<size_t>(wpos) * half + (tid % half));
+  }
+  if (tid == 0) s_fail = 0;
+  // ---- input vector: 4 values per thread per float4 slot (cols <= 16 * kThreads)
+  const int n4 = cols >> 2;
+  if (normed) {
+    float4 xv[4], wv[4];
+    const float4 *x4 = reinterpret_cast<const float4 *>(P.X);
+    const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
+    const bool embed = ph.kind == K_QKV && ph.do_embed;
+    if (embed) {
       int tok = ldst(&st->fwd_token);
       if (tok < 0 || tok >= st->vocab) tok = 0;  // engine/model.go:222-224
-      dequant_row_cta(P.embd_type, P.embd_w + static_cast<size_t>(tok) * P.embd_row_bytes, xn, ph.cols);
-      csync();
-      if (c == 0)
-        for (int i = tid; i < ph.cols; i += kThreads) P.X[i] = xn[i];
-    } else {
-      load_vec_to_smem(xn, P.X, ph.cols);
+      dequant_row_cta(P.embd_type, P.embd_w + static_cast<size_t>(tok) * P.embd_row_bytes, xn, cols);
       csync();
     }
-    // RMSNorm (tensor/ops.go:207-218); norm weights come from L2
-    float ss0 = 0.f, ss1 = 0.f;
-    int i = tid;
-    for (; i + kThreads < ph.cols; i += 2 * kThreads) {
-      ss0 = fmaf(xn[i], xn[i], ss0);
-      ss1 = fmaf(xn[i + kThreads], xn[i + kThreads], ss1);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = tid + k * kThreads;
+      xv[k] = wv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < n4) {
+        xv[k] = embed ? reinterpret_cast<const float4 *>(xn)[i] : __ldcg(x4 + i);
+        wv[k] = __ldg(w4 + i);
+      }
     }
-    if (i < ph.cols) ss0 = fmaf(xn[i], xn[i], ss0);
-    const float ss = block_sum(ss0 + ss1, scratch);
-    const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(ph.cols)), P.eps);
+    if (embed && c == 0)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (tid + k * kThreads < n4) reinterpret_cast<float4 *>(P.X)[tid + k * kThreads] = xv[k];
+    // RMSNorm (tensor/ops.go:207-218)
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      ss = fmaf(xv[k].x, xv[k].x, ss);
+      ss = fmaf(xv[k].y, xv[k].y, ss);
+      ss = fmaf(xv[k].z, xv[k].z, ss);
+      ss = fmaf(xv[k].w, xv[k].w, ss);
+    }
+    ss = block_sum(ss, scratch);
+    const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(cols)), P.eps);
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(mean)));
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int e = tid + k * kThreads;
-      if (e < ph.cols) xn[e] = __fmul_rn(__fmul_rn(xn[e], inv), nwr[k]);
+    for (int k = 0; k < 4; ++k) {
+      xv[k].x = __fmul_rn(__fmul_rn(xv[k].x, inv), wv[k].x);
+      xv[k].y = __fmul_rn(__fmul_rn(xv[k].y, inv), wv[k].y);
+      xv[k].z = __fmul_rn(__fmul_rn(xv[k].z, inv), wv[k].z);
+      xv[k].w = __fmul_rn(__fmul_rn(xv[k].w, inv), wv[k].w);
     }
-    csync();
     if (ph.kind == K_LOGITS && c == 0)
-      for (int kk = tid; kk < ph.cols; kk += kThreads) P.normx[kk] = xn[kk];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (tid + k * kThreads < n4) reinterpret_cast<float4 *>(P.normx)[tid + k * kThreads] = xv[k];
     if (ph.need_f32)
-      for (int kk = tid; kk < ph.cols; kk += kThreads) xt[(kk & 31) * nbx + (kk >> 5)] = xn[kk];
-    if (ph.need_q8k) build_q8k(xn, ph.cols, q8qs, q8d, q8bs);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (k * kThreads < n4) put_limbs(xv[k], tid + k * kThreads, tid + k * kThreads < n4, la, lb, lc, ls, nb);
+    if (ph.need_q8k) {
+      if (embed) csync();  // xn held the embedding row
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (tid + k * kThreads < n4) reinterpret_cast<float4 *>(xn)[tid + k * kThreads] = xv[k];
+      csync();
+      build_q8k(xn, cols, q8qs, q8d, q8bs);
+    }
   } else {
     if (ph.need_f32) {
-      load_vec_to_smem(xn, ph.x_in, ph.cols);
-      csync();
-      for (int kk = tid; kk < ph.cols; kk += kThreads) xt[(kk & 31) * nbx + (kk >> 5)] = xn[kk];
+      const float4 *x4 = reinterpret_cast<const float4 *>(ph.x_in);
+      for (int i0 = 0; i0 < n4; i0 += kThreads) {
+        const int i = i0 + tid;
+        const float4 v = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        put_limbs(v, i, i < n4, la, lb, lc, ls, nb);
+      }
     }
-    if (ph.need_q8k) build_q8k_global(ph.x_in, ph.cols, q8qs, q8d, q8bs);
+    if (ph.need_q8k) build_q8k_global(ph.x_in, cols, q8qs, q8d, q8bs);
   }
   csync();
-  XLimbs xl;
-  const bool xreg = ph.need_f32 && nbx <= 32;
-  if (xreg) lane_limbs(xt, nbx, xl);
   if (tr) tr[1] = globaltimer_ns();
-  // ---- chunks from the ring
+  // ---- chunks from the ring: each warp takes rows j = warp (mod kWarps) of
+  // the phase and releases each slot itself (empty barriers count kWarps)
   long long wait_cyc = 0;
   const long long loop_t0 = tr ? clock64() : 0;
-  for (int i = 0; i < nchunks; ++i, ++k_ring) {
-    const int slot = static_cast<int>(k_ring % static_cast<uint32_t>(P.nslot));
-    const uint32_t parity = (k_ring / static_cast<uint32_t>(P.nslot)) & 1u;
-    if (tid == 0) {
-      const long long w0 = tr ? clock64() : 0;
-      *s_flag = mbar_wait_bounded(&full[slot], parity, &st->err) ? 1 : 0;
-      if (tr) wait_cyc += clock64() - w0;
+  int jbase = 0;
+  for (int i = 0; i < nchunks; ++i) {
+    const uint32_t k = k_ring + static_cast<uint32_t>(i);
+    const int slot = static_cast<int>(k % static_cast<uint32_t>(P.nslot));
+    const uint32_t parity = (k / static_cast<uint32_t>(P.nslot)) & 1u;
+    const long long w0 = tr ? clock64() : 0;
+    if (*reinterpret_cast<volatile int *>(&s_fail) || !warp_wait_full(&full[slot], parity, &st->err)) {
+      s_fail = 1;
+      break;
     }
-    csync();
-    if (!*s_flag) return false;
-    const ChunkRef ch = phase_chunk_at(ph, my0, my1, i);
+    if (tr) wait_cyc += clock64() - w0;
+    const PChunk ch = phase_chunk(ph, R, i);
     const Seg &S = ph.seg[ch.seg];
     const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
-    const uint8_t *rows = smem + static_cast<size_t>(slot) * kStageAlloc + (src & 15);
-    MatParams dummy{};
-    compute_chunk(dummy, S, rows, ch.r1 - ch.r0, ch.r0, xt, nbx, q8,
-                  ybuf + ch.seg * P.yrows + (ch.r0 - my0[ch.seg]), red, xl, xreg);
-    csync();
-    if (tid == 0) mbar_arrive(&empty[slot]);
+    const uint8_t *rows = smem + static_cast<size_t>(slot) * P.slot_alloc + (src & 15);
+    const int first = ((warp - jbase) % kWarps + kWarps) % kWarps;
+    if (first < ch.nr) {
+      const int cnt = (ch.nr - first + kWarps - 1) / kWarps;
+      float *y = ybuf + ch.seg * P.yrows + ch.lr0;
+      switch (S.type) {
+        case T_Q8_0: warp_rows<T_Q8_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
+        case T_Q5_0: warp_rows<T_Q5_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
+        case T_Q4_K: warp_rows<T_Q4_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
+        case T_Q6_K: warp_rows<T_Q6_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
+        default: break;
+      }
+    }
+    jbase += ch.nr;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
   }
+  k_ring += static_cast<uint32_t>(nchunks);
+  csync();
+  if (s_fail) return false;
   if (tr) {
     tr[2] = globaltimer_ns();
     tr[4] = static_cast<unsigned long long>(wait_cyc);
@@ -591,11 +523,12 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   }
   // ---- epilogue
   if (ph.kind == K_QKV) {
-    for (int s = 0; s < ph.nseg; ++s)
-      if (my0[s] + tid < my1[s])
-        ph.seg[s].out[my0[s] + tid] = __fadd_rn(ybuf[s * P.yrows + tid], bias[s]);
+#pragma unroll
+    for (int s = 0; s < kMaxSegs; ++s)
+      if (s < ph.nseg && R.r0[s] + tid < R.r1[s])
+        ph.seg[s].out[R.r0[s] + tid] = __fadd_rn(ybuf[s * P.yrows + tid], bias[s]);
   } else if (residual) {
-    if (my0[0] + tid < my1[0]) P.X[my0[0] + tid] = __fadd_rn(xres, ybuf[tid]);
+    if (R.r0[0] + tid < R.r1[0]) P.X[R.r0[0] + tid] = __fadd_rn(xres, ybuf[tid]);
     if (ph.kind == K_FFN_DOWN && ph.commit_here && c == 0 && tid == 0 && ldst(&st->commit)) {
       const int pos = ldst(&st->fwd_pos);
       if (pos >= 0 && pos < st->out_cap) P.token_ids[pos] = ldst(&st->fwd_token);  // KVCache.StoreTokenID
@@ -607,32 +540,44 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     }
   } else if (ph.kind == K_FFN_UP) {
     // SwiGLU (internal/simd/c2_tensor_swiglu_nosimd_gen.go:11-19), float64 exp
-    if (my0[0] + tid < my1[0]) {
+    if (R.r0[0] + tid < R.r1[0]) {
       const double g = static_cast<double>(ybuf[tid]);
       const float silu = static_cast<float>(g / (1.0 + exp(-g)));
-      P.h[my0[0] + tid] = __fmul_rn(silu, ybuf[P.yrows + tid]);
+      P.h[R.r0[0] + tid] = __fmul_rn(silu, ybuf[P.yrows + tid]);
     }
   } else if (ph.kind == K_LOGITS) {
-    const int n = my1[0] - my0[0];
-    for (int r = tid; r < n; r += kThreads) P.logits[my0[0] + r] = ybuf[r];
-    // the penalty window's ids, fetched in parallel
-    __shared__ int win[kThreads];
-    const int wpos = ldst(&st->seq_len);
-    const int wlen = max(0, min(st->window, wpos));
-    if (tid < wlen) win[tid] = ldst(P.token_ids + wpos - wlen + tid);
-    csync();
-    if (tid == 0) {  // repetition penalty on this CTA's rows (c2slm.go:156-170)
-      const int pos = wpos;
-      int start = pos - st->window;
-      if (start < 0) start = 0;
-      const float pen = st->penalty;
-      for (int p = start; p < pos; ++p) {
-        const int k = p - (pos - wlen);
-        const int tok = k < kThreads ? win[k] : ldst(P.token_ids + p);
-        if (tok >= 0 && tok < st->vocab && tok != st->im_end && tok != st->eos && tok >= my0[0] && tok < my1[0]) {
-          float &v = ybuf[tok - my0[0]];
-          v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
+    const int lo = R.r0[0], n = R.r1[0] - lo;
+    for (int r = tid; r < n; r += kThreads) P.logits[lo + r] = ybuf[r];
+    // repetition penalty on this CTA's rows (c2slm.go:156-170): every
+    // occurrence in the window applies the factor once; the thread holding a
+    // token's first occurrence applies all of them, in place
+    const int pos = *s_pos, wlen = max(0, min(st->window, pos));
+    const float pen = st->penalty;
+    auto penalise = [&](float &v, int times) {
+      for (int q = 0; q < times; ++q) v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
+    };
+    auto eligible = [&](int tok) {
+      return tok >= 0 && tok < st->vocab && tok != st->im_end && tok != st->eos && tok >= lo && tok < lo + n;
+    };
+    csync();  // logits stored before ybuf is penalised
+    if (wlen <= kThreads) {
+      if (tid < wlen) {
+        const int tok = win[tid];
+        if (eligible(tok)) {
+          bool first = true;
+          int times = 0;
+          for (int q = 0; q < wlen; ++q)
+            if (win[q] == tok) {
+              first = first && q >= tid;
+              ++times;
+            }
+          if (first) penalise(ybuf[tok - lo], times);
         }
+      }
+    } else if (tid == 0) {
+      for (int p = pos - wlen; p < pos; ++p) {
+        const int tok = ldst(P.token_ids + p);
+        if (eligible(tok)) penalise(ybuf[tok - lo], 1);
       }
     }
     csync();
@@ -640,9 +585,9 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     int bi = 0x7fffffff;
     for (int r = tid; r < n; r += kThreads) {
       const float v = ybuf[r];
-      if (v > bv || (v == bv && my0[0] + r < bi)) {
+      if (v > bv || (v == bv && lo + r < bi)) {
         bv = v;
-        bi = my0[0] + r;
+        bi = lo + r;
       }
     }
 #pragma unroll
@@ -654,9 +599,9 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
         bi = oi;
       }
     }
-    if ((tid & 31) == 0) {
-      red[0][tid >> 5] = bv;
-      red[1][tid >> 5] = __int_as_float(bi);
+    if (lane == 0) {
+      red[0][warp] = bv;
+      red[1][warp] = __int_as_float(bi);
     }
     csync();
     if (tid == 0) {
@@ -696,9 +641,9 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
         }
       }
       csync();
-      if ((tid & 31) == 0) {
-        red[0][tid >> 5] = best_v;
-        red[1][tid >> 5] = __int_as_float(best_i);
+      if (lane == 0) {
+        red[0][warp] = best_v;
+        red[1][warp] = __int_as_float(best_i);
       }
       csync();
     }
@@ -734,6 +679,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   __shared__ int s_flag, s_ok;
   __shared__ volatile int s_stop;
   __shared__ PPhase s_ph, s_pph;  // current phase: compute side / producer side
+  __shared__ int s_pos;           // position forwarded by the current step
+  __shared__ float s_rope[256];   // its RoPE row: cos[hd/2], sin[hd/2]
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + P.off_empty);
   uint64_t *abar = reinterpret_cast<uint64_t *>(smem + P.off_abar);
@@ -742,7 +689,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   if (tid == 0) {
     for (int i = 0; i < P.nslot; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], kWarps);  // every compute warp releases the slot
     }
     mbar_init(&abar[0], 1);
     mbar_init(&abar[1], 1);
@@ -761,8 +708,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
         build_phase(P, pi, s_pph);
         const PPhase &ph = s_pph;
         if (ph.kind == K_ATTN) continue;
-        int my0[kMaxSegs], my1[kMaxSegs];
-        const int nch = phase_chunks(ph, c, G, my0, my1);
+        PhaseRows R;
+        const int nch = phase_rows(ph, c, G, R);
         for (int i = 0; i < nch; ++i, ++k) {
           const int slot = static_cast<int>(k % static_cast<uint32_t>(P.nslot));
           const uint32_t use = k / static_cast<uint32_t>(P.nslot);
@@ -781,8 +728,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
             }
             if (stopped) break;
           }
-          issue_rows(ph.seg[phase_chunk_at(ph, my0, my1, i).seg], phase_chunk_at(ph, my0, my1, i),
-                     smem + static_cast<size_t>(slot) * kStageAlloc, &full[slot]);
+          const PChunk ch = phase_chunk(ph, R, i);
+          issue_chunk_rows(ph.seg[ch.seg], ch, smem + static_cast<size_t>(slot) * P.slot_alloc, &full[slot]);
         }
       }
     }
@@ -830,9 +777,12 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
         tr[7] = static_cast<unsigned long long>(b1);
       }
       if (ph.kind == K_ATTN) {
-        p_attention(P, ph, reinterpret_cast<float *>(smem + P.off_act), abar, abar_uses, c);
+        if (!p_attention(P, ph, reinterpret_cast<float *>(smem + P.off_act), abar, abar_uses, c, s_pos, s_rope)) {
+          ok = false;
+          break;
+        }
       } else {
-        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag, tr)) { ok = false; break; }
+        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag, &s_pos, s_rope, tr)) { ok = false; break; }
       }
       csync();
       if (tr) tr[3] = globaltimer_ns();
