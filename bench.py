@@ -10,8 +10,8 @@ chosen token.  Decoding stays at config 1's positions (32..159): every 128
 steps SeqLen is rewound to the prompt (KVCache.Rewind), so any --steps K
 measures the same workload.
 
-  value  device-resident decode (CUDA graph replays, inputs in HBM), CUDA
-         events on the engine's stream, max over ranks.
+  value  device-resident decode (one launch of the persistent decode kernel,
+         inputs in HBM), CUDA events on the engine's stream, max over ranks.
   e2e    the public C ABI driven from the host one token per call
          (c2s_decode_step: host token in, next token out, synchronised).
 --impl reference times the reference's algorithm on the host cores instead
@@ -85,6 +85,31 @@ def stage_bytes(path: str) -> dict:
         hd = H // f.get_uint32("qwen2.attention.head_count")[0]
         out["kv_per_pos"] = 2 * L * kvh * hd * 4  # fp32 K and V read per position
         out["layers"] = L
+    return out
+
+
+def phase_table(tr, sb: dict, mean_pos: float) -> dict:
+    """Per-phase time of the persistent decode kernel from its trace
+    ([step, phase, cta, 8]): a phase lasts from the first CTA's start to the
+    first CTA's start of the next phase (grid barrier included); summed over
+    layers, median over steps; bytes are the phase's algorithmic bytes."""
+    import numpy as np
+    tr = tr.astype(np.int64)
+    S, NP, G, _ = tr.shape
+    first = tr[..., 0].min(axis=2).reshape(-1)              # phase starts, in order
+    dur = np.diff(first).astype(np.float64)
+    dur = np.append(dur, np.nan).reshape(S, NP)
+    kinds = ["logits"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * ((NP - 1) // 5)
+    out = {}
+    for k in ("qkv", "attention", "o_proj", "gate_up", "down", "logits"):
+        idx = [i for i, n in enumerate(kinds) if n == k]
+        per_step = np.nansum(dur[:, idx], axis=1)[:-1] / 1000.0  # us; the last step lacks an end
+        b = sb["kv_per_pos"] * (mean_pos + 1) if k == "attention" else sb[k]
+        if len(per_step) == 0:
+            out[k] = {"us_per_step": None, "bytes_per_step": int(b), "gbs": None}
+            continue
+        us = float(np.median(per_step))
+        out[k] = {"us_per_step": round(us, 2), "bytes_per_step": int(b), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
     return out
 
 
@@ -215,7 +240,7 @@ def run_ours(args) -> None:
         path = synth.cached_model(args.model)
     barrier()
     path = synth.cached_model(args.model)
-    eng = K.Engine(path, device=local, max_tokens=16384)
+    eng = K.Engine(path, device=local, max_tokens=1024)
     prompt = np.random.default_rng(rank).integers(0, 151643, PROMPT).astype(np.int32)
     eng.ingest_from(0, prompt)
 
@@ -252,32 +277,45 @@ def run_ours(args) -> None:
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = world * e2e_steps / e2e_s
 
-    # ---- per-stage table and the dominant kernel's roofline ---------------
-    eng.seq_len = PROMPT
-    prof = eng.profile_step(args.profile_steps, PENALTY, WINDOW)
+    # ---- roofline of the dominant kernel and the per-phase breakdown ------
     sb = stage_bytes(path)
-    mean_pos = PROMPT + args.profile_steps / 2.0
-    sb["attention"] = sb["kv_per_pos"] * (mean_pos + 1)
     peak, peak_kind = measured_peaks()
-    stages = {}
-    for name, d in prof.items():
-        if d["launches"] == 0:
-            continue
-        per_launch_bytes = sb[name] * args.profile_steps / d["launches"]
-        avg_s = d["ms"] / d["launches"] / 1000.0
-        stages[name] = {"ms_per_step": round(d["ms"] / args.profile_steps, 4), "launches": d["launches"],
-                        "bytes_per_launch": int(per_launch_bytes),
-                        "gbs": round(per_launch_bytes / avg_s / 1e9, 1)}
-    dom = max(stages, key=lambda k: stages[k]["ms_per_step"])
-    dstage = stages[dom]
-    achieved = dstage["gbs"]
+    per_token = sum(sb[k] for k in ("qkv", "o_proj", "gate_up", "down", "logits")) + \
+        sb["kv_per_pos"] * (PROMPT + PERIOD / 2.0 + 1)
+    step_ms = ms_max / args.steps
+    launches = eng.decode_launches(args.steps)
     traffic = None
     tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
-        traffic = json.load(open(tp)).get(dom)
-    per_token = sum(sb[k] for k in ("qkv", "o_proj", "gate_up", "down", "logits")) + \
-        sb["kv_per_pos"] * (PROMPT + PERIOD / 2.0)
-    step_ms = ms_max / args.steps
+    if launches == 1:
+        # one persistent launch ran the whole timed region: its algorithmic
+        # bytes are the weights + KV rows of every step
+        kernel = "k_persistent"
+        bytes_per_launch = per_token * args.steps
+        achieved = bytes_per_launch / (ms / 1000.0) / 1e9
+        if os.path.exists(tp):
+            t = json.load(open(tp)).get(kernel)
+            if t and t.get("dram_bytes_per_step"):
+                traffic = int(t["dram_bytes_per_step"] * args.steps)
+        eng.seq_len = PROMPT
+        phases = phase_table(eng.trace_decode(args.profile_steps + 2, PENALTY, WINDOW)[2:], sb,
+                             PROMPT + 2 + args.profile_steps / 2.0)
+    else:
+        eng.seq_len = PROMPT
+        prof = eng.profile_step(args.profile_steps, PENALTY, WINDOW)
+        sb["attention"] = sb["kv_per_pos"] * (PROMPT + args.profile_steps / 2.0 + 1)
+        phases = {}
+        for name, d in prof.items():
+            if d["launches"]:
+                per_launch = sb[name] * args.profile_steps / d["launches"]
+                phases[name] = {"us_per_step": round(1000 * d["ms"] / args.profile_steps, 2),
+                                "launches": d["launches"], "bytes_per_launch": int(per_launch),
+                                "gbs": round(per_launch / (d["ms"] / d["launches"] / 1000.0) / 1e9, 1)}
+        kernel = max(phases, key=lambda k: phases[k]["us_per_step"])
+        bytes_per_launch = phases[kernel]["bytes_per_launch"]
+        achieved = phases[kernel]["gbs"]
+        if os.path.exists(tp):
+            t = json.load(open(tp)).get(kernel)
+            traffic = t.get("dram_bytes_per_launch") if isinstance(t, dict) else t
 
     # ---- CPU baseline (rank 0, N=1) ---------------------------------------
     cpu = None
@@ -299,14 +337,14 @@ def run_ours(args) -> None:
                        "l2": "inputs larger than L2 (%.0f MB of weights streamed per step)" % (per_token / 1e6),
                        "bytes_per_token": int(per_token),
                        "step_hbm_frac": round(per_token / (step_ms / 1000.0) / 1e9 / peak, 4)},
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1), "peak": peak,
                          "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic, "bytes_per_launch": dstage["bytes_per_launch"]},
-            "stages": stages,
+                         "traffic": traffic, "bytes_per_launch": int(bytes_per_launch)},
+            "phases": phases,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 36, "d2h_bytes_per_step": 4,
                     "api": "c2s_decode_step"},
-            "gpu_launches": eng.kernels_per_step * args.steps,
+            "gpu_launches": launches,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

@@ -812,9 +812,10 @@ int persistent_setup(c2s_engine *e) {
 
 // n_steps decode steps (logits+select+forward) in one cooperative launch
 int launch_persistent(c2s_engine *e, int n_steps, int rewind_period, int rewind_base,
-                      unsigned long long *trace = nullptr) {
+                      unsigned long long *trace = nullptr, int phase0 = 0) {
   PParams P = e->pp;
   P.trace = trace;
+  P.phase0 = phase0;
   P.n_steps = n_steps;
   P.rewind_period = rewind_period;
   P.rewind_base = rewind_base;
@@ -1392,7 +1393,11 @@ int c2s_decode_step(c2s_engine *e, int32_t token, float penalty, int window, int
   DeviceGuard g(e->device);
   if (int rc = set_gen_state(e, penalty, window, 0)) return rc;
   if (int rc = set_fwd_input(e, token, e->host_seq, 1)) return rc;
-  CK(cudaGraphLaunch(e->g_fwd_select, e->stream));
+  if (e->use_persistent) {  // forward of `token`, then logits + selection
+    if (int rc = launch_persistent(e, 1, 0, 0, nullptr, 1)) return rc;
+  } else {
+    CK(cudaGraphLaunch(e->g_fwd_select, e->stream));
+  }
   CK(cudaMemcpyAsync(e->h_tokens, e->out_tokens, 4, cudaMemcpyDeviceToHost, e->stream));
   CK(cudaStreamSynchronize(e->stream));
   *next_out = e->h_tokens[0];
@@ -1421,6 +1426,11 @@ int c2s_bench_decode(c2s_engine *e, int n_steps, float penalty, int window) {
 }
 
 int c2s_kernels_per_step(const c2s_engine *e) { return e ? e->kernels_per_step : 0; }
+
+int c2s_decode_launches(const c2s_engine *e, int n_steps) {
+  if (!e || n_steps <= 0) return 0;
+  return e->use_persistent ? 1 : e->kernels_per_step * n_steps;
+}
 
 int c2s_bench_decode_timed(c2s_engine *e, int n_steps, float penalty, int window, int period, float *ms_out) {
   if (!e || !ms_out) return fail(C2S_ERR_ARG, "null argument");

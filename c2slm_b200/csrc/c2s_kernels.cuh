@@ -686,11 +686,13 @@ __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int 
 
 __host__ __device__ inline int attn_sub(int hd) { return 4096 / hd; }
 
-// Scores of positions a .. a+len-1 for the qpk (<= 8) heads of a group: one
-// warp per position, lane l holds d = l*E .. l*E+E-1 of q and k.
+// Scores of positions a .. a+len-1 (rows of kb) for the qpk (<= 8) heads of
+// a group: one warp per position, lane l holds d = l*E .. l*E+E-1 of q and
+// k; the 8 head dots are reduced together by a transposing butterfly, after
+// which lane 4h holds head h.
 template <int E>
-__device__ __forceinline__ void attn_scores(const float *qs, const float *knew, const float *kb, int a, int len,
-                                            int pos, int qpk, float scale, float *sc, int SUB) {
+__device__ __forceinline__ void attn_scores(const float *qs, const float *kb, int len, int qpk, float scale,
+                                            float *sc, int SUB) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, hd = 32 * E;
   float qr[8][E];
 #pragma unroll
@@ -698,10 +700,9 @@ __device__ __forceinline__ void attn_scores(const float *qs, const float *knew, 
 #pragma unroll
     for (int j = 0; j < E; ++j) qr[h][j] = h < qpk ? qs[h * hd + lane * E + j] : 0.f;
   for (int t = warp; t < len; t += kWarps) {
-    const float *kp = (a + t == pos) ? knew : kb + t * hd;
     float kv[E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) kv[j] = kp[lane * E + j];
+    for (int j = 0; j < E; ++j) kv[j] = kb[t * hd + lane * E + j];
     float dot[8];
 #pragma unroll
     for (int h = 0; h < 8; ++h) {
@@ -710,16 +711,9 @@ __device__ __forceinline__ void attn_scores(const float *qs, const float *knew, 
       for (int j = 0; j < E; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
       dot[h] = d0;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int h = 0; h < 8; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], o);
-    if (lane < qpk) {
-      float v = dot[0];
-#pragma unroll
-      for (int h = 1; h < 8; ++h) v = (lane == h) ? dot[h] : v;
-      sc[lane * SUB + t] = __fmul_rn(v, scale);
-    }
+    const float v = reduce_rows<8>(dot);
+    const int h = lane >> 2;
+    if ((lane & 3) == 0 && h < qpk) sc[h * SUB + t] = __fmul_rn(v, scale);
   }
 }
 
@@ -740,15 +734,18 @@ struct AttnJob {
 };
 
 // Shared memory: asmem holds [2][SUB][hd] K, [2][SUB][hd] V, [qpk][hd] q,
-// [hd] k, [hd] v, [qpk][SUB] scores, [qpk][hd] accumulators.  bars[2] are the
-// staging barriers; uses[2] counts their completed phases (kept by the
-// caller across items).  Returns false if a bounded wait expired.
-__device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[2], unsigned *err) {
+// [hd] k, [hd] v, [qpk][SUB] scores.  bars[2] are the staging barriers;
+// uses[2] counts their completed phases (kept by the caller across items).
+// Warp h owns head h for the softmax and the weighted sum of V, with its
+// accumulators in registers.  Returns false if a bounded wait expired.
+template <int E>
+__device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[2], unsigned *err) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int hd = J.hd, qpk = J.qpk, SUB = attn_sub(hd), pos = J.pos, p0 = J.p0, p1 = J.p1;
+  constexpr int hd = 32 * E;
+  const int qpk = J.qpk, SUB = attn_sub(hd), pos = J.pos, p0 = J.p0, p1 = J.p1;
   float *kbuf = asmem, *vbuf = kbuf + 2 * SUB * hd, *qs = vbuf + 2 * SUB * hd;
-  float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd, *acc = sc + qpk * SUB;
-  __shared__ float s_m[8], s_l[8], s_scale[8];
+  float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd;
+  __shared__ float s_m[8], s_l[8];
   __shared__ int s_last;
   const int n_sub = (p1 - p0 + SUB - 1) / SUB;
   // stage the cached rows (positions < pos) of sub-chunk it into buffer it&1
@@ -768,15 +765,14 @@ __device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t 
     }
   };
   if (tid == 0) {
-    asm volatile("fence.proxy.async.global;" ::: "memory");  // cache rows stored earlier by this CTA
+    // cache rows this CTA stored in earlier calls, and staging rows it wrote,
+    // are next accessed by the async proxy
+    asm volatile("fence.proxy.async;" ::: "memory");
     issue(0);
     if (n_sub > 1) issue(1);
   }
   // projections: every load in flight at once
-  for (int i = tid; i < qpk * hd; i += kThreads) {
-    qs[i] = __ldcg(J.q + i);
-    acc[i] = 0.f;
-  }
+  for (int i = tid; i < qpk * hd; i += kThreads) qs[i] = __ldcg(J.q + i);
   for (int i = tid; i < hd; i += kThreads) {
     knew[i] = __ldcg(J.k + i);
     vnew[i] = __ldcg(J.v + i);
@@ -793,7 +789,7 @@ __device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t 
     csync();
   }
   if (J.rope_cs) {  // NeoX RoPE of every q head and k: one thread per (head, pair)
-    const int half = hd / 2;
+    constexpr int half = hd / 2;
     for (int t = tid; t < (qpk + 1) * half; t += kThreads) {
       const int h = t / half, i = t - h * half;
       float *v = h < qpk ? qs + h * hd : knew;
@@ -804,34 +800,39 @@ __device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t 
     }
     csync();
   }
-  if (pos >= p0 && pos < p1) {  // KVCache.StoreKV (engine/kvcache.go:143-158)
+  if (pos >= p0 && pos < p1)  // KVCache.StoreKV (engine/kvcache.go:143-158)
     for (int i = tid; i < hd; i += kThreads) {
       J.kc[static_cast<size_t>(pos) * hd + i] = knew[i];
       J.vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
     }
-    asm volatile("fence.proxy.async.global;" ::: "memory");  // later staged reads of this row see it
-  }
+  float acc[E];  // warp h: head h, d = lane*E .. lane*E+E-1
+#pragma unroll
+  for (int j = 0; j < E; ++j) acc[j] = 0.f;
   bool ok = true;
   for (int it = 0; it < n_sub; ++it) {
     const int a = p0 + it * SUB, b = min(p1, a + SUB), len = b - a;
+    float *kb = kbuf + (it & 1) * SUB * hd;
+    float *vb = vbuf + (it & 1) * SUB * hd;
     if (cached_rows(it) > 0) {  // completions of a buffer's barrier alternate parity
       ok = mbar_wait_bounded(&bars[it & 1], uses[it & 1] & 1u, err) && ok;
       uses[it & 1] += 1;
     }
-    const float *kb = kbuf + (it & 1) * SUB * hd;
-    const float *vb = vbuf + (it & 1) * SUB * hd;
-    switch (hd / 32) {
-      case 2: attn_scores<2>(qs, knew, kb, a, len, pos, qpk, J.scale, sc, SUB); break;
-      case 4: attn_scores<4>(qs, knew, kb, a, len, pos, qpk, J.scale, sc, SUB); break;
-      default: attn_scores<8>(qs, knew, kb, a, len, pos, qpk, J.scale, sc, SUB); break;
+    if (pos >= a && pos < b) {  // this token's k, v complete the staged rows
+      for (int i = tid; i < hd; i += kThreads) {
+        kb[(pos - a) * hd + i] = knew[i];
+        vb[(pos - a) * hd + i] = vnew[i];
+      }
+      csync();
     }
+    attn_scores<E>(qs, kb, len, qpk, J.scale, sc, SUB);
     csync();
-    // online softmax per head: warp h owns head h (exp in float64)
-    for (int h = warp; h < qpk; h += kWarps) {
+    if (warp < qpk) {
+      // online softmax of head h = warp (exp in float64), then V
+      const int h = warp;
       float m = -INFINITY;
       for (int t = lane; t < len; t += 32) m = fmaxf(m, sc[h * SUB + t]);
       m = warp_max(m);
-      const float m_new = fmaxf(s_m[h], m);
+      const float m_old = s_m[h], m_new = fmaxf(m_old, m);
       float l = 0.f;
       for (int t = lane; t < len; t += 32) {
         const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sc[h * SUB + t], m_new))));
@@ -839,45 +840,53 @@ __device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t 
         l += e;
       }
       l = warp_sum(l);
+      const float scale = static_cast<float>(exp(static_cast<double>(m_old - m_new)));
+      __syncwarp();
+      float a0[E], a1[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) a0[j] = a1[j] = 0.f;
+      const float *e = sc + h * SUB;
+      int t = 0;
+      for (; t + 1 < len; t += 2) {
+        const float e0 = e[t], e1 = e[t + 1];
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          a0[j] = fmaf(e0, vb[t * hd + lane * E + j], a0[j]);
+          a1[j] = fmaf(e1, vb[(t + 1) * hd + lane * E + j], a1[j]);
+        }
+      }
+      if (t < len)
+#pragma unroll
+        for (int j = 0; j < E; ++j) a0[j] = fmaf(e[t], vb[t * hd + lane * E + j], a0[j]);
+#pragma unroll
+      for (int j = 0; j < E; ++j) acc[j] = acc[j] * scale + (a0[j] + a1[j]);
       if (lane == 0) {
-        const float scale = static_cast<float>(exp(static_cast<double>(s_m[h] - m_new)));
-        s_scale[h] = scale;
         s_l[h] = s_l[h] * scale + l;
         s_m[h] = m_new;
       }
     }
     csync();
-    // acc[h][d] = acc*scale + sum_t e[h][t] v[t][d]
-    for (int i = tid; i < qpk * hd; i += kThreads) {
-      const int h = i / hd, d = i - h * hd;
-      const float *e = sc + h * SUB;
-      float a0 = 0.f, a1 = 0.f;
-      int t = 0;
-      for (; t + 1 < len; t += 2) {
-        const float v0 = (a + t == pos) ? vnew[d] : vb[t * hd + d];
-        const float v1 = (a + t + 1 == pos) ? vnew[d] : vb[(t + 1) * hd + d];
-        a0 = fmaf(e[t], v0, a0);
-        a1 = fmaf(e[t + 1], v1, a1);
-      }
-      if (t < len) a0 = fmaf(e[t], (a + t == pos) ? vnew[d] : vb[t * hd + d], a0);
-      acc[i] = acc[i] * s_scale[h] + (a0 + a1);
+    if (tid == 0 && it + 2 < n_sub) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(it + 2);
     }
-    csync();
-    if (tid == 0 && it + 2 < n_sub) issue(it + 2);
   }
   const int h0 = J.g * qpk;
   if (J.nsplit == 1) {  // single split: normalise and write the heads directly
-    for (int i = tid; i < qpk * hd; i += kThreads) {
-      const int h = i / hd;
-      J.out[(h0 + h) * hd + (i - h * hd)] = acc[i] / s_l[h];
-    }
+    if (warp < qpk)
+#pragma unroll
+      for (int j = 0; j < E; ++j) J.out[(h0 + warp) * hd + lane * E + j] = acc[j] / s_l[warp];
     return ok;
   }
   // partial (m, l, acc) of this split; the last split of the group combines
-  for (int i = tid; i < qpk * (hd + 2); i += kThreads) {
-    const int h = i / (hd + 2), k = i - h * (hd + 2);
-    float *pp = J.part + (static_cast<size_t>(h0 + h) * J.max_splits + J.s) * (hd + 2);
-    pp[k] = k == 0 ? s_m[h] : (k == 1 ? s_l[h] : acc[h * hd + k - 2]);
+  if (warp < qpk) {
+    float *pp = J.part + (static_cast<size_t>(h0 + warp) * J.max_splits + J.s) * (hd + 2);
+    if (lane == 0) {
+      pp[0] = s_m[warp];
+      pp[1] = s_l[warp];
+    }
+#pragma unroll
+    for (int j = 0; j < E; ++j) pp[2 + lane * E + j] = acc[j];
   }
   __threadfence();
   csync();
@@ -904,6 +913,11 @@ __device__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t 
   }
   if (tid == 0) *J.counter = 0;
   return ok;
+}
+
+__device__ __forceinline__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[2],
+                                       unsigned *err) {
+  return J.hd == 64 ? attend_t<2>(J, asmem, bars, uses, err) : attend_t<4>(J, asmem, bars, uses, err);
 }
 
 __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {

@@ -64,6 +64,8 @@ struct PParams {
   unsigned *gbar;       // grid barrier arrival counter, zero at launch
   int rewind_period;    // > 0: SeqLen returns to rewind_base every period steps
   int rewind_base;
+  int phase0;           // 0: a step starts with logits + selection; 1: with the forward
+                        // of the token in DevState (the last phase is then logits)
   unsigned long long *trace;  // optional: [step][phase][cta][kTraceFields], see k_persistent
 };
 
@@ -265,7 +267,7 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   const int n = pos + 1, hd = P.hd;
   const int nsplit = (n + P.split_len - 1) / P.split_len;
   if (item >= P.n_kv * nsplit) return true;
-  const int g = item / nsplit, s = item % nsplit;
+  const int g = item % P.n_kv, s = item / P.n_kv;  // split-major: (g, s) stays on one CTA as n grows
   const size_t head_stride = static_cast<size_t>(P.max_tokens) * hd;
   const size_t off = (static_cast<size_t>(ph.layer) * P.n_kv + g) * head_stride;
   AttnJob J;
@@ -703,8 +705,10 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
     if (tid != kThreads) return;
     uint32_t k = 0;
     bool stopped = false;
-    for (int step = 0; step < P.n_steps && !stopped; ++step) {
-      for (int pi = 0; pi < P.nphase && !stopped; ++pi) {
+    const int total = P.n_steps * P.nphase;
+    for (int kp = 0; kp < total && !stopped; ++kp) {
+      {
+        const int pi = (P.phase0 + kp) % P.nphase;
         build_phase(P, pi, s_pph);
         const PPhase &ph = s_pph;
         if (ph.kind == K_ATTN) continue;
@@ -755,20 +759,28 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   uint32_t abar_uses[2] = {0, 0};
   unsigned bar_target = 0;
   bool ok = true;
-  for (int step = 0; step < P.n_steps && ok; ++step) {
-    for (int pi = 0; pi < P.nphase && ok; ++pi) {
+  if (tid == 0) s_pos = ldst(&st->fwd_pos);  // the forward's position when phase0 == 1
+  if (tid < P.hd && P.phase0 == 1) {
+    const int pos0 = ldst(&st->fwd_pos), half = P.hd / 2;
+    if (pos0 >= 0 && pos0 < P.rope_len)
+      s_rope[tid] = __ldg((tid < half ? P.rope_cos : P.rope_sin) + static_cast<size_t>(pos0) * half + (tid % half));
+  }
+  const int total = P.n_steps * P.nphase;
+  for (int kp = 0; kp < total && ok; ++kp) {
+    {
+      const int step = (P.phase0 + kp) / P.nphase, pi = (P.phase0 + kp) % P.nphase;
       if (tid == 0) build_phase(P, pi, s_ph);
       csync();
       const PPhase &ph = s_ph;
       const long long b0 = P.trace ? clock64() : 0;
-      if (step > 0 || pi > 0) {
+      if (kp > 0) {
         bar_target += 1;
         if (!grid_barrier(P.gbar, bar_target, &st->err, &s_ok)) { ok = false; break; }
       }
       if (pi == 0 && ldst(&st->halted)) { ok = false; break; }
       unsigned long long *tr =
           (P.trace && tid == 0)
-              ? P.trace + ((static_cast<size_t>(step) * P.nphase + pi) * G + c) * kTraceFields
+              ? P.trace + (static_cast<size_t>(kp) * G + c) * kTraceFields
               : nullptr;
       if (tr) {
         const long long b1 = clock64();

@@ -48,6 +48,7 @@ SIGNATURES = {
     "c2s_bench_decode_timed": (I, [P, I, F, I, I, C.POINTER(F)]),
     "c2s_profile_step": (I, [P, I, F, I, P, P]),
     "c2s_trace_decode": (I, [P, I, F, I, P, C.POINTER(I)]),
+    "c2s_decode_launches": (I, [P, I]),
     "c2s_quantize_row_q8_k": (I, [P, P, I]),
     "c2s_gemv": (I, [I, P, P, P, I, I]),
     "c2s_gemv_device": (I, [I, I, P, P, P, I, I]),
@@ -385,3 +386,7 @@ class Engine:
     @property
     def kernels_per_step(self) -> int:
         return load_library().c2s_kernels_per_step(self._h)
+
+    def decode_launches(self, n_steps: int) -> int:
+        """Kernel launches of one bench_decode(_timed) call of n_steps."""
+        return load_library().c2s_decode_launches(self._h, n_steps)

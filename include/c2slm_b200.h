@@ -163,8 +163,13 @@ int c2s_profile_step(c2s_engine *e, int n_steps, float penalty, int window, floa
  * qkv, attention, o-proj, gate/up, down). */
 int c2s_trace_decode(c2s_engine *e, int n_steps, float penalty, int window, uint64_t *trace_out,
                      int *nphase_out);
-/* Number of kernels one decode step launches (for the bench's launch count). */
+/* Number of kernels one decode step launches on the per-phase (CUDA graph)
+ * path (for the bench's launch count). */
 int c2s_kernels_per_step(const c2s_engine *e);
+/* Kernel launches one c2s_bench_decode / c2s_bench_decode_timed call of
+ * n_steps issues: 1 when the persistent decode kernel is in use, else
+ * c2s_kernels_per_step(e) * n_steps.  No counterpart in the reference. */
+int c2s_decode_launches(const c2s_engine *e, int n_steps);
 
 /* ------------------------------------------------------------------------ */
 /* Kernel-level entry points (tensor.* of the reference), host buffers       */
