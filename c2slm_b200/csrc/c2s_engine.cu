@@ -1548,6 +1548,36 @@ int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, i
   return op_finish(c);
 }
 
+// ---------------------------------------------------------------------------
+// c2s_gemv_noalloc: c2s_gemv with every device byte it touches in one
+// file-scope array.  Some callers cannot allocate device memory at the
+// moment they need a matvec: a host whose free HBM is held by another
+// allocator (a framework's caching pool) gets out-of-memory from cudaMalloc
+// although nothing is in use, and a latency-critical loop cannot afford the
+// device-wide synchronisation that cudaFree performs.  This entry point makes
+// neither call: it stages the operands in kNoAllocScratchBytes of statically
+// reserved device memory, runs the same kernel as c2s_gemv on the calling
+// thread's default stream, and copies y back.
+//
+//   - The first call on a device does the set-up (it looks up the array's
+//     device address, which may load this library's device code onto that
+//     device); make that first call before any stream capture.
+//   - Weights + x + y + 1 KB must fit in the array (4 MiB); larger calls are
+//     rejected with C2S_ERR_ARG before any device work.
+//   - The array's first 256 bytes are the kernel's status block, whose error
+//     word must be zero when a call starts: it is zero when the library
+//     loads, and a call that finds it set clears it before returning.
+//     Nothing else needs an initial value (each call writes x and the
+//     weights before the kernel reads them).
+//   - All calls on one device share the array: calls that overlap in time
+//     (from several host threads) race on it and must be serialised by the
+//     caller.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static uint8_t *g_noalloc_base[64];  // device address of the array, per device (set-up done)
+static std::mutex g_noalloc_mu;
+
 int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x, float *d_y, int rows, int cols) {
   if (!d_weight || !d_x || !d_y) return fail(C2S_ERR_ARG, "null argument");
   if (reinterpret_cast<uintptr_t>(d_weight) & 255) return fail(C2S_ERR_ARG, "d_weight must be 256-byte aligned");
@@ -1555,6 +1585,53 @@ int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x
   if (int rc = op_ctx(device, &c)) return rc;
   DeviceGuard g(device);
   return gemv_launch(c, type, d_weight, d_x, d_y, rows, cols, nullptr);
+}
+
+int c2s_gemv_noalloc(int type, const void *weight, const float *x, float *y, int rows, int cols) {
+  if (!weight || !x || !y) return fail(C2S_ERR_ARG, "null argument");
+  if (int rc = check_matrix(type, rows, cols, "gemv_noalloc")) return rc;
+  auto a256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t wb = row_bytes_of(type, cols) * rows;
+  // [status block | x | y | weights], each 256-byte aligned, 64 B of slack after each
+  const size_t off_x = 256, off_y = off_x + a256(static_cast<size_t>(cols) * 4 + 64);
+  const size_t off_w = off_y + a256(static_cast<size_t>(rows) * 4 + 64);
+  const size_t need = off_w + a256(wb + 64);
+  if (need > kNoAllocScratchBytes)
+    return fail(C2S_ERR_ARG, "gemv_noalloc: needs %zu bytes of scratch (weights %zu), the static scratch holds %zu",
+                need, wb, kNoAllocScratchBytes);
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return fail(C2S_ERR_CUDA, "gemv_noalloc: no current CUDA device");
+  uint8_t *base = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_base[dev]) {  // set-up, once per device, with that device current
+      void *p = nullptr;
+      const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (rc != cudaSuccess)
+        return fail(C2S_ERR_CUDA, "gemv_noalloc set-up: cudaGetSymbolAddress: %s", cudaGetErrorString(rc));
+      CK(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      g_noalloc_base[dev] = static_cast<uint8_t *>(p);
+    }
+    base = g_noalloc_base[dev];
+  }
+  OpCtx c;  // no stream or status block is created: both come from the caller / the array
+  c.stream = cudaStreamPerThread;
+  c.st = reinterpret_cast<DevState *>(base);
+  CK(cudaMemcpyAsync(base + off_w, weight, wb, cudaMemcpyHostToDevice, c.stream));
+  CK(cudaMemcpyAsync(base + off_x, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c.stream));
+  if (int rc = gemv_launch(&c, type, base + off_w, reinterpret_cast<const float *>(base + off_x),
+                           reinterpret_cast<float *>(base + off_y), rows, cols, nullptr))
+    return rc;
+  CK(cudaMemcpyAsync(y, base + off_y, static_cast<size_t>(rows) * 4, cudaMemcpyDeviceToHost, c.stream));
+  unsigned err = 0;
+  CK(cudaMemcpyAsync(&err, &c.st->err, sizeof err, cudaMemcpyDeviceToHost, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  if (err) {
+    CK(cudaMemsetAsync(&c.st->err, 0, sizeof(unsigned), c.stream));
+    CK(cudaStreamSynchronize(c.stream));
+    return fail(C2S_ERR_TIMEOUT, "gemv_noalloc: device reported error flags 0x%x", err);
+  }
+  return C2S_OK;
 }
 
 int c2s_kquant_partials(int type, const void *weight, const float *x, int32_t *dots, int rows, int cols) {

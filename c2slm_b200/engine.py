@@ -51,6 +51,7 @@ SIGNATURES = {
     "c2s_decode_launches": (I, [P, I]),
     "c2s_quantize_row_q8_k": (I, [P, P, I]),
     "c2s_gemv": (I, [I, P, P, P, I, I]),
+    "c2s_gemv_noalloc": (I, [I, P, P, P, I, I]),
     "c2s_gemv_device": (I, [I, I, P, P, P, I, I]),
     "c2s_kquant_partials": (I, [I, P, P, P, I, I]),
     "c2s_dot_rows_f32x": (I, [I, P, P, P, I, P, I, I]),
@@ -133,6 +134,15 @@ def gemv(kind: int, w, x, rows: int, cols: int) -> np.ndarray:
     w, x = _u8(w), _f32(x)
     y = np.zeros(rows, np.float32)
     _check(load_library().c2s_gemv(kind, _ptr(w), _ptr(x), _ptr(y), rows, cols))
+    return y
+
+
+def gemv_noalloc(kind: int, w, x, rows: int, cols: int) -> np.ndarray:
+    """c2s_gemv with the operands staged in the library's static device array
+    (no device allocation or free); see c2s_gemv_noalloc in the header."""
+    w, x = _u8(w), _f32(x)
+    y = np.zeros(rows, np.float32)
+    _check(load_library().c2s_gemv_noalloc(kind, _ptr(w), _ptr(x), _ptr(y), rows, cols))
     return y
 
 

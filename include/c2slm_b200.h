@@ -190,6 +190,18 @@ int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, i
 int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x, float *d_y,
                     int rows, int cols);
 
+/* c2s_gemv without any device allocation or free, for callers that cannot
+ * allocate when they need the matvec (device memory held by another
+ * allocator; loops that must not take cudaFree's device-wide
+ * synchronisation).  The operands are staged in a 4 MiB statically reserved
+ * device array: weights + x + y + 1 KB must fit, larger calls return
+ * C2S_ERR_ARG.  Runs on the calling thread's default stream and returns when
+ * y is written.  The first call on a device does the set-up and should come
+ * before any stream capture; calls on one device share the array and must
+ * not overlap.  No counterpart in the reference (its GEMV runs on host
+ * memory, engine/model.go:250). */
+int c2s_gemv_noalloc(int type, const void *weight, const float *x, float *y, int rows, int cols);
+
 /* Integer partials of the K-quant x Q8_K dots, computed by the same device
  * code as c2s_gemv (bit-exact contract):
  *   Q4_K: dots[(r*nsb + sb)*8 + 2j + {0,1}] = sub-block dot (lo, hi nibbles)
