@@ -6,7 +6,9 @@
 // arena; a decode step is a CUDA graph of 5 kernels per layer plus one logits
 // kernel, chained with programmatic dependent launch.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <fcntl.h>
+#include <nccl.h>  // types only: the library is loaded with dlopen when a tensor-parallel engine is created
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -98,6 +100,22 @@ cudaError_t launch(void (*kernel)(P), dim3 grid, dim3 block, size_t smem, cudaSt
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+// same, for kernels with several arguments
+template <class... KArgs, class... Args>
+cudaError_t launchv(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_use_pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 // shared-memory layout of one k_matvec launch
@@ -343,6 +361,70 @@ struct HostFwdIn {
   int token, pos, commit;
 };
 
+// Tensor-parallel shard of one rank (one GPU): query heads [h0, h1) in units
+// of whole 256-column superblocks of attn_output's input (pairs of heads at
+// head_dim 128), the kv heads [g0, g1) they use, FFN rows [f0, f1) in
+// superblocks of 256, vocabulary rows [v0, v1) of an even split padded to
+// vpad rows per rank.  One GPU: the whole model.
+struct TpPlan {
+  int rank = 0, world = 1;
+  int h0 = 0, h1 = 0, g0 = 0, g1 = 0, f0 = 0, f1 = 0, v0 = 0, v1 = 0, vpad = 0;
+};
+
+int tp_plan(const c2s_model_desc &d, int rank, int world, TpPlan &p, std::string &why) {
+  p = TpPlan{};
+  p.rank = rank;
+  p.world = world;
+  const int hd = d.head_dim > 0 ? d.head_dim : d.embd / d.n_heads;
+  const int qpk = d.n_heads / d.n_kv_heads;
+  if (world <= 1) {
+    p.h1 = d.n_heads;
+    p.g1 = d.n_kv_heads;
+    p.f1 = d.ffn / 256;
+    p.v1 = p.vpad = d.vocab;
+    return 0;
+  }
+  if (hd <= 0 || 256 % hd != 0 || d.n_heads % (256 / hd) != 0) {
+    why = "tensor parallel: heads must group into 256-column superblocks";
+    return -1;
+  }
+  if (d.ffn % 256) {
+    why = "tensor parallel: ffn must be a multiple of 256";
+    return -1;
+  }
+  auto split = [](int n, int parts, int r, int &a, int &b) {  // first n % parts parts get one more
+    const int q = n / parts, m = n % parts;
+    a = r * q + std::min(r, m);
+    b = a + q + (r < m ? 1 : 0);
+  };
+  const int upb = 256 / hd, units = d.n_heads / upb;
+  if (units < world || d.ffn / 256 < world) {
+    why = "tensor parallel: fewer head groups or FFN superblocks than ranks";
+    return -1;
+  }
+  int u0, u1;
+  split(units, world, rank, u0, u1);
+  p.h0 = u0 * upb;
+  p.h1 = u1 * upb;
+  p.g0 = p.h0 / qpk;
+  p.g1 = (p.h1 + qpk - 1) / qpk;
+  split(d.ffn / 256, world, rank, p.f0, p.f1);
+  p.vpad = (d.vocab + world - 1) / world;
+  p.v0 = std::min(d.vocab, rank * p.vpad);
+  p.v1 = std::min(d.vocab, p.v0 + p.vpad);
+  return 0;
+}
+
+// NCCL entry points, resolved from libnccl.so.2 at first use
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_id = nullptr;
+  decltype(&ncclCommInitRank) init_rank = nullptr;
+  decltype(&ncclCommDestroy) destroy = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclGetErrorString) err_str = nullptr;
+};
+
 struct c2s_engine {
   int device = 0;
   int num_sms = 148;
@@ -382,6 +464,11 @@ struct c2s_engine {
   PParams pp{};
   size_t p_smem = 0;
   bool use_persistent = true;
+  // tensor parallel (world > 1)
+  TpPlan plan;
+  ncclComm_t comm = nullptr;
+  float *delta = nullptr;        // this rank's partial o-proj / down output, allreduced in place
+  float *logits_full = nullptr;  // gathered logits [world * vpad]
 };
 
 namespace {
@@ -398,6 +485,34 @@ struct DeviceGuard {
     if (prev >= 0 && cur != prev) cudaSetDevice(prev);
   }
 };
+
+// libnccl.so.2 is opened on the first tensor-parallel call only; a process
+// that already loaded it (e.g. through torch.distributed) shares that copy.
+int nccl_api(const NcclApi **out) {
+  static NcclApi api;
+  static std::string why;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      why = dlerror() ? dlerror() : "dlopen(libnccl.so.2) failed";
+      return;
+    }
+    api.get_id = reinterpret_cast<decltype(api.get_id)>(dlsym(h, "ncclGetUniqueId"));
+    api.init_rank = reinterpret_cast<decltype(api.init_rank)>(dlsym(h, "ncclCommInitRank"));
+    api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.err_str = reinterpret_cast<decltype(api.err_str)>(dlsym(h, "ncclGetErrorString"));
+    if (!api.get_id || !api.init_rank || !api.destroy || !api.all_reduce || !api.all_gather || !api.err_str) {
+      why = "libnccl.so.2 lacks an expected symbol";
+      api = NcclApi{};
+    }
+  });
+  if (!api.get_id) return fail(C2S_ERR_UNSUPPORTED, "NCCL unavailable: %s", why.c_str());
+  *out = &api;
+  return C2S_OK;
+}
 
 const c2s_tensor_desc *find_t(const c2s_tensor_desc *ts, int n, const std::string &name) {
   for (int i = 0; i < n; ++i)
@@ -438,9 +553,28 @@ cudaError_t mark(KTimer *t, cudaStream_t s, int kind) {
   return cudaEventRecord(ev, s);
 }
 
+// allreduce (sum) of this rank's partial in e->delta, then X += delta on every
+// rank (and the commit of the forwarded token after the last layer)
+cudaError_t enqueue_tp_reduce(c2s_engine *e, cudaStream_t s, bool commit_here, bool check_halt) {
+  const NcclApi *nc = nullptr;
+  if (nccl_api(&nc)) return cudaErrorUnknown;
+  const ncclResult_t r = nc->all_reduce(e->delta, e->delta, e->d.embd, ncclFloat32, ncclSum, e->comm, s);
+  if (r != ncclSuccess) {
+    fail(C2S_ERR_CUDA, "ncclAllReduce: %s", nc->err_str(r));
+    return cudaErrorUnknown;
+  }
+  const int blocks = (e->d.embd + kThreads - 1) / kThreads;
+  return launchv(k_residual_add, dim3(blocks), dim3(kThreads), 0, s, e->X, static_cast<const float *>(e->delta),
+                e->d.embd, e->st, e->token_ids, commit_here ? 1 : 0, check_halt ? 1 : 0);
+}
+
 cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool final_norm, KTimer *tm = nullptr) {
-  const int L = e->d.n_layers, H = e->d.embd, F = e->d.ffn, hd = e->d.head_dim;
-  const int kvd = e->d.n_kv_heads * hd;
+  const int L = e->d.n_layers, H = e->d.embd, hd = e->d.head_dim;
+  const TpPlan &pl = e->plan;
+  const bool tp = pl.world > 1;
+  // this rank's rows: query heads, kv heads, FFN (the whole model on one GPU)
+  const int nq = (pl.h1 - pl.h0) * hd, kvd = (pl.g1 - pl.g0) * hd;
+  const int F = tp ? (pl.f1 - pl.f0) * 256 : e->d.ffn;
   const int G = e->num_sms;
   cudaError_t err = cudaSuccess;
   for (int l = 0; l < L && err == cudaSuccess; ++l) {
@@ -450,7 +584,7 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     P.kind = K_QKV;
     P.nseg = 3;
     P.cols = H;
-    P.seg[0] = make_seg(Ld.q, Ld.tq, H, H, Ld.qb, e->q);
+    P.seg[0] = make_seg(Ld.q, Ld.tq, nq, H, Ld.qb, e->q);
     P.seg[1] = make_seg(Ld.k, Ld.tk, kvd, H, Ld.kb, e->k);
     P.seg[2] = make_seg(Ld.v, Ld.tv, kvd, H, Ld.vb, e->v);
     P.norm_w = Ld.attn_norm;
@@ -467,7 +601,11 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     AttnParams A{};
     A.layer = l;
     A.n_heads = e->d.n_heads;
-    A.n_kv = e->d.n_kv_heads;
+    A.n_kv = pl.g1 - pl.g0;
+    A.qpk = e->d.n_heads / e->d.n_kv_heads;
+    A.tp_h0 = pl.h0;
+    A.tp_h1 = pl.h1;
+    A.tp_g0 = pl.g0;
     A.hd = hd;
     A.max_tokens = e->d.max_tokens;
     A.max_splits = e->max_splits;
@@ -477,7 +615,7 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     A.q = e->q;
     A.k = e->k;
     A.v = e->v;
-    const size_t plane = static_cast<size_t>(L) * e->d.n_kv_heads * e->d.max_tokens * hd;
+    const size_t plane = static_cast<size_t>(L) * (pl.g1 - pl.g0) * e->d.max_tokens * hd;
     A.kcache = e->kv;
     A.vcache = e->kv + plane;
     A.rope_cos = e->rope_cos;
@@ -490,19 +628,20 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     A.check_halt = check_halt;
     A.split_len = e->split_len;
     if ((err = mark(tm, s, -1))) break;
-    err = launch(k_attention, dim3(e->d.n_kv_heads, e->max_splits), dim3(kThreads), e->attn_smem, s, A);
+    err = launch(k_attention, dim3(pl.g1 - pl.g0, e->max_splits), dim3(kThreads), e->attn_smem, s, A);
     if (err || (err = mark(tm, s, 7))) break;
-    // o_proj + residual
+    // o_proj + residual (tensor parallel: this rank's heads' columns, then an allreduce)
     P = MatParams{};
-    P.kind = K_OPROJ;
+    P.kind = tp ? K_RAW : K_OPROJ;
     P.nseg = 1;
-    P.cols = e->d.n_heads * hd;
-    P.seg[0] = make_seg(Ld.o, Ld.to, H, e->d.n_heads * hd, nullptr, e->X);
+    P.cols = nq;
+    P.seg[0] = make_seg(Ld.o, Ld.to, H, nq, nullptr, tp ? e->delta : e->X);
     P.x_in = e->attn_out;
     P.check_halt = check_halt;
     matvec_params_common(e, P);
     if ((err = mark(tm, s, -1))) break;
     err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
+    if (!err && tp) err = enqueue_tp_reduce(e, s, false, check_halt);
     if (err || (err = mark(tm, s, K_OPROJ))) break;
     // gate/up + SwiGLU
     P = MatParams{};
@@ -518,18 +657,20 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     if ((err = mark(tm, s, -1))) break;
     err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
     if (err || (err = mark(tm, s, K_FFN_UP))) break;
-    // down + residual (+ commit on the last layer)
+    // down + residual (+ commit on the last layer); tensor parallel: this
+    // rank's FFN columns, then an allreduce
     P = MatParams{};
-    P.kind = K_FFN_DOWN;
+    P.kind = tp ? K_RAW : K_FFN_DOWN;
     P.nseg = 1;
     P.cols = F;
-    P.seg[0] = make_seg(Ld.down, Ld.tdown, H, F, nullptr, e->X);
+    P.seg[0] = make_seg(Ld.down, Ld.tdown, H, F, nullptr, tp ? e->delta : e->X);
     P.x_in = e->h;
     P.commit_here = (l == L - 1);
     P.check_halt = check_halt;
     matvec_params_common(e, P);
     if ((err = mark(tm, s, -1))) break;
     err = launch(k_matvec, dim3(G), dim3(kThreads), P.smem_bytes, s, P);
+    if (!err && tp) err = enqueue_tp_reduce(e, s, l == L - 1, check_halt);
     if (err || (err = mark(tm, s, K_FFN_DOWN))) break;
   }
   if (err == cudaSuccess && final_norm) {
@@ -548,19 +689,38 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
 
 cudaError_t enqueue_logits(c2s_engine *e, cudaStream_t s, bool select, bool from_normx, bool check_halt,
                            KTimer *tm = nullptr) {
+  const TpPlan &pl = e->plan;
+  const bool tp = pl.world > 1;
   MatParams P{};
   P.kind = K_LOGITS;
   P.nseg = 1;
   P.cols = e->d.embd;
-  P.seg[0] = make_seg(e->output, e->out_type, e->d.vocab, e->d.embd, nullptr, e->logits);
+  P.seg[0] = make_seg(e->output, e->out_type, pl.v1 - pl.v0, e->d.embd, nullptr, e->logits);
   P.norm_w = e->out_norm;
   P.x_in = from_normx ? e->normx : nullptr;
   P.normx_out = from_normx ? nullptr : e->normx;
-  P.select = select;
+  P.select = select && !tp;
   P.check_halt = check_halt;
   matvec_params_common(e, P);
   cudaError_t err = mark(tm, s, -1);
   if (!err) err = launch(k_matvec, dim3(e->num_sms), dim3(kThreads), P.smem_bytes, s, P);
+  if (!err && tp) {
+    // every rank gathers the whole vocabulary (rows of rank r at r * vpad),
+    // then selects from it with the same rules: identical ids on all ranks
+    const NcclApi *nc = nullptr;
+    if (nccl_api(&nc)) return cudaErrorUnknown;
+    const ncclResult_t r = nc->all_gather(e->logits, e->logits_full, pl.vpad, ncclFloat32, e->comm, s);
+    if (r != ncclSuccess) {
+      fail(C2S_ERR_CUDA, "ncclAllGather: %s", nc->err_str(r));
+      return cudaErrorUnknown;
+    }
+    if (select) {
+      const size_t smem = (static_cast<size_t>(e->d.vocab) / e->num_sms + 2) * 4;
+      err = launchv(k_select, dim3(e->num_sms), dim3(kThreads), smem, s, static_cast<const float *>(e->logits_full),
+                   e->d.vocab, e->st, static_cast<const int *>(e->token_ids), e->out_tokens, e->amax_part,
+                   check_halt ? 1 : 0);
+    }
+  }
   if (!err) err = mark(tm, s, K_LOGITS);
   return err;
 }
@@ -846,10 +1006,19 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   if (!on) return fail(C2S_ERR_FORMAT, "missing output_norm.weight");
   const c2s_tensor_desc *ow = find_t(ts, n, "output.weight");
   if (!ow) ow = te;  // tied fallback (engine/model.go:126-130)
-  const int H = d.embd, F = d.ffn, hd = d.head_dim, kvd = d.n_kv_heads * hd;
+  const int H = d.embd, hd = d.head_dim;
   if (d.n_heads * hd != H) return fail(C2S_ERR_UNSUPPORTED, "n_heads*head_dim != embd");
   if (H % 256 && (is_kquant(te->type))) return fail(C2S_ERR_UNSUPPORTED, "embedding type needs embd %% 256 == 0");
-  if (int rc = check_matrix(ow->type, d.vocab, H, "output")) return rc;
+  if (e->plan.world <= 1) {
+    std::string why;
+    tp_plan(d, 0, 1, e->plan, why);
+  }
+  const TpPlan &pl = e->plan;
+  // this engine's rows (tensor parallel: the rank's shard; else the model)
+  const int nq = (pl.h1 - pl.h0) * hd, kvd = (pl.g1 - pl.g0) * hd;
+  const int F = pl.world > 1 ? (pl.f1 - pl.f0) * 256 : d.ffn;
+  const int V = pl.v1 - pl.v0;
+  if (int rc = check_matrix(ow->type, V, H, "output")) return rc;
   if (!(te->type == T_Q8_0 || te->type == T_Q5_0 || te->type == T_Q4_K || te->type == T_Q6_K || te->type == T_F32))
     return fail(C2S_ERR_UNSUPPORTED, "token_embd type %d", te->type);
   if (H > 16384 || F > 65536) return fail(C2S_ERR_UNSUPPORTED, "dimensions too large");
@@ -887,13 +1056,13 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
     if (!an || !q || !k || !v || !o || !fn || !g || !u || !dn)
       return fail(C2S_ERR_FORMAT, "blk.%d is missing a projection or norm tensor", l);
     int rc;
-    if ((rc = check_matrix(q->type, H, H, "attn_q")) || (rc = check_matrix(k->type, kvd, H, "attn_k")) ||
-        (rc = check_matrix(v->type, kvd, H, "attn_v")) || (rc = check_matrix(o->type, H, H, "attn_output")) ||
+    if ((rc = check_matrix(q->type, nq, H, "attn_q")) || (rc = check_matrix(k->type, kvd, H, "attn_k")) ||
+        (rc = check_matrix(v->type, kvd, H, "attn_v")) || (rc = check_matrix(o->type, H, nq, "attn_output")) ||
         (rc = check_matrix(g->type, F, H, "ffn_gate")) || (rc = check_matrix(u->type, F, H, "ffn_up")) ||
         (rc = check_matrix(dn->type, H, F, "ffn_down")))
       return rc;
-    if (t_cols(q) != H || t_rows(q) != H || t_cols(k) != H || t_rows(k) != kvd || t_cols(v) != H ||
-        t_rows(v) != kvd || t_cols(o) != H || t_rows(o) != H || t_cols(g) != H || t_rows(g) != F ||
+    if (t_cols(q) != H || t_rows(q) != nq || t_cols(k) != H || t_rows(k) != kvd || t_cols(v) != H ||
+        t_rows(v) != kvd || t_cols(o) != nq || t_rows(o) != H || t_cols(g) != H || t_rows(g) != F ||
         t_cols(u) != H || t_rows(u) != F || t_cols(dn) != F || t_rows(dn) != H)
       return fail(C2S_ERR_FORMAT, "blk.%d tensor shapes do not match the hyper-parameters", l);
     LOff &x = lo[l];
@@ -903,7 +1072,7 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
     const c2s_tensor_desc *qb = T("attn_q.bias"), *kb = T("attn_k.bias"), *vb = T("attn_v.bias");
     const c2s_tensor_desc *qn = T("attn_q_norm.weight"), *kn = T("attn_k_norm.weight");
     x.hqb = qb; x.hkb = kb; x.hvb = vb; x.hqn = qn; x.hkn = kn;
-    if (qb) { if (qb->nbytes < static_cast<uint64_t>(H) * 4) return fail(C2S_ERR_FORMAT, "attn_q.bias too short"); x.qb = add(qb); }
+    if (qb) { if (qb->nbytes < static_cast<uint64_t>(nq) * 4) return fail(C2S_ERR_FORMAT, "attn_q.bias too short"); x.qb = add(qb); }
     if (kb) { if (kb->nbytes < static_cast<uint64_t>(kvd) * 4) return fail(C2S_ERR_FORMAT, "attn_k.bias too short"); x.kb = add(kb); }
     if (vb) { if (vb->nbytes < static_cast<uint64_t>(kvd) * 4) return fail(C2S_ERR_FORMAT, "attn_v.bias too short"); x.vb = add(vb); }
     if (qn) x.qn = add(qn);
@@ -958,8 +1127,9 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
     CK(cudaMemcpy(e->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(e->rope_sin, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
   }
-  // KV cache [2][L][KVH][max_tokens][hd] fp32 (engine/kvcache.go:31)
-  const size_t kvn = static_cast<size_t>(2) * d.n_layers * d.n_kv_heads * d.max_tokens * hd;
+  // KV cache [2][L][KVH][max_tokens][hd] fp32 (engine/kvcache.go:31); a
+  // tensor-parallel rank keeps its kv heads only
+  const size_t kvn = static_cast<size_t>(2) * d.n_layers * (pl.g1 - pl.g0) * d.max_tokens * hd;
   if (cudaMalloc(&e->kv, kvn * 4) != cudaSuccess) return fail(C2S_ERR_OOM, "KV cache: cudaMalloc(%zu) failed", kvn * 4);
   CK(cudaMemset(e->kv, 0, kvn * 4));
   e->max_splits = std::max(1, std::min(kMaxSplits, e->num_sms / d.n_kv_heads));
@@ -999,6 +1169,17 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
       (rc = dalloc(reinterpret_cast<void **>(&e->scratch_x), static_cast<size_t>(d.vocab) * 4)) ||
       (rc = dalloc(reinterpret_cast<void **>(&e->st), sizeof(DevState))))
     return rc;
+  if (pl.world > 1) {
+    if ((rc = dalloc(reinterpret_cast<void **>(&e->delta), static_cast<size_t>(H) * 4 + 64)) ||
+        (rc = dalloc(reinterpret_cast<void **>(&e->logits_full),
+                     static_cast<size_t>(pl.world) * pl.vpad * 4 + 64)))
+      return rc;
+    // rows past this rank's share of the padded split never win the argmax
+    if (V < pl.vpad) {
+      std::vector<float> ninf(static_cast<size_t>(pl.vpad - V), -INFINITY);
+      CK(cudaMemcpy(e->logits + V, ninf.data(), ninf.size() * 4, cudaMemcpyHostToDevice));
+    }
+  }
   CK(cudaMallocHost(&e->h_in, sizeof(HostFwdIn) * (d.max_tokens + 8)));
   CK(cudaMallocHost(&e->h_buf, static_cast<size_t>(std::max(d.vocab, H)) * 4 + 64));
   CK(cudaMallocHost(&e->h_st, sizeof(DevState)));
@@ -1030,8 +1211,90 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
       return rc;
   }
   e->kernels_per_step = 5 * d.n_layers + 1;
-  if ((rc = persistent_setup(e))) return rc;
+  if (pl.world > 1) {
+    e->kernels_per_step = 7 * d.n_layers + 2;  // + a residual add after each allreduce, + selection
+    e->use_persistent = false;                 // collectives run between per-phase kernels
+  } else if ((rc = persistent_setup(e))) {
+    return rc;
+  }
   CK(cudaStreamSynchronize(e->stream));
+  return C2S_OK;
+}
+
+// Copies of the tensors one tensor-parallel rank holds: rows of attn_q /
+// attn_k / attn_v (+ biases), ffn_gate / ffn_up and the output projection
+// (the tied token_embd serves as output.weight), columns of attn_output and
+// ffn_down (whole blocks of every row).  Row slices point into the caller's
+// memory; column slices are gathered into `own`.
+int tp_slice(const c2s_model_desc &d, const TpPlan &pl, const c2s_tensor_desc *ts, int n,
+             std::vector<c2s_tensor_desc> &out, std::vector<std::vector<uint8_t>> &own,
+             std::vector<std::string> &names) {
+  const int hd = d.head_dim;
+  out.clear();
+  own.clear();
+  names.clear();
+  names.reserve(static_cast<size_t>(n) + 1);
+  auto rows = [&](const c2s_tensor_desc &t, int64_t r0, int64_t r1) -> int {
+    const bool vec = t.n_dims < 2;  // a bias: its elements are the rows
+    const int64_t cols = vec ? 1 : t_cols(&t), nr = vec ? t.dims[0] : t_rows(&t);
+    if (vec && t.type != T_F32) return fail(C2S_ERR_FORMAT, "%s: 1-D tensor of type %d", t.name, t.type);
+    const size_t rb = t.type == T_F32 ? static_cast<size_t>(cols) * 4 : row_bytes_of(t.type, cols);
+    if (r1 > nr || r0 < 0 || r0 > r1) return fail(C2S_ERR_FORMAT, "%s: rows %lld..%lld of %lld", t.name, (long long)r0, (long long)r1, (long long)nr);
+    c2s_tensor_desc c = t;
+    c.data = static_cast<const uint8_t *>(t.data) + static_cast<size_t>(r0) * rb;
+    c.nbytes = static_cast<uint64_t>(r1 - r0) * rb;
+    if (t.n_dims >= 2) c.dims[1] = r1 - r0; else c.dims[0] = r1 - r0;
+    out.push_back(c);
+    return C2S_OK;
+  };
+  auto cols = [&](const c2s_tensor_desc &t, int64_t c0, int64_t c1) -> int {
+    const int64_t nc = t_cols(&t), nr = t_rows(&t);
+    const int blk = is_kquant(t.type) ? 256 : 32;
+    const size_t bb = row_bytes_of(t.type, blk);
+    if (!(is_kquant(t.type) || is_f32x(t.type)) || c0 % blk || c1 % blk || c1 > nc)
+      return fail(C2S_ERR_UNSUPPORTED, "%s: column slice %lld..%lld of type %d", t.name, (long long)c0, (long long)c1, t.type);
+    const size_t rb = row_bytes_of(t.type, nc), sb = static_cast<size_t>((c1 - c0) / blk) * bb;
+    own.emplace_back(static_cast<size_t>(nr) * sb);
+    std::vector<uint8_t> &buf = own.back();
+    const uint8_t *src = static_cast<const uint8_t *>(t.data);
+    for (int64_t r = 0; r < nr; ++r)
+      memcpy(buf.data() + r * sb, src + r * rb + static_cast<size_t>(c0 / blk) * bb, sb);
+    c2s_tensor_desc c = t;
+    c.data = buf.data();
+    c.nbytes = buf.size();
+    c.dims[0] = c1 - c0;
+    out.push_back(c);
+    return C2S_OK;
+  };
+  own.reserve(static_cast<size_t>(2 * d.n_layers) + 1);
+  bool has_output = false;
+  for (int i = 0; i < n; ++i) {
+    const c2s_tensor_desc &t = ts[i];
+    const std::string nm = t.name ? t.name : "";
+    auto ends = [&](const char *suf) {
+      const size_t k = strlen(suf);
+      return nm.size() >= k && nm.compare(nm.size() - k, k, suf) == 0;
+    };
+    int rc = C2S_OK;
+    if (ends(".attn_q.weight") || ends(".attn_q.bias")) rc = rows(t, int64_t(pl.h0) * hd, int64_t(pl.h1) * hd);
+    else if (ends(".attn_k.weight") || ends(".attn_k.bias") || ends(".attn_v.weight") || ends(".attn_v.bias"))
+      rc = rows(t, int64_t(pl.g0) * hd, int64_t(pl.g1) * hd);
+    else if (ends(".attn_output.weight")) rc = cols(t, int64_t(pl.h0) * hd, int64_t(pl.h1) * hd);
+    else if (ends(".ffn_gate.weight") || ends(".ffn_up.weight")) rc = rows(t, int64_t(pl.f0) * 256, int64_t(pl.f1) * 256);
+    else if (ends(".ffn_down.weight")) rc = cols(t, int64_t(pl.f0) * 256, int64_t(pl.f1) * 256);
+    else if (nm == "output.weight") {
+      rc = rows(t, pl.v0, pl.v1);
+      has_output = true;
+    } else out.push_back(t);
+    if (rc) return rc;
+  }
+  if (!has_output) {  // tied embeddings: the rank's vocabulary rows of token_embd project the logits
+    const c2s_tensor_desc *te = find_t(ts, n, "token_embd.weight");
+    if (!te) return fail(C2S_ERR_FORMAT, "missing token_embd.weight");
+    if (int rc = rows(*te, pl.v0, pl.v1)) return rc;
+    names.push_back("output.weight");
+    out.back().name = names.back().c_str();
+  }
   return C2S_OK;
 }
 
@@ -1048,8 +1311,13 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->part), static_cast<void *>(e->amax_part), static_cast<void *>(e->token_ids),
                   static_cast<void *>(e->out_tokens), static_cast<void *>(e->rows_idx),
                   static_cast<void *>(e->scratch_x), static_cast<void *>(e->st),
-                  static_cast<void *>(e->gbar)})
+                  static_cast<void *>(e->gbar), static_cast<void *>(e->delta),
+                  static_cast<void *>(e->logits_full)})
     if (p) cudaFree(p);
+  if (e->comm) {
+    const NcclApi *nc = nullptr;
+    if (nccl_api(&nc) == C2S_OK) nc->destroy(e->comm);
+  }
   for (void *p : {static_cast<void *>(e->h_in), static_cast<void *>(e->h_buf), static_cast<void *>(e->h_st),
                   static_cast<void *>(e->h_tokens)})
     if (p) cudaFreeHost(p);
@@ -1163,12 +1431,10 @@ int c2s_engine_create(const c2s_model_desc *desc, const c2s_tensor_desc *tensors
   return C2S_OK;
 }
 
-int c2s_engine_open(const char *path, int device, int max_tokens, c2s_engine **out) {
-  if (!path || !out) return fail(C2S_ERR_ARG, "null argument");
-  std::unique_ptr<GFile> f;
-  if (int rc = gguf_open(path, f)) return rc;
+// hyper-parameters and tensor table of an opened GGUF, as engine.LoadModel reads them
+static void gguf_descs(GFile *f, int max_tokens, c2s_model_desc &d, std::vector<c2s_tensor_desc> &ts) {
   // engine/model.go:64-112: qwen2.* keys, then qwen3.*, then defaults
-  c2s_model_desc d{};
+  d = c2s_model_desc{};
   uint32_t u;
   auto hp = [&](const char *k2, const char *k3, int dflt) {
     u = 0;
@@ -1193,7 +1459,7 @@ int c2s_engine_open(const char *path, int device, int max_tokens, c2s_engine **o
   d.max_tokens = max_tokens > 0 ? max_tokens : kMaxContext;
   d.im_end = f->im_end;
   d.eos = f->eos;
-  std::vector<c2s_tensor_desc> ts(f->tensors.size());
+  ts.assign(f->tensors.size(), c2s_tensor_desc{});
   for (size_t i = 0; i < ts.size(); ++i) {
     const GTensor &t = f->tensors[i];
     ts[i].name = t.name.c_str();
@@ -1203,7 +1469,101 @@ int c2s_engine_open(const char *path, int device, int max_tokens, c2s_engine **o
     ts[i].data = t.data;
     ts[i].nbytes = t.nbytes;
   }
+}
+
+int c2s_engine_open(const char *path, int device, int max_tokens, c2s_engine **out) {
+  if (!path || !out) return fail(C2S_ERR_ARG, "null argument");
+  std::unique_ptr<GFile> f;
+  if (int rc = gguf_open(path, f)) return rc;
+  c2s_model_desc d;
+  std::vector<c2s_tensor_desc> ts;
+  gguf_descs(f.get(), max_tokens, d, ts);
   return c2s_engine_create(&d, ts.data(), static_cast<int>(ts.size()), device, out);
+}
+
+int c2s_engine_open_tp(const char *path, int device, int max_tokens, int rank, int world, const uint8_t *nccl_id,
+                       c2s_engine **out) {
+  if (!path || !out) return fail(C2S_ERR_ARG, "null argument");
+  std::unique_ptr<GFile> f;
+  if (int rc = gguf_open(path, f)) return rc;
+  c2s_model_desc d;
+  std::vector<c2s_tensor_desc> ts;
+  gguf_descs(f.get(), max_tokens, d, ts);
+  return c2s_engine_create_tp(&d, ts.data(), static_cast<int>(ts.size()), device, rank, world, nccl_id, out);
+}
+
+int c2s_nccl_unique_id(uint8_t *id_out) {
+  if (!id_out) return fail(C2S_ERR_ARG, "null argument");
+  const NcclApi *nc = nullptr;
+  if (int rc = nccl_api(&nc)) return rc;
+  ncclUniqueId id;
+  const ncclResult_t r = nc->get_id(&id);
+  if (r != ncclSuccess) return fail(C2S_ERR_CUDA, "ncclGetUniqueId: %s", nc->err_str(r));
+  static_assert(sizeof(ncclUniqueId) == C2S_NCCL_ID_BYTES, "NCCL unique id size");
+  memcpy(id_out, &id, sizeof id);
+  return C2S_OK;
+}
+
+int c2s_tp_plan(const c2s_model_desc *desc, int rank, int world, int32_t *plan_out) {
+  if (!desc || !plan_out) return fail(C2S_ERR_ARG, "null argument");
+  if (world < 1 || rank < 0 || rank >= world) return fail(C2S_ERR_ARG, "rank %d of %d", rank, world);
+  c2s_model_desc d = *desc;
+  if (d.head_dim <= 0 && d.n_heads > 0) d.head_dim = d.embd / d.n_heads;
+  if (d.n_heads <= 0 || d.n_kv_heads <= 0 || d.n_heads % d.n_kv_heads || d.vocab <= 0)
+    return fail(C2S_ERR_ARG, "model desc: heads / vocab");
+  TpPlan p;
+  std::string why;
+  if (tp_plan(d, rank, world, p, why)) return fail(C2S_ERR_UNSUPPORTED, "%s", why.c_str());
+  const int32_t v[9] = {p.h0, p.h1, p.g0, p.g1, p.f0, p.f1, p.v0, p.v1, p.vpad};
+  memcpy(plan_out, v, sizeof v);
+  return C2S_OK;
+}
+
+int c2s_engine_create_tp(const c2s_model_desc *desc, const c2s_tensor_desc *tensors, int n_tensors, int device,
+                         int rank, int world, const uint8_t *nccl_id, c2s_engine **out) {
+  if (!desc || !tensors || n_tensors <= 0 || !out || !nccl_id) return fail(C2S_ERR_ARG, "null argument");
+  if (world < 2 || rank < 0 || rank >= world) return fail(C2S_ERR_ARG, "rank %d of world %d", rank, world);
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(C2S_ERR_CUDA, "no CUDA device");
+  if (device < 0 || device >= ndev) return fail(C2S_ERR_ARG, "device %d of %d", device, ndev);
+  // the dimensions LoadModel derives (engine/model.go:118,137)
+  c2s_model_desc d = *desc;
+  if (d.n_heads <= 0 || d.n_kv_heads <= 0 || d.embd <= 0) return fail(C2S_ERR_ARG, "model desc: non-positive dimension");
+  if (d.head_dim <= 0) d.head_dim = d.embd / d.n_heads;
+  const c2s_tensor_desc *te = find_t(tensors, n_tensors, "token_embd.weight");
+  if (!te || te->n_dims < 2) return fail(C2S_ERR_FORMAT, "missing token_embd.weight");
+  if (d.vocab <= 0) d.vocab = static_cast<int32_t>(t_rows(te));
+  TpPlan plan;
+  std::string why;
+  if (tp_plan(d, rank, world, plan, why)) return fail(C2S_ERR_UNSUPPORTED, "%s", why.c_str());
+  std::vector<c2s_tensor_desc> shard;
+  std::vector<std::vector<uint8_t>> own;
+  std::vector<std::string> names;
+  if (int rc = tp_slice(d, plan, tensors, n_tensors, shard, own, names)) return rc;
+  const NcclApi *nc = nullptr;
+  if (int rc = nccl_api(&nc)) return rc;
+  DeviceGuard g(device);
+  auto *e = new c2s_engine();
+  e->device = device;
+  e->plan = plan;
+  ncclUniqueId id;
+  memcpy(&id, nccl_id, sizeof id);
+  const ncclResult_t r = nc->init_rank(&e->comm, world, id, rank);
+  if (r != ncclSuccess) {
+    e->comm = nullptr;
+    engine_free(e);
+    return fail(C2S_ERR_CUDA, "ncclCommInitRank: %s", nc->err_str(r));
+  }
+  const int rc = engine_build(e, &d, shard.data(), static_cast<int>(shard.size()));
+  if (rc != C2S_OK) {
+    const std::string msg = g_err;
+    engine_free(e);
+    g_err = msg;
+    return rc;
+  }
+  *out = e;
+  return C2S_OK;
 }
 
 void c2s_engine_close(c2s_engine *e) { engine_free(e); }
@@ -1235,6 +1595,17 @@ int c2s_compute_logits(c2s_engine *e, const float *normx_in, const int32_t *targ
     memcpy(e->h_buf, normx_in, e->d.embd * 4);
     CK(cudaMemcpyAsync(e->normx, e->h_buf, e->d.embd * 4, cudaMemcpyHostToDevice, e->stream));
   }
+  if (targets && n_targets > 0 && e->plan.world > 1) {
+    // tensor parallel: the vocabulary is spread over the ranks; project it
+    // whole (a collective every rank makes) and keep the targets
+    std::vector<float> all(static_cast<size_t>(e->d.vocab));
+    if (int rc = c2s_compute_logits(e, nullptr, nullptr, 0, all.data())) return rc;
+    for (int i = 0; i < n_targets; ++i) {
+      const int t = targets[i];
+      if (t >= 0 && t < e->d.vocab) logits_out[t] = all[t];  // engine/forward.go:177-179
+    }
+    return C2S_OK;
+  }
   if (targets && n_targets > 0) {
     if (n_targets > e->d.vocab) return fail(C2S_ERR_ARG, "too many targets");
     memcpy(e->h_tokens, targets, static_cast<size_t>(n_targets) * 4);
@@ -1256,7 +1627,8 @@ int c2s_compute_logits(c2s_engine *e, const float *normx_in, const int32_t *targ
     return C2S_OK;
   }
   CK(cudaGraphLaunch(e->g_logits, e->stream));
-  CK(cudaMemcpyAsync(e->h_buf, e->logits, static_cast<size_t>(e->d.vocab) * 4, cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaMemcpyAsync(e->h_buf, e->plan.world > 1 ? e->logits_full : e->logits, static_cast<size_t>(e->d.vocab) * 4,
+                     cudaMemcpyDeviceToHost, e->stream));
   if (int rc = read_status(e)) return rc;
   memcpy(logits_out, e->h_buf, static_cast<size_t>(e->d.vocab) * 4);
   return C2S_OK;
@@ -1310,11 +1682,14 @@ int c2s_kv_get(const c2s_engine *e, int is_value, int layer, int kv_head, int po
   if (layer < 0 || layer >= e->d.n_layers || kv_head < 0 || kv_head >= e->d.n_kv_heads || pos < 0 ||
       pos >= e->d.max_tokens)
     return fail(C2S_ERR_ARG, "kv index out of range");
-  DeviceGuard g(e->device);
+  // a tensor-parallel rank holds kv heads [g0, g1)
+  const int nkv = e->plan.g1 - e->plan.g0, g = kv_head - e->plan.g0;
+  if (g < 0 || g >= nkv) return fail(C2S_ERR_ARG, "kv head %d is not held by this rank", kv_head);
+  DeviceGuard dg(e->device);
   const size_t hd = e->d.head_dim;
-  const size_t plane = static_cast<size_t>(e->d.n_layers) * e->d.n_kv_heads * e->d.max_tokens * hd;
+  const size_t plane = static_cast<size_t>(e->d.n_layers) * nkv * e->d.max_tokens * hd;
   const size_t off = (is_value ? plane : 0) +
-                     ((static_cast<size_t>(layer) * e->d.n_kv_heads + kv_head) * e->d.max_tokens + pos) * hd;
+                     ((static_cast<size_t>(layer) * nkv + g) * e->d.max_tokens + pos) * hd;
   CK(cudaMemcpy(out, e->kv + off, hd * 4, cudaMemcpyDeviceToHost));
   return C2S_OK;
 }

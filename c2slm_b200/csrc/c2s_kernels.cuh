@@ -670,6 +670,10 @@ struct AttnParams {
   DevState *st;
   int check_halt;
   int split_len;  // positions per split: position p is always in split p / split_len
+  // tensor parallel: this rank holds query heads [tp_h0, tp_h1) (q and out
+  // rows start at tp_h0) and kv heads tp_g0 .. tp_g0 + n_kv - 1; qpk is the
+  // model's query heads per kv head.  One GPU: 0, n_heads, 0.
+  int qpk, tp_h0, tp_h1, tp_g0;
 };
 
 __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int hd, float eps) {
@@ -726,9 +730,9 @@ struct AttnJob {
   const float *q_norm, *k_norm;    // Qwen3 per-head norms, or null
   float *kc, *vc;                  // cache planes of this layer and kv head: row p at [p * hd]
   const float *rope_cs, *rope_sn;  // RoPE row of pos (hd/2 each), or null outside the table
-  float *out, *part;
+  float *out, *part;               // head h0 + j of this item at out[(h0 + j) * hd]
   unsigned *counter;               // arrivals of the group's splits (last one combines)
-  int g, s, nsplit, p0, p1, pos;
+  int g, s, nsplit, p0, p1, pos, h0;
   int hd, qpk, max_splits;
   float eps, scale;
 };
@@ -871,7 +875,7 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
       issue(it + 2);
     }
   }
-  const int h0 = J.g * qpk;
+  const int h0 = J.h0;
   if (J.nsplit == 1) {  // single split: normalise and write the heads directly
     if (warp < qpk)
 #pragma unroll
@@ -934,7 +938,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   pdl_wait();
   DevState *st = A.st;
   if (A.check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
-  const int g = blockIdx.x, s = blockIdx.y;
+  const int g = blockIdx.x, s = blockIdx.y;  // g: local kv head
   const int pos = st->fwd_pos;
   if (pos < 0 || pos >= A.max_tokens) {
     if (tid == 0 && s == 0 && g == 0) atomicOr(&st->err, kErrPos);
@@ -943,12 +947,17 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   const int n = pos + 1, hd = A.hd;
   const int nsplit = (n + A.split_len - 1) / A.split_len;
   if (s >= nsplit) return;
+  // query heads of kv head tp_g0 + g that this rank holds
+  const int gg = A.tp_g0 + g;
+  const int hs = max(A.tp_h0, gg * A.qpk), he = min(A.tp_h1, (gg + 1) * A.qpk);
+  if (he <= hs) return;
   // KV layout [L][KVH][max_tokens][hd] per plane (engine/kvcache.go:127-140)
   const size_t head_stride = static_cast<size_t>(A.max_tokens) * hd;
   const size_t off = static_cast<size_t>(A.layer) * A.n_kv * head_stride + g * head_stride;
   AttnJob J;
-  J.qpk = A.n_heads / A.n_kv;
-  J.q = A.q + g * J.qpk * hd;
+  J.qpk = he - hs;
+  J.h0 = hs - A.tp_h0;
+  J.q = A.q + static_cast<size_t>(J.h0) * hd;
   J.k = A.k + g * hd;
   J.v = A.v + g * hd;
   J.q_norm = A.q_norm;
@@ -1100,6 +1109,121 @@ __global__ void k_swiglu_op(float *out, const float *gate, const float *up, int 
 
 __global__ void __launch_bounds__(kThreads) k_dequant_op(int type, const uint8_t *row, float *out, int cols) {
   dequant_row_cta(type, row, out, cols);
+}
+
+
+// ---------------------------------------------------------------------------
+// Tensor parallel: the residual add after an allreduced o-proj / down partial
+// (commit of the forwarded token after the last layer, as the single-GPU
+// down epilogue does), and greedy selection over gathered logits.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) k_residual_add(float *X, const float *delta, int n, DevState *st,
+                                                           int *token_ids, int commit_here, int check_halt) {
+  pdl_wait();
+  if (check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
+  for (int i = blockIdx.x * kThreads + threadIdx.x; i < n; i += gridDim.x * kThreads) X[i] = __fadd_rn(X[i], delta[i]);
+  if (commit_here && blockIdx.x == 0 && threadIdx.x == 0 && st->commit) {
+    const int pos = st->fwd_pos;
+    if (pos >= 0 && pos < st->out_cap) token_ids[pos] = st->fwd_token;  // KVCache.StoreTokenID
+    st->seq_len = pos + 1;
+    if (st->halt_pending) {
+      st->halted = 1;
+      st->halt_pending = 0;
+    }
+  }
+}
+
+// Repetition penalty + strict '>' argmax (ties: lowest id) over `vocab`
+// logits (c2slm.go:156-180), then the next forward's state.  Each CTA takes
+// a contiguous slice into shared memory; the last CTA to finish reduces the
+// per-CTA bests.  Same rules and float operations as the logits epilogue of
+// k_matvec.
+__global__ void __launch_bounds__(kThreads) k_select(const float *logits, int vocab, DevState *st,
+                                                     const int *token_ids, int *out_tokens, float2 *part,
+                                                     int check_halt) {
+  extern __shared__ __align__(16) float ybuf[];
+  __shared__ int s_flag;
+  __shared__ float s_bv[kWarps];
+  __shared__ int s_bi[kWarps];
+  pdl_wait();
+  if (check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
+  const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x;
+  int r0, r1;
+  seg_rows(vocab, c, G, r0, r1);
+  const int n = r1 - r0;
+  for (int i = tid; i < n; i += kThreads) ybuf[i] = __ldcg(logits + r0 + i);
+  __syncthreads();
+  if (tid == 0) {
+    const int pos = st->seq_len;
+    int start = pos - st->window;
+    if (start < 0) start = 0;
+    const float pen = st->penalty;
+    for (int p = start; p < pos; ++p) {
+      const int tok = token_ids[p];
+      if (tok >= 0 && tok < st->vocab && tok != st->im_end && tok != st->eos && tok >= r0 && tok < r1) {
+        float &v = ybuf[tok - r0];
+        v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
+      }
+    }
+  }
+  __syncthreads();
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = tid; i < n; i += kThreads) {
+    const float v = ybuf[i];
+    if (v > bv || (v == bv && r0 + i < bi)) {
+      bv = v;
+      bi = r0 + i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((tid & 31) == 0) {
+    s_bv[tid >> 5] = bv;
+    s_bi[tid >> 5] = bi;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < kWarps; ++w)
+      if (s_bv[w] > bv || (s_bv[w] == bv && s_bi[w] < bi)) {
+        bv = s_bv[w];
+        bi = s_bi[w];
+      }
+    part[c] = make_float2(bv, __int_as_float(bi));
+    __threadfence();
+    const unsigned t = atomicAdd(&st->logits_counter, 1u);
+    s_flag = (t == static_cast<unsigned>(G - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (s_flag && tid == 0) {
+    __threadfence();
+    float best_v = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int k = 0; k < G; ++k) {
+      const float2 pv = __ldcg(part + k);
+      const int pi = __float_as_int(pv.y);
+      if (pi == 0x7fffffff) continue;
+      if (pv.x > best_v || (pv.x == best_v && pi < best_i) || best_i == 0x7fffffff) {
+        best_v = pv.x;
+        best_i = pi;
+      }
+    }
+    if (best_i == 0x7fffffff) best_i = 0;
+    if (st->n_out < st->out_cap) out_tokens[st->n_out] = best_i;
+    st->n_out += 1;
+    st->fwd_token = best_i;
+    st->fwd_pos = st->seq_len;
+    st->commit = 1;
+    if (st->stop_on_special && (best_i == st->im_end || best_i == st->eos)) st->halt_pending = 1;
+    st->logits_counter = 0;
+  }
 }
 
 }  // namespace c2s

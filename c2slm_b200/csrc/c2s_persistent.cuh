@@ -272,6 +272,7 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   const size_t off = (static_cast<size_t>(ph.layer) * P.n_kv + g) * head_stride;
   AttnJob J;
   J.qpk = P.n_heads / P.n_kv;
+  J.h0 = g * J.qpk;
   J.q = P.q + g * J.qpk * hd;
   J.k = P.k + g * hd;
   J.v = P.v + g * hd;

@@ -28,6 +28,10 @@ SIGNATURES = {
     "c2s_version": (C.c_char_p, []),
     "c2s_engine_open": (I, [C.c_char_p, I, I, C.POINTER(P)]),
     "c2s_engine_create": (I, [P, P, I, I, C.POINTER(P)]),
+    "c2s_nccl_unique_id": (I, [P]),
+    "c2s_tp_plan": (I, [P, I, I, P]),
+    "c2s_engine_create_tp": (I, [P, P, I, I, I, I, P, C.POINTER(P)]),
+    "c2s_engine_open_tp": (I, [C.c_char_p, I, I, I, I, P, C.POINTER(P)]),
     "c2s_engine_close": (None, [P]),
     "c2s_engine_desc": (I, [P, P]),
     "c2s_forward": (I, [P, C.c_int32, C.c_int32, P]),
@@ -186,14 +190,40 @@ def dequant_row(kind: int, row, cols: int) -> np.ndarray:
 # ---------------------------------------------------------------------------
 # Engine
 # ---------------------------------------------------------------------------
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id() -> bytes:
+    """An NCCL unique id for a tensor-parallel group (rank 0 shares it)."""
+    buf = (C.c_uint8 * NCCL_ID_BYTES)()
+    _check(load_library().c2s_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+def tp_plan(desc, rank: int, world: int) -> dict:
+    """The shard of `rank` in a `world`-way tensor-parallel engine."""
+    out = (C.c_int32 * 9)()
+    _check(load_library().c2s_tp_plan(C.byref(desc), rank, world, out))
+    return dict(zip(("h0", "h1", "g0", "g1", "f0", "f1", "v0", "v1", "vpad"), list(out)))
+
+
 class Engine:
     """c2slm.Engine over one GPU (tokenizer stays with the caller)."""
 
     def __init__(self, path: str | None = None, device: int = 0, max_tokens: int = MAX_CONTEXT_LEN,
-                 gguf_file=None):
+                 gguf_file=None, tp: tuple[int, int, bytes] | None = None):
+        """tp = (rank, world, nccl_id): this process's shard of a tensor-parallel
+        engine (every rank opens the same file with the same nccl_id, from
+        nccl_unique_id() on rank 0, and then makes the same calls)."""
         lib = load_library()
         h = C.c_void_p()
-        if gguf_file is not None:
+        if tp is not None:
+            rank, world, nid = tp
+            if path is None or len(nid) != NCCL_ID_BYTES:
+                raise ValueError("tensor parallel needs a GGUF path and a 128-byte NCCL id")
+            idbuf = (C.c_uint8 * NCCL_ID_BYTES).from_buffer_copy(nid)
+            _check(lib.c2s_engine_open_tp(path.encode(), device, max_tokens, rank, world, idbuf, C.byref(h)))
+        elif gguf_file is not None:
             self._create_from_gguf(gguf_file, device, max_tokens, h)
         else:
             _check(lib.c2s_engine_open(path.encode(), device, max_tokens, C.byref(h)))

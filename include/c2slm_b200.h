@@ -83,6 +83,30 @@ int c2s_engine_open(const char *gguf_path, int device, int max_tokens, c2s_engin
 int c2s_engine_create(const c2s_model_desc *desc, const c2s_tensor_desc *tensors,
                       int n_tensors, int device, c2s_engine **out);
 
+/* Tensor parallel over `world` GPUs of one node (one process or thread per
+ * GPU), the sharding of the 7B-shaped config: rank r holds query heads
+ * [h0, h1) (whole 256-column superblocks of attn_output's input: pairs of
+ * heads at head_dim 128) with the kv heads they use, FFN rows [f0, f1) in
+ * superblocks, and vocabulary rows [v0, v1) of an even split padded to vpad
+ * rows.  attn_output and ffn_down run on the rank's columns and are summed
+ * by an NCCL allreduce before the residual add; the logits are all-gathered
+ * and every rank applies the same penalty and argmax, so all ranks select
+ * the same ids.  Every rank must make the same sequence of calls (forward,
+ * ingest, generate, decode_step, compute_logits, bench) with the same
+ * arguments.  No counterpart in the reference (CPU only). */
+#define C2S_NCCL_ID_BYTES 128
+/* An NCCL unique id (C2S_NCCL_ID_BYTES bytes) for rank 0 to share with the
+ * other ranks. */
+int c2s_nccl_unique_id(uint8_t *id_out);
+/* The shard of `rank`: plan_out[9] = {h0, h1, g0, g1, f0, f1, v0, v1, vpad}
+ * (f in superblocks of 256 rows).  head_dim 0 and vocab are derived as for
+ * c2s_engine_create. */
+int c2s_tp_plan(const c2s_model_desc *desc, int rank, int world, int32_t *plan_out);
+int c2s_engine_create_tp(const c2s_model_desc *desc, const c2s_tensor_desc *tensors, int n_tensors,
+                         int device, int rank, int world, const uint8_t *nccl_id, c2s_engine **out);
+int c2s_engine_open_tp(const char *gguf_path, int device, int max_tokens, int rank, int world,
+                       const uint8_t *nccl_id, c2s_engine **out);
+
 /* Engine.Close (c2slm.go:44-55).  NULL is accepted. */
 void c2s_engine_close(c2s_engine *e);
 
