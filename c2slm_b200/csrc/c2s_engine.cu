@@ -469,6 +469,12 @@ struct c2s_engine {
   ncclComm_t comm = nullptr;
   float *delta = nullptr;        // this rank's partial o-proj / down output, allreduced in place
   float *logits_full = nullptr;  // gathered logits [world * vpad]
+  // persistent decode across the group: tagged words recv [2][world][H] | argbuf [2][world][G][2],
+  // mapped into every rank (peer_shared[r] = rank r's region, this rank's own included)
+  uint8_t *tp_shared = nullptr;
+  uint8_t *peer_shared[8] = {};
+  float *xbuf = nullptr;         // [2][H] residual stream
+  bool tp_persist_ok = false;    // the persistent kernel fits; enabled once the peers are mapped
 };
 
 namespace {
@@ -782,8 +788,14 @@ int set_fwd_input(c2s_engine *e, int token, int pos, int commit) {
 // ---------------------------------------------------------------------------
 int persistent_setup(c2s_engine *e) {
   const c2s_model_desc &d = e->d;
-  const int L = d.n_layers, H = d.embd, F = d.ffn, hd = d.head_dim, kvd = d.n_kv_heads * hd;
+  const TpPlan &pl = e->plan;
+  const bool tp = pl.world > 1;
+  // this rank's rows (the model's on one GPU)
+  const int L = d.n_layers, H = d.embd, hd = d.head_dim;
+  const int F = tp ? (pl.f1 - pl.f0) * 256 : d.ffn, kvd = (pl.g1 - pl.g0) * hd, nq = (pl.h1 - pl.h0) * hd;
+  const int V = pl.v1 - pl.v0;
   const int G = e->num_sms;
+  if (tp && pl.world > kMaxRanks) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: more than %d ranks", kMaxRanks);
   std::vector<PPhase> ph;
   auto mk = [&](int kind, int layer) {
     PPhase p{};
@@ -803,7 +815,7 @@ int persistent_setup(c2s_engine *e) {
     PPhase p = mk(K_LOGITS, -1);
     p.nseg = 1;
     p.cols = H;
-    p.seg[0] = make_seg(e->output, e->out_type, d.vocab, H, nullptr, e->logits);
+    p.seg[0] = make_seg(e->output, e->out_type, V, H, nullptr, e->logits);
     p.norm_w = e->out_norm;
     needs(p);
     ph.push_back(p);
@@ -813,7 +825,7 @@ int persistent_setup(c2s_engine *e) {
     PPhase q = mk(K_QKV, l);
     q.nseg = 3;
     q.cols = H;
-    q.seg[0] = make_seg(Ld.q, Ld.tq, H, H, Ld.qb, e->q);
+    q.seg[0] = make_seg(Ld.q, Ld.tq, nq, H, Ld.qb, e->q);
     q.seg[1] = make_seg(Ld.k, Ld.tk, kvd, H, Ld.kb, e->k);
     q.seg[2] = make_seg(Ld.v, Ld.tv, kvd, H, Ld.vb, e->v);
     q.norm_w = Ld.attn_norm;
@@ -827,7 +839,8 @@ int persistent_setup(c2s_engine *e) {
     PPhase o = mk(K_OPROJ, l);
     o.nseg = 1;
     o.cols = H;
-    o.seg[0] = make_seg(Ld.o, Ld.to, H, H, nullptr, e->X);
+    o.cols = nq;
+    o.seg[0] = make_seg(Ld.o, Ld.to, H, nq, nullptr, e->X);
     o.x_in = e->attn_out;
     needs(o);
     ph.push_back(o);
@@ -926,13 +939,22 @@ int persistent_setup(c2s_engine *e) {
   P.F = F;
   P.kvd = kvd;
   P.vocab = d.vocab;
+  P.qrows = nq;
+  P.vrows = V;
+  P.world = pl.world;
+  P.rank = pl.rank;
+  P.qpk = d.n_heads / d.n_kv_heads;
+  P.tp_h0 = pl.h0;
+  P.tp_h1 = pl.h1;
+  P.tp_g0 = pl.g0;
+  P.tp_v0 = pl.v0;  // the exchange buffers of a tensor-parallel group are set by tp_exchange_setup
   e->nphase = static_cast<int>(ph.size());
   CK(cudaMalloc(&e->gbar, 4 * static_cast<size_t>(G) + 64));
   CK(cudaMemset(e->gbar, 0, 4 * static_cast<size_t>(G) + 64));
   P.nphase = e->nphase;
   P.H = H;
   P.n_heads = d.n_heads;
-  P.n_kv = d.n_kv_heads;
+  P.n_kv = pl.g1 - pl.g0;
   P.hd = hd;
   P.max_tokens = d.max_tokens;
   P.max_splits = e->max_splits;
@@ -950,7 +972,7 @@ int persistent_setup(c2s_engine *e) {
   P.logits = e->logits;
   P.part = e->part;
   P.amax_part = e->amax_part;
-  const size_t plane = static_cast<size_t>(L) * d.n_kv_heads * d.max_tokens * hd;
+  const size_t plane = static_cast<size_t>(L) * (pl.g1 - pl.g0) * d.max_tokens * hd;
   P.kcache = e->kv;
   P.vcache = e->kv + plane;
   P.rope_cos = e->rope_cos;
@@ -1211,13 +1233,71 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
       return rc;
   }
   e->kernels_per_step = 5 * d.n_layers + 1;
-  if (pl.world > 1) {
-    e->kernels_per_step = 7 * d.n_layers + 2;  // + a residual add after each allreduce, + selection
-    e->use_persistent = false;                 // collectives run between per-phase kernels
-  } else if ((rc = persistent_setup(e))) {
-    return rc;
+  if (pl.world > 1) e->kernels_per_step = 7 * d.n_layers + 2;  // + a residual add after each allreduce, + selection
+  if ((rc = persistent_setup(e))) return rc;
+  if (pl.world > 1) {  // until tp_exchange_setup has mapped the peers' buffers
+    e->tp_persist_ok = e->use_persistent;
+    e->use_persistent = false;
   }
   CK(cudaStreamSynchronize(e->stream));
+  return C2S_OK;
+}
+
+// Persistent decode across a tensor-parallel group: every rank allocates one
+// exchange region of tagged 64-bit words (partial rows [2][world][H], argmax
+// partials [2][world][G][2]), zeroed, and maps every other
+// rank's region through CUDA IPC; the handles travel through an NCCL
+// all-gather, which also guarantees that every rank has zeroed its region
+// before any rank starts decoding.
+int tp_exchange_setup(c2s_engine *e) {
+  const TpPlan &pl = e->plan;
+  const int W = pl.world, G = e->num_sms, H = e->d.embd;
+  if (W > kMaxRanks) return fail(C2S_ERR_UNSUPPORTED, "more than %d ranks", kMaxRanks);
+  const NcclApi *nc = nullptr;
+  if (int rc = nccl_api(&nc)) return rc;
+  auto a256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+  // tagged words: recv [2][W][H], argbuf [2][W][G][2]; zero = tag 0, never expected
+  const size_t off_arg = a256(static_cast<size_t>(2) * W * H * 8);
+  const size_t bytes = off_arg + a256(static_cast<size_t>(2) * W * G * 2 * 8);
+  CK(cudaMalloc(&e->tp_shared, bytes));
+  CK(cudaMemset(e->tp_shared, 0, bytes));
+  CK(cudaMalloc(&e->xbuf, static_cast<size_t>(2) * H * 4 + 64));
+  CK(cudaMemset(e->xbuf, 0, static_cast<size_t>(2) * H * 4 + 64));
+  CK(cudaDeviceSynchronize());
+  cudaIpcMemHandle_t mine;
+  CK(cudaIpcGetMemHandle(&mine, e->tp_shared));
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  uint8_t *dh = nullptr;
+  CK(cudaMalloc(&dh, static_cast<size_t>(64) * W));
+  CK(cudaMemcpy(dh + 64 * pl.rank, &mine, 64, cudaMemcpyHostToDevice));
+  const ncclResult_t r = nc->all_gather(dh + 64 * pl.rank, dh, 64, ncclUint8, e->comm, e->stream);
+  if (r != ncclSuccess) {
+    cudaFree(dh);
+    return fail(C2S_ERR_CUDA, "ncclAllGather (IPC handles): %s", nc->err_str(r));
+  }
+  std::vector<cudaIpcMemHandle_t> hs(W);
+  CK(cudaStreamSynchronize(e->stream));
+  CK(cudaMemcpy(hs.data(), dh, static_cast<size_t>(64) * W, cudaMemcpyDeviceToHost));
+  cudaFree(dh);
+  for (int k = 0; k < W; ++k) {
+    if (k == pl.rank) {
+      e->peer_shared[k] = e->tp_shared;
+      continue;
+    }
+    void *p = nullptr;
+    const cudaError_t er = cudaIpcOpenMemHandle(&p, hs[k], cudaIpcMemLazyEnablePeerAccess);
+    if (er != cudaSuccess) return fail(C2S_ERR_CUDA, "cudaIpcOpenMemHandle (rank %d): %s", k, cudaGetErrorString(er));
+    e->peer_shared[k] = static_cast<uint8_t *>(p);
+  }
+  PParams &P = e->pp;
+  P.xbuf = e->xbuf;
+  P.recv = reinterpret_cast<const unsigned long long *>(e->tp_shared);
+  P.argbuf = reinterpret_cast<const unsigned long long *>(e->tp_shared + off_arg);
+  for (int k = 0; k < W; ++k) {
+    P.peer_recv[k] = reinterpret_cast<unsigned long long *>(e->peer_shared[k]);
+    P.peer_arg[k] = reinterpret_cast<unsigned long long *>(e->peer_shared[k] + off_arg);
+  }
+  e->use_persistent = e->tp_persist_ok;
   return C2S_OK;
 }
 
@@ -1313,6 +1393,10 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->scratch_x), static_cast<void *>(e->st),
                   static_cast<void *>(e->gbar), static_cast<void *>(e->delta),
                   static_cast<void *>(e->logits_full)})
+    if (p) cudaFree(p);
+  for (int k = 0; k < 8; ++k)
+    if (e->peer_shared[k] && e->peer_shared[k] != e->tp_shared) cudaIpcCloseMemHandle(e->peer_shared[k]);
+  for (void *p : {static_cast<void *>(e->tp_shared), static_cast<void *>(e->xbuf)})
     if (p) cudaFree(p);
   if (e->comm) {
     const NcclApi *nc = nullptr;
@@ -1555,7 +1639,8 @@ int c2s_engine_create_tp(const c2s_model_desc *desc, const c2s_tensor_desc *tens
     engine_free(e);
     return fail(C2S_ERR_CUDA, "ncclCommInitRank: %s", nc->err_str(r));
   }
-  const int rc = engine_build(e, &d, shard.data(), static_cast<int>(shard.size()));
+  int rc = engine_build(e, &d, shard.data(), static_cast<int>(shard.size()));
+  if (rc == C2S_OK) rc = tp_exchange_setup(e);
   if (rc != C2S_OK) {
     const std::string msg = g_err;
     engine_free(e);

@@ -23,6 +23,7 @@ struct DevState {
   unsigned err;
   unsigned logits_counter;
   unsigned attn_counter[64];
+  unsigned xbar;                   // cross-GPU barriers completed (tensor-parallel persistent decode)
 };
 
 // K_NORM: final RMSNorm only (NormX of engine.Forward).  K_LOGITS normalises

@@ -45,7 +45,8 @@ struct PParams {
   PLayer layers[kMaxLayers];
   const uint8_t *out_w;
   const float *out_norm;
-  int out_type, n_layers, F, kvd, vocab;
+  int out_type, n_layers, F, kvd, vocab;  // F, kvd: this rank's rows (the model's on one GPU)
+  int qrows, vrows;                        // this rank's attn_q rows and vocabulary rows
   int nphase, n_steps;
   int nslot;
   int off_full, off_empty, off_abar, off_act;
@@ -67,7 +68,24 @@ struct PParams {
   int phase0;           // 0: a step starts with logits + selection; 1: with the forward
                         // of the token in DevState (the last phase is then logits)
   unsigned long long *trace;  // optional: [step][phase][cta][kTraceFields], see k_persistent
+  // tensor parallel over `world` GPUs (world == 1: everything below unused).
+  // n_kv is then this rank's kv heads (global ids tp_g0 ..), q rows start at
+  // query head tp_h0, vocabulary rows at tp_v0; qpk = the model's query heads
+  // per kv head.  Exchanges between ranks are tagged 64-bit words (tag << 32 |
+  // value bits) stored straight into every rank's buffers over NVLink: a
+  // reader polls the words themselves until each carries the expected tag, so
+  // no barrier or fence crosses GPUs.  Tags count the exchanges over the
+  // engine's lifetime (DevState::xbar), so buffers are never reset.
+  //   recv   [2][world][H]       o-proj / down partial rows (parity: o-proj 0, down 1)
+  //   argbuf [2][world][G][2]    per-CTA argmax (value, id) of the logits (parity: step)
+  // The next normed phase adds the received partials to the residual
+  // xbuf[2][H] (each CTA stores its share of the new residual).
+  int world, rank, qpk, tp_h0, tp_h1, tp_g0, tp_v0;
+  float *xbuf;
+  const unsigned long long *recv, *argbuf;
+  unsigned long long *peer_recv[8], *peer_arg[8];
 };
+constexpr int kMaxRanks = 8;
 
 // trace record per (step, phase, CTA): globaltimer ns at phase start (after
 // the grid barrier), inputs ready, chunks done and end; then SM cycles thread
@@ -140,6 +158,66 @@ __device__ __forceinline__ bool grid_barrier(unsigned *counter, unsigned seq, un
   return *s_ok != 0;
 }
 
+// tagged words: single-copy atomic 64-bit stores / loads at system scope
+__device__ __forceinline__ void st_tagged(unsigned long long *p, unsigned tag, uint32_t bits) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"((static_cast<unsigned long long>(tag) << 32) | bits)
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Sum over ranks (in rank order) of element i .. i+3 of the tagged partial
+// rows recv[par][r][*], polling until every word carries `tag`.  Bounded
+// (~2 s): on expiry sets the error flag and returns zeros with *ok cleared.
+__device__ __forceinline__ float4 sum_tagged4(const PParams &P, int par, int i, unsigned tag, unsigned *err,
+                                              bool &ok) {
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  const unsigned long long *base = P.recv + static_cast<size_t>(par) * P.world * P.H + i;
+  for (int r0 = 0; r0 < P.world; r0 += 2) {
+    const int nr = min(2, P.world - r0);
+    unsigned long long w[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[j][e] = j < nr ? ld_tagged(base + static_cast<size_t>(r0 + j) * P.H + e) : 0ull;
+    const long long t0 = clock64();
+    for (uint32_t it = 0;; ++it) {
+      bool all = true;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (j < nr && static_cast<unsigned>(w[j][e] >> 32) != tag) {
+            all = false;
+            w[j][e] = ld_tagged(base + static_cast<size_t>(r0 + j) * P.H + e);
+          }
+      if (all) break;
+      if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+        atomicOr(err, kErrCounter);
+        ok = false;
+        return make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+      if (j < nr) {
+        if (r0 + j == 0) {
+          o = make_float4(__uint_as_float(static_cast<uint32_t>(w[j][0])), __uint_as_float(static_cast<uint32_t>(w[j][1])),
+                          __uint_as_float(static_cast<uint32_t>(w[j][2])), __uint_as_float(static_cast<uint32_t>(w[j][3])));
+        } else {
+          o.x = __fadd_rn(o.x, __uint_as_float(static_cast<uint32_t>(w[j][0])));
+          o.y = __fadd_rn(o.y, __uint_as_float(static_cast<uint32_t>(w[j][1])));
+          o.z = __fadd_rn(o.z, __uint_as_float(static_cast<uint32_t>(w[j][2])));
+          o.w = __fadd_rn(o.w, __uint_as_float(static_cast<uint32_t>(w[j][3])));
+        }
+      }
+  }
+  return o;
+}
+
 // Q8_K of a global vector straight into shared memory: warp w quantises
 // superblocks w, w + kWarps, ... with all of its loads in flight first
 // (cols <= 4 * kWarps * 256 per call round).
@@ -199,7 +277,7 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
     ph.layer = -1;
     ph.nseg = 1;
     ph.cols = P.H;
-    ph.seg[0] = pseg(P.out_w, P.out_type, P.vocab, P.H, nullptr, P.logits, P.slot_bytes);
+    ph.seg[0] = pseg(P.out_w, P.out_type, P.vrows, P.H, nullptr, P.logits, P.slot_bytes);
     ph.norm_w = P.out_norm;
     needs();
     return;
@@ -212,7 +290,7 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
       ph.kind = K_QKV;
       ph.nseg = 3;
       ph.cols = P.H;
-      ph.seg[0] = pseg(L.q, L.tq, P.H, P.H, L.qb, P.q, P.slot_bytes);
+      ph.seg[0] = pseg(L.q, L.tq, P.qrows, P.H, L.qb, P.q, P.slot_bytes);
       ph.seg[1] = pseg(L.k, L.tk, P.kvd, P.H, L.kb, P.k, P.slot_bytes);
       ph.seg[2] = pseg(L.v, L.tv, P.kvd, P.H, L.vb, P.v, P.slot_bytes);
       ph.norm_w = L.attn_norm;
@@ -227,8 +305,8 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
     case 2:
       ph.kind = K_OPROJ;
       ph.nseg = 1;
-      ph.cols = P.H;
-      ph.seg[0] = pseg(L.o, L.to, P.H, P.H, nullptr, P.X, P.slot_bytes);
+      ph.cols = P.qrows;
+      ph.seg[0] = pseg(L.o, L.to, P.H, P.qrows, nullptr, P.X, P.slot_bytes);
       ph.x_in = P.attn_out;
       break;
     case 3:
@@ -268,12 +346,16 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   const int nsplit = (n + P.split_len - 1) / P.split_len;
   if (item >= P.n_kv * nsplit) return true;
   const int g = item % P.n_kv, s = item / P.n_kv;  // split-major: (g, s) stays on one CTA as n grows
+  // this rank's query heads of kv head tp_g0 + g (one GPU: all qpk of them)
+  const int gg = P.tp_g0 + g;
+  const int hs = max(P.tp_h0, gg * P.qpk), he = min(P.tp_h1, (gg + 1) * P.qpk);
+  if (he <= hs) return true;
   const size_t head_stride = static_cast<size_t>(P.max_tokens) * hd;
   const size_t off = (static_cast<size_t>(ph.layer) * P.n_kv + g) * head_stride;
   AttnJob J;
-  J.qpk = P.n_heads / P.n_kv;
-  J.h0 = g * J.qpk;
-  J.q = P.q + g * J.qpk * hd;
+  J.qpk = he - hs;
+  J.h0 = hs - P.tp_h0;
+  J.q = P.q + static_cast<size_t>(J.h0) * hd;
   J.k = P.k + g * hd;
   J.v = P.v + g * hd;
   J.q_norm = ph.q_norm;
@@ -366,7 +448,8 @@ __device__ __forceinline__ bool warp_wait_full(uint64_t *bar, uint32_t parity, u
 }
 
 __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint32_t &k_ring, float (*red)[kWarps],
-                         float *scratch, int *s_flag, int *s_pos, float *s_rope, unsigned long long *tr) {
+                         float *scratch, int *s_flag, int *s_pos, float *s_rope, unsigned long long *tr,
+                         unsigned &xb, bool from_X) {
   const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   DevState *st = P.st;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
@@ -389,7 +472,8 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   const bool normed = ph.kind == K_QKV || ph.kind == K_FFN_UP || ph.kind == K_LOGITS;
   // ---- loads the epilogue needs, requested first
   float xres = 0.f, bias[kMaxSegs] = {0.f, 0.f, 0.f};
-  if (residual && R.r0[0] + tid < R.r1[0]) xres = __ldcg(P.X + R.r0[0] + tid);
+  const bool tp = P.world > 1;
+  if (residual && !tp && R.r0[0] + tid < R.r1[0]) xres = __ldcg(P.X + R.r0[0] + tid);
 #pragma unroll
   for (int s = 0; s < kMaxSegs; ++s)
     if (s < ph.nseg && ph.seg[s].bias && R.r0[s] + tid < R.r1[s]) bias[s] = __ldg(ph.seg[s].bias + R.r0[s] + tid);
@@ -420,19 +504,52 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       dequant_row_cta(P.embd_type, P.embd_w + static_cast<size_t>(tok) * P.embd_row_bytes, xn, cols);
       csync();
     }
+    // tensor parallel: X = residual + the partials every rank sent (rank
+    // order), from xbuf[par]; this CTA stores its share of the new X in
+    // xbuf[1 - par] for the next reduction.  gate/up follows o-proj's
+    // reduction (par 0); qkv (layers > 0) and logits follow down's (par 1).
+    // The first phase of a launch reads the residual the per-phase kernels
+    // left in X (from_X).
+    const int par = ph.kind == K_FFN_UP ? 0 : 1;
+    const bool reduce = tp && !embed && !from_X;
+    const float4 *xs4 = reduce ? reinterpret_cast<const float4 *>(P.xbuf + static_cast<size_t>(par) * P.H) : x4;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int i = tid + k * kThreads;
       xv[k] = wv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i < n4) {
-        xv[k] = embed ? reinterpret_cast<const float4 *>(xn)[i] : __ldcg(x4 + i);
+        xv[k] = embed ? reinterpret_cast<const float4 *>(xn)[i] : __ldcg(xs4 + i);
         wv[k] = __ldg(w4 + i);
       }
     }
-    if (embed && c == 0)
+    if (reduce) {  // the exchange this phase follows is number xb
+      bool got = true;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = tid + k * kThreads;
+        if (i < n4 && got) {
+          const float4 o = sum_tagged4(P, par, 4 * i, xb, &st->err, got);
+          xv[k] = make_float4(__fadd_rn(xv[k].x, o.x), __fadd_rn(xv[k].y, o.y), __fadd_rn(xv[k].z, o.z),
+                              __fadd_rn(xv[k].w, o.w));
+        }
+      }
+      if (!got) *reinterpret_cast<volatile int *>(&s_fail) = 1;
+    }
+    if (tp && (embed || reduce)) {  // this CTA's share of the new residual (logits: back in X)
+      float4 *xd = ph.kind == K_LOGITS ? reinterpret_cast<float4 *>(P.X)
+                                       : reinterpret_cast<float4 *>(P.xbuf + static_cast<size_t>(embed ? 0 : 1 - par) * P.H);
+      const int a = static_cast<int>((static_cast<unsigned>(c) * n4) / G);
+      const int b = static_cast<int>((static_cast<unsigned>(c + 1) * n4) / G);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = tid + k * kThreads;
+        if (i >= a && i < b) xd[i] = xv[k];
+      }
+    } else if (embed && c == 0) {
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         if (tid + k * kThreads < n4) reinterpret_cast<float4 *>(P.X)[tid + k * kThreads] = xv[k];
+    }
     // RMSNorm (tensor/ops.go:207-218)
     float ss = 0.f;
 #pragma unroll
@@ -531,7 +648,16 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       if (s < ph.nseg && R.r0[s] + tid < R.r1[s])
         ph.seg[s].out[R.r0[s] + tid] = __fadd_rn(ybuf[s * P.yrows + tid], bias[s]);
   } else if (residual) {
-    if (R.r0[0] + tid < R.r1[0]) P.X[R.r0[0] + tid] = __fadd_rn(xres, ybuf[tid]);
+    if (tp) {  // partial rows to every rank, tagged as exchange xb + 1 (summed by the next normed phase)
+      const int par = ph.kind == K_OPROJ ? 0 : 1;
+      if (R.r0[0] + tid < R.r1[0]) {
+        const uint32_t v = __float_as_uint(ybuf[tid]);
+        const size_t at = (static_cast<size_t>(par) * P.world + P.rank) * P.H + R.r0[0] + tid;
+        for (int r = 0; r < P.world; ++r) st_tagged(P.peer_recv[r] + at, xb + 1, v);
+      }
+    } else if (R.r0[0] + tid < R.r1[0]) {
+      P.X[R.r0[0] + tid] = __fadd_rn(xres, ybuf[tid]);
+    }
     if (ph.kind == K_FFN_DOWN && ph.commit_here && c == 0 && tid == 0 && ldst(&st->commit)) {
       const int pos = ldst(&st->fwd_pos);
       if (pos >= 0 && pos < st->out_cap) P.token_ids[pos] = ldst(&st->fwd_token);  // KVCache.StoreTokenID
@@ -551,6 +677,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   } else if (ph.kind == K_LOGITS) {
     const int lo = R.r0[0], n = R.r1[0] - lo;
     for (int r = tid; r < n; r += kThreads) P.logits[lo + r] = ybuf[r];
+    const int glo = P.tp_v0 + lo;  // vocabulary id of this CTA's first row
     // repetition penalty on this CTA's rows (c2slm.go:156-170): every
     // occurrence in the window applies the factor once; the thread holding a
     // token's first occurrence applies all of them, in place
@@ -560,7 +687,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       for (int q = 0; q < times; ++q) v = v > 0.f ? __fdiv_rn(v, pen) : __fmul_rn(v, pen);
     };
     auto eligible = [&](int tok) {
-      return tok >= 0 && tok < st->vocab && tok != st->im_end && tok != st->eos && tok >= lo && tok < lo + n;
+      return tok >= 0 && tok < st->vocab && tok != st->im_end && tok != st->eos && tok >= glo && tok < glo + n;
     };
     csync();  // logits stored before ybuf is penalised
     if (wlen <= kThreads) {
@@ -574,13 +701,13 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
               first = first && q >= tid;
               ++times;
             }
-          if (first) penalise(ybuf[tok - lo], times);
+          if (first) penalise(ybuf[tok - glo], times);
         }
       }
     } else if (tid == 0) {
       for (int p = pos - wlen; p < pos; ++p) {
         const int tok = ldst(P.token_ids + p);
-        if (eligible(tok)) penalise(ybuf[tok - lo], 1);
+        if (eligible(tok)) penalise(ybuf[tok - glo], 1);
       }
     }
     csync();
@@ -588,9 +715,9 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     int bi = 0x7fffffff;
     for (int r = tid; r < n; r += kThreads) {
       const float v = ybuf[r];
-      if (v > bv || (v == bv && lo + r < bi)) {
+      if (v > bv || (v == bv && glo + r < bi)) {
         bv = v;
-        bi = lo + r;
+        bi = glo + r;
       }
     }
 #pragma unroll
@@ -616,18 +743,49 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
           bi = ix;
         }
       }
-      P.amax_part[c] = make_float2(bv, __int_as_float(bi));
-      __threadfence();
-      const unsigned t = atomicAdd(&st->logits_counter, 1u);
-      *s_flag = (t == static_cast<unsigned>(G - 1)) ? 1 : 0;
+      if (tp) {  // to every rank, tagged as exchange xb + 1: each one reduces all ranks' partials
+        const size_t at = ((static_cast<size_t>((xb + 1) & 1u) * P.world + P.rank) * G + c) * 2;
+        for (int r = 0; r < P.world; ++r) {
+          st_tagged(P.peer_arg[r] + at, xb + 1, __float_as_uint(bv));
+          st_tagged(P.peer_arg[r] + at + 1, xb + 1, static_cast<uint32_t>(bi));
+        }
+      } else {
+        P.amax_part[c] = make_float2(bv, __int_as_float(bi));
+        __threadfence();
+        const unsigned t = atomicAdd(&st->logits_counter, 1u);
+        *s_flag = (t == static_cast<unsigned>(G - 1)) ? 1 : 0;
+      }
     }
     csync();
-    if (*s_flag) {  // the last CTA reduces the G partials (ties: lowest id)
+    if (tp) {
+      xb += 1;
+      *s_flag = c == 0 ? 1 : 0;  // CTA 0 of every rank selects (the same id on all ranks)
+      csync();
+    }
+    const int nparts = tp ? P.world * G : G;
+    const unsigned long long *tagged = P.argbuf + static_cast<size_t>(xb & 1u) * P.world * G * 2;
+    if (*s_flag) {  // the selecting CTA reduces the partials (ties: lowest id)
       __threadfence();
       float best_v = -INFINITY;
       int best_i = 0x7fffffff;
-      for (int kk = tid; kk < G; kk += kThreads) {
-        const float2 pv = __ldcg(P.amax_part + kk);
+      for (int kk = tid; kk < nparts; kk += kThreads) {
+        float2 pv;
+        if (tp) {  // poll until both words of the partial carry the exchange's tag (bounded)
+          unsigned long long a = ld_tagged(tagged + 2 * kk), b = ld_tagged(tagged + 2 * kk + 1);
+          const long long t0 = clock64();
+          for (uint32_t it = 0; static_cast<unsigned>(a >> 32) != xb || static_cast<unsigned>(b >> 32) != xb; ++it) {
+            if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+              atomicOr(&st->err, kErrCounter);
+              *reinterpret_cast<volatile int *>(&s_fail) = 1;
+              break;
+            }
+            a = ld_tagged(tagged + 2 * kk);
+            b = ld_tagged(tagged + 2 * kk + 1);
+          }
+          pv = make_float2(__uint_as_float(static_cast<uint32_t>(a)), __int_as_float(static_cast<int>(static_cast<uint32_t>(b))));
+        } else {
+          pv = __ldcg(P.amax_part + kk);
+        }
         const int pi = __float_as_int(pv.y);
         if (pi != 0x7fffffff && (pv.x > best_v || (pv.x == best_v && pi < best_i) || best_i == 0x7fffffff)) {
           best_v = pv.x;
@@ -760,6 +918,9 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   uint32_t abar_uses[2] = {0, 0};
   unsigned bar_target = 0;
   bool ok = true;
+  unsigned xb = static_cast<unsigned>(ldst(reinterpret_cast<const int *>(&st->xbar)));  // cross-GPU barriers so far
+  bool crossed = false;  // the previous phase ended with a cross-GPU barrier
+  int last_kind = -1;    // kind of the last phase completed
   if (tid == 0) s_pos = ldst(&st->fwd_pos);  // the forward's position when phase0 == 1
   if (tid < P.hd && P.phase0 == 1) {
     const int pos0 = ldst(&st->fwd_pos), half = P.hd / 2;
@@ -774,11 +935,12 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
       csync();
       const PPhase &ph = s_ph;
       const long long b0 = P.trace ? clock64() : 0;
-      if (kp > 0) {
+      if (kp > 0 && !(crossed && pi != 0)) {
         bar_target += 1;
         if (!grid_barrier(P.gbar, bar_target, &st->err, &s_ok)) { ok = false; break; }
       }
-      if (pi == 0 && ldst(&st->halted)) { ok = false; break; }
+      crossed = false;
+      if (pi == 0 && ldst(&st->halted)) break;  // stop token forwarded: a normal end
       unsigned long long *tr =
           (P.trace && tid == 0)
               ? P.trace + (static_cast<size_t>(kp) * G + c) * kTraceFields
@@ -795,7 +957,10 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
           break;
         }
       } else {
-        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag, &s_pos, s_rope, tr)) { ok = false; break; }
+        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag, &s_pos, s_rope, tr, xb, kp == 0)) {
+          ok = false;
+          break;
+        }
       }
       csync();
       if (tr) tr[3] = globaltimer_ns();
@@ -803,8 +968,34 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
       if (ph.kind == K_FFN_DOWN && ph.commit_here && P.rewind_period > 0 && c == 0 && tid == 0 &&
           (step + 1) % P.rewind_period == 0)
         st->seq_len = P.rewind_base;
+      // tensor parallel: o-proj / down sent exchange xb + 1; the next phase
+      // polls its tagged words instead of waiting at a grid barrier (except
+      // logits, which reads the state the down phase committed)
+      if (P.world > 1 && (ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN)) {
+        xb += 1;
+        crossed = true;
+      }
+      last_kind = ph.kind;
     }
   }
+  if (P.world > 1 && ok && last_kind == K_FFN_DOWN) {
+    // the launch ends after a forward: leave its residual in X for the
+    // per-phase kernels and the next launch (X = xbuf[1] + the down partials)
+    const int n4 = P.H / 4;
+    const int a = static_cast<int>((static_cast<unsigned>(c) * n4) / G);
+    const int b = static_cast<int>((static_cast<unsigned>(c + 1) * n4) / G);
+    const float4 *xs = reinterpret_cast<const float4 *>(P.xbuf + P.H);
+    bool got = true;
+    for (int i = a + tid; i < b && got; i += kThreads) {
+      const float4 o = sum_tagged4(P, 1, 4 * i, xb, &st->err, got);
+      const float4 x = __ldcg(xs + i);
+      reinterpret_cast<float4 *>(P.X)[i] =
+          make_float4(__fadd_rn(x.x, o.x), __fadd_rn(x.y, o.y), __fadd_rn(x.z, o.z), __fadd_rn(x.w, o.w));
+    }
+  }
+  // exchanges done; after a failure, jump far past every tag already written
+  // so that no later exchange can match a stale word
+  if (c == 0 && tid == 0) st->xbar = ok ? xb : xb + (1u << 24);
   // tell the producer where consumption stopped, then let it drain
   csync();
   if (tid == 0) {

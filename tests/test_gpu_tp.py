@@ -22,30 +22,35 @@ def rel(a, b):
     return float(np.max(np.abs(a - b)) / max(1e-30, np.max(np.abs(b))))
 
 
-def _rank(rank, world, nid, path, prompt, q):
+def _decode(e, prompt):
+    """ingest, logits, then decode through three launches of different kinds:
+    generate, host-driven decode_step, generate again"""
+    nx = e.ingest_from(0, prompt)
+    lg = e.compute_logits()
+    ids = list(e.generate(STEPS, stop_on_special=False))
+    tok = ids[-1]
+    for _ in range(3):
+        tok = e.decode_step(tok)
+        ids.append(tok)
+    ids += list(e.generate(STEPS, stop_on_special=False))
+    return nx, lg, np.asarray(ids), e.seq_len
+
+
+def _rank(rank, world, nid, path, prompt, mode, q):
     try:
+        os.environ["C2S_DECODE"] = mode
         with K.Engine(path, device=rank, max_tokens=256, tp=(rank, world, nid)) as e:
-            nx = e.ingest_from(0, prompt)
-            lg = e.compute_logits()
-            toks = e.generate(STEPS, stop_on_special=False)
-            q.put((rank, nx, lg, np.asarray(toks), e.seq_len, None))
+            nx, lg, ids, sl = _decode(e, prompt)
+            q.put((rank, nx, lg, ids, sl, None))
     except Exception as ex:  # reported to the parent, which fails the test
         q.put((rank, None, None, None, None, repr(ex)))
 
 
-@pytest.mark.gpu
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_one_gpu(model_cache):
-    path = synth.cached_model("qwen7b", layers=2, cache_dir=model_cache)
-    prompt = np.random.default_rng(2).integers(0, 151643, 16).astype(np.int32)
-    e1 = K.Engine(path, device=0, max_tokens=256)
-    nx1 = e1.ingest_from(0, prompt)
-    toks1 = np.asarray(e1.generate(STEPS, stop_on_special=False))
-    world = 2
+def _run_group(world, path, prompt, mode):
     nid = KE.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, nid, path, prompt, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, nid, path, prompt, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -60,6 +65,22 @@ def test_tp2_matches_one_gpu(model_cache):
                 p.kill()
     for r in range(world):
         assert res[r][5] is None, res[r][5]
+    return res
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["persistent", "graph"])
+def test_tp2_matches_one_gpu(model_cache, mode):
+    """mode: the decode kernels of the group -- the persistent kernel with
+    the o-proj / down reduction over NVLink peer memory, or the per-phase
+    kernels with NCCL collectives."""
+    path = synth.cached_model("qwen7b", layers=2, cache_dir=model_cache)
+    prompt = np.random.default_rng(2).integers(0, 151643, 16).astype(np.int32)
+    e1 = K.Engine(path, device=0, max_tokens=256)
+    nx1, _, ids1, sl1 = _decode(e1, prompt)
+    world = 2
+    res = _run_group(world, path, prompt, mode)
     (_, nxa, lga, ta, sla, _), (_, nxb, lgb, tb, slb, _) = res[0], res[1]
     # the ranks agree exactly
     assert np.array_equal(nxa, nxb) and np.array_equal(lga, lgb) and np.array_equal(ta, tb) and sla == slb
@@ -70,8 +91,10 @@ def test_tp2_matches_one_gpu(model_cache):
     # the K-quant output projection, so raw logits are not compared)
     lg1 = e1.compute_logits(nxa)
     e1.close()
-    print(f"normx {rel(nxa, nx1):.2e} logits-on-same-normx {rel(lga, lg1):.2e} "
-          f"ids tp {ta.tolist()} one {toks1.tolist()}")
+    print(f"{mode}: normx {rel(nxa, nx1):.2e} logits-on-same-normx {rel(lga, lg1):.2e} "
+          f"ids tp {ta.tolist()} one {ids1.tolist()}")
     assert rel(nxa, nx1) <= TOL
     assert rel(lga, lg1) <= 1e-5
-    assert sla == 16 + STEPS
+    assert sla == sl1 == 16 + 2 * STEPS + 3
+    same = next((i for i in range(len(ids1)) if ta[i] != ids1[i]), len(ids1))
+    assert same >= 4  # 2 layers: greedy ids agree well past the first steps
