@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--model", default="qwen05b")
     ap.add_argument("--profile-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B tensor-parallel line (config 3)")
+    ap.add_argument("--tp-ctx", type=int, default=4096, help="config 3 context length before decoding")
+    ap.add_argument("--tp-steps", type=int, default=256, help="config 3 decode steps")
     return ap.parse_args()
 
 
@@ -347,11 +350,70 @@ def run_ours(args) -> None:
             "gpu_launches": launches,
             "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
     eng.close()
+    tp7b = None
+    if not args.no_tp7b:
+        tp7b = run_tp7b(args, world, rank, local, dist)
+    if rank == 0:
+        if tp7b is not None:
+            line["tp7b"] = tp7b
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_tp7b(args, world: int, rank: int, local: int, dist) -> dict:
+    """the 7B-shaped model tensor-parallel over the run's
+    GPUs (one rank per GPU; one GPU runs the whole model), context prefilled
+    to --tp-ctx positions from a uniform-random prompt (seed 2), then
+    --tp-steps greedy decode steps timed on the device (max over ranks).
+    Strong scaling: one request stream whatever the GPU count."""
+    import numpy as np
+    import torch
+    import c2slm_b200 as K
+    import c2slm_b200.engine as KE
+    from c2slm_b200 import synth
+
+    if rank == 0:
+        synth.cached_model("qwen7b")
+    nid = None
+    if world > 1:
+        dist.barrier()
+        obj = [KE.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    path = synth.cached_model("qwen7b")
+    ctx, steps = args.tp_ctx, args.tp_steps
+    eng = K.Engine(path, device=local, max_tokens=ctx + steps + 16, tp=(rank, world, nid) if world > 1 else None)
+    prompt = np.random.default_rng(2).integers(0, 151643, ctx).astype(np.int32)
+    t0 = time.perf_counter()
+    eng.ingest_from(0, prompt)
+    prefill_s = time.perf_counter() - t0
+    eng.bench_decode_timed(3, PENALTY, WINDOW, period=0)
+    eng.seq_len = ctx
+    torch.cuda.synchronize()
+    ms = eng.bench_decode_timed(steps, PENALTY, WINDOW, period=steps)
+    launches = eng.decode_launches(steps)
+    eng.close()
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    sb = stage_bytes(path)
+    per_token = sum(sb[k] for k in ("qkv", "o_proj", "gate_up", "down", "logits")) + \
+        sb["kv_per_pos"] * (ctx + steps / 2.0 + 1)
+    peak, kind = measured_peaks()
+    tok_s = steps / (ms / 1000.0)
+    per_gpu = per_token * tok_s / world / 1e9
+    return {"metric": "batch-1 greedy decode tokens/s, Qwen2.5-7B-shaped Q4_K_M (config 3), tensor parallel",
+            "value": round(tok_s, 2), "unit": "tokens/s", "n_gpus": world, "scaling": "strong",
+            "ms_per_step": round(ms / steps, 4), "context": ctx, "steps": steps,
+            "bytes_per_token": int(per_token), "achieved_gbs_per_gpu": round(per_gpu, 1),
+            "frac_per_gpu": round(per_gpu / peak, 4), "peak_kind": f"{kind} hbm_gbs",
+            "gpu_launches": launches, "prefill_s": round(prefill_s, 1),
+            "decode": "persistent kernel, partial sums exchanged over NVLink peer memory" if launches == 1
+                      else "per-phase kernels with NCCL collectives"}
 
 
 def eng_seq_wrap(i: int) -> bool:
