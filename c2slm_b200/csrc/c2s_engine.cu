@@ -890,7 +890,7 @@ int persistent_setup(c2s_engine *e) {
   const size_t at_act = (static_cast<size_t>(4) * SUB * hd + 2 * static_cast<size_t>(qpk) * hd + 2 * hd +
                          static_cast<size_t>(qpk) * SUB) * 4;
   const size_t act = a16(std::max(mv_act, at_act));
-  const size_t budget = 227 * 1024 - 4096;  // dynamic smem; static smem of the kernel is < 4 KB
+  const size_t budget = 227 * 1024 - 8192;  // dynamic smem; static smem of the kernel is < 8 KB
   // weight ring: a few large slots (each warp consumes many rows per slot)
   int slot_kb = 48;
   if (const char *sk = getenv("C2S_SLOT_KB")) slot_kb = std::max(8, std::min(96, atoi(sk)));

@@ -23,6 +23,7 @@ struct DevState {
   unsigned err;
   unsigned logits_counter;
   unsigned attn_counter[64];
+  unsigned attn_done[64];          // splits done combining (persistent decode)
   unsigned xbar;                   // cross-GPU barriers completed (tensor-parallel persistent decode)
 };
 
@@ -691,6 +692,12 @@ __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int 
 
 __host__ __device__ inline int attn_sub(int hd) { return 4096 / hd; }
 
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Scores of positions a .. a+len-1 (rows of kb) for the qpk (<= 8) heads of
 // a group: one warp per position, lane l holds d = l*E .. l*E+E-1 of q and
 // k; the 8 head dots are reduced together by a transposing butterfly, after
@@ -732,7 +739,11 @@ struct AttnJob {
   float *kc, *vc;                  // cache planes of this layer and kv head: row p at [p * hd]
   const float *rope_cs, *rope_sn;  // RoPE row of pos (hd/2 each), or null outside the table
   float *out, *part;               // head h0 + j of this item at out[(h0 + j) * hd]
-  unsigned *counter;               // arrivals of the group's splits (last one combines)
+  unsigned *counter;               // arrivals of the group's splits
+  unsigned *done;                  // distributed combine: splits that finished combining
+  int dist;                        // 1: every split combines a slice of the outputs once all have
+                                   // arrived (the group's CTAs are co-resident); 0: the last one
+                                   // combines them all
   int g, s, nsplit, p0, p1, pos, h0;
   int hd, qpk, max_splits;
   float eps, scale;
@@ -895,28 +906,86 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
   }
   __threadfence();
   csync();
+  const int ns = J.nsplit;
   if (tid == 0) {
     const unsigned t = atomicAdd(J.counter, 1u);
-    s_last = (t == static_cast<unsigned>(J.nsplit - 1)) ? 1 : 0;
+    s_last = (t == static_cast<unsigned>(ns - 1)) ? 1 : 0;
+    if (J.dist) {  // wait (bounded) for every split of the group
+      const long long t0 = clock64();
+      for (uint32_t it = 0; ld_acquire_gpu_u32(J.counter) < static_cast<unsigned>(ns); ++it)
+        if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+          atomicOr(err, kErrCounter);
+          ok = false;
+          break;
+        }
+      s_last = 1;
+    }
   }
   csync();
   if (!s_last) return ok;
   __threadfence();
-  for (int i = tid; i < qpk * hd; i += kThreads) {
-    const int h = h0 + i / hd, d = i % hd;
-    const float *base = J.part + static_cast<size_t>(h) * J.max_splits * (hd + 2);
-    float M = -INFINITY;
-    for (int k = 0; k < J.nsplit; ++k) M = fmaxf(M, __ldcg(base + static_cast<size_t>(k) * (hd + 2)));
-    float L = 0.f, O = 0.f;
-    for (int k = 0; k < J.nsplit; ++k) {
-      const float *pk = base + static_cast<size_t>(k) * (hd + 2);
-      const float w = static_cast<float>(exp(static_cast<double>(__fsub_rn(__ldcg(pk), M))));
-      L = fmaf(w, __ldcg(pk + 1), L);
-      O = fmaf(w, __ldcg(pk + 2 + d), O);
-    }
-    J.out[h * hd + d] = O / L;
+  // outputs combined here: all of them, or this split's slice
+  int o_lo = 0, o_hi = qpk * hd;
+  if (J.dist) seg_rows(qpk * hd, J.s, ns, o_lo, o_hi);
+  // combine the splits: per (head, split) weight w = exp(m_k - M) once, then
+  // each output sums w_k * acc_k[d] over k in split order
+  float *wk = kbuf;  // [qpk][nsplit] weights | [qpk][nsplit] l | [qpk][hd] sums (the staging buffers are free now)
+  __shared__ float s_M[8], s_L[8];
+  float *lk = wk + qpk * ns;
+  auto part_of = [&](int h, int k) {
+    return J.part + (static_cast<size_t>(h0 + h) * J.max_splits + k) * (hd + 2);
+  };
+  for (int t = tid; t < qpk * ns; t += kThreads) {  // every split's (m, l) in one round of loads
+    const int h = t / ns, k = t - h * ns;
+    wk[t] = __ldcg(part_of(h, k));
+    lk[t] = __ldcg(part_of(h, k) + 1);
   }
-  if (tid == 0) *J.counter = 0;
+  csync();
+  if (tid < qpk) {
+    float M = -INFINITY;
+    for (int k = 0; k < ns; ++k) M = fmaxf(M, wk[tid * ns + k]);
+    s_M[tid] = M;
+  }
+  csync();
+  for (int t = tid; t < qpk * ns; t += kThreads) {
+    const int h = t / ns;
+    wk[t] = static_cast<float>(exp(static_cast<double>(__fsub_rn(wk[t], s_M[h]))));
+  }
+  csync();
+  if (tid < qpk) {
+    float L = 0.f;
+    for (int k = 0; k < ns; ++k) L = fmaf(wk[tid * ns + k], lk[tid * ns + k], L);
+    s_L[tid] = L;
+  }
+  for (int i = o_lo + tid; i < o_hi; i += kThreads) {
+    const int h = i / hd, d = i - h * hd;
+    const float *w = wk + h * ns;
+    float O = 0.f;
+    int k = 0;
+    for (; k + 8 <= ns; k += 8) {  // eight loads in flight, then the fixed-order sum
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __ldcg(part_of(h, k + j) + 2 + d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) O = fmaf(w[k + j], v[j], O);
+    }
+    for (; k < ns; ++k) O = fmaf(w[k], __ldcg(part_of(h, k) + 2 + d), O);
+    wk[2 * qpk * ns + i] = O;  // staged: L is complete only after the next barrier
+  }
+  csync();
+  for (int i = o_lo + tid; i < o_hi; i += kThreads) {
+    const int h = i / hd;
+    J.out[(h0 + h) * hd + (i - h * hd)] = wk[2 * qpk * ns + i] / s_L[h];
+  }
+  if (J.dist) {  // the last split to finish returns both counters to zero
+    csync();
+    if (tid == 0 && atomicAdd(J.done, 1u) == static_cast<unsigned>(ns - 1)) {
+      *J.counter = 0;
+      *J.done = 0;
+    }
+  } else if (tid == 0) {
+    *J.counter = 0;
+  }
   return ok;
 }
 
@@ -971,6 +1040,8 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   J.out = A.out;
   J.part = A.part;
   J.counter = &st->attn_counter[g];
+  J.done = nullptr;
+  J.dist = 0;  // the CTAs of a launch are not guaranteed to be co-resident
   J.g = g;
   J.s = s;
   J.nsplit = nsplit;

@@ -367,6 +367,8 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   J.out = P.attn_out;
   J.part = P.part;
   J.counter = &st->attn_counter[g];
+  J.done = &st->attn_done[g];
+  J.dist = 1;  // cooperative launch: all CTAs are resident
   J.g = g;
   J.s = s;
   J.nsplit = nsplit;

@@ -280,6 +280,31 @@ def test_large_shapes_reduced_depth(model_cache, name):
         assert_greedy_parity(got, want, m, mx, 8)
 
 
+@pytest.mark.slow
+def test_long_context_split_attention(model_cache, monkeypatch):
+    """Contexts longer than one attention split (head_dim 128: 128 positions
+    per split at this capacity): the splits' partial softmax sums are combined
+    by the last split of each kv head.  Against the oracle after a 400-token
+    prompt, and the persistent and per-phase decode paths against each other
+    while the context grows past further split boundaries."""
+    path = synth.cached_model("qwen15b", layers=2, cache_dir=model_cache)
+    prompt = np.random.default_rng(5).integers(0, 151643, 400).astype(np.int32)
+    with K.Engine(path, max_tokens=1024) as e, O.OracleModel(path, max_tokens=1024, nthreads=16) as o:
+        nx_g = e.ingest_from(0, prompt)
+        nx_o = o.ingest_from(0, prompt)
+        assert rel(nx_g, nx_o) <= TOL
+        assert rel(e.compute_logits(), o.compute_logits(nx_g)) <= 1e-5
+    out = {}
+    for mode in ("graph", "persistent"):
+        monkeypatch.setenv("C2S_DECODE", mode)
+        with K.Engine(path, max_tokens=1024) as e:
+            e.ingest_from(0, prompt[:250])
+            toks = e.generate(24, stop_on_special=False)  # positions 250..273: splits 1 -> 2 -> 3
+            out[mode] = (toks, e.compute_logits())
+    assert np.array_equal(out["graph"][0], out["persistent"][0])
+    assert np.array_equal(out["graph"][1], out["persistent"][1])
+
+
 @pytest.mark.parametrize("name", ["tiny05", "tiny15", "tiny7", "tiny3"])
 def test_persistent_decode_equals_graph_decode(models, name, monkeypatch):
     """The persistent decode kernel and the per-phase CUDA-graph path run the
