@@ -886,9 +886,8 @@ int persistent_setup(c2s_engine *e) {
   P.off_y = P.off_q8 + static_cast<int>(a16(q8b));
   P.yrows = yrows;
   const size_t mv_act = static_cast<size_t>(P.off_y) + static_cast<size_t>(kMaxSegs) * yrows * 4;
-  const int qpk = d.n_heads / d.n_kv_heads, SUB = attn_sub(hd);
-  const size_t at_act = (static_cast<size_t>(4) * SUB * hd + 2 * static_cast<size_t>(qpk) * hd + 2 * hd +
-                         static_cast<size_t>(qpk) * SUB) * 4;
+  const int qpk = d.n_heads / d.n_kv_heads;
+  const size_t at_act = attn_smem_bytes(hd, qpk);
   const size_t act = a16(std::max(mv_act, at_act));
   const size_t budget = 227 * 1024 - 8192;  // dynamic smem; static smem of the kernel is < 8 KB
   // weight ring: a few large slots (each warp consumes many rows per slot)
@@ -914,7 +913,7 @@ int persistent_setup(c2s_engine *e) {
   P.off_empty = static_cast<int>(off);
   off += 8 * nslot;
   P.off_abar = static_cast<int>(off);
-  off += 16;
+  off += 8 * kAttnBufs;
   off = (off + 127) & ~size_t(127);
   P.off_act = static_cast<int>(off);
   e->p_smem = off + act;
@@ -1162,11 +1161,7 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   const int qpk = d.n_heads / d.n_kv_heads;
   if (qpk > 8) return fail(C2S_ERR_UNSUPPORTED, "more than 8 query heads per kv head");
   if (hd != 64 && hd != 128) return fail(C2S_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
-  {
-    const int SUB = attn_sub(hd);
-    e->attn_smem = (static_cast<size_t>(4) * SUB * hd + 2 * static_cast<size_t>(qpk) * hd + 2 * hd +
-                    static_cast<size_t>(qpk) * SUB) * 4;
-  }
+  e->attn_smem = attn_smem_bytes(hd, qpk);
   if (e->attn_smem > 200 * 1024) return fail(C2S_ERR_UNSUPPORTED, "attention smem %zu too large", e->attn_smem);
   auto dalloc = [&](void **p, size_t bytes) -> int {
     if (cudaMalloc(p, bytes) != cudaSuccess) return fail(C2S_ERR_OOM, "cudaMalloc(%zu) failed", bytes);

@@ -22,8 +22,7 @@ struct DevState {
   int im_end, eos, vocab;
   unsigned err;
   unsigned logits_counter;
-  unsigned attn_counter[64];
-  unsigned attn_done[64];          // splits done combining (persistent decode)
+  unsigned attn_counter[64];       // arrivals of a kv head's attention splits
   unsigned xbar;                   // cross-GPU barriers completed (tensor-parallel persistent decode)
 };
 
@@ -690,7 +689,14 @@ __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int 
   __syncwarp();
 }
 
+// staged rows per K/V sub-chunk (16 KB), and the attention's shared memory
+constexpr int kAttnBufs = 4;
 __host__ __device__ inline int attn_sub(int hd) { return 4096 / hd; }
+__host__ __device__ inline size_t attn_smem_bytes(int hd, int qpk) {
+  const size_t sub = static_cast<size_t>(attn_sub(hd));
+  return (kAttnBufs * sub * hd + static_cast<size_t>(qpk) * hd + 2 * static_cast<size_t>(hd) +
+          static_cast<size_t>(qpk) * kAttnBufs * sub) * 4;
+}
 
 __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned *p) {
   unsigned v;
@@ -698,34 +704,70 @@ __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned *p) {
   return v;
 }
 
+// E consecutive floats of shared memory (16-B aligned for E = 4, 8-B for
+// E = 2) in one vector load
+template <int E>
+__device__ __forceinline__ void lds_vec(const float *p, float (&v)[E]) {
+  if constexpr (E == 4) {
+    const float4 t = *reinterpret_cast<const float4 *>(p);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else if constexpr (E == 2) {
+    const float2 t = *reinterpret_cast<const float2 *>(p);
+    v[0] = t.x, v[1] = t.y;
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) v[j] = p[j];
+  }
+}
+
 // Scores of positions a .. a+len-1 (rows of kb) for the qpk (<= 8) heads of
-// a group: one warp per position, lane l holds d = l*E .. l*E+E-1 of q and
-// k; the 8 head dots are reduced together by a transposing butterfly, after
-// which lane 4h holds head h.
+// a group: warp w takes positions w, w + 8, ..., four at a time; lane l
+// holds d = l*E .. l*E+E-1 of q and k; the 8 head dots of a position are
+// reduced together by a transposing butterfly, after which lane 4h holds
+// head h.  The four positions' butterflies are independent and interleave.
 template <int E>
 __device__ __forceinline__ void attn_scores(const float *qs, const float *kb, int len, int qpk, float scale,
-                                            float *sc, int SUB) {
+                                            float *sc, int stride) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, hd = 32 * E;
   float qr[8][E];
 #pragma unroll
-  for (int h = 0; h < 8; ++h)
+  for (int h = 0; h < 8; ++h) {
+    if (h < qpk) {
+      lds_vec<E>(qs + h * hd + lane * E, qr[h]);
+    } else {
 #pragma unroll
-    for (int j = 0; j < E; ++j) qr[h][j] = h < qpk ? qs[h * hd + lane * E + j] : 0.f;
-  for (int t = warp; t < len; t += kWarps) {
-    float kv[E];
-#pragma unroll
-    for (int j = 0; j < E; ++j) kv[j] = kb[t * hd + lane * E + j];
-    float dot[8];
-#pragma unroll
-    for (int h = 0; h < 8; ++h) {
-      float d0 = 0.f;
-#pragma unroll
-      for (int j = 0; j < E; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
-      dot[h] = d0;
+      for (int j = 0; j < E; ++j) qr[h][j] = 0.f;
     }
-    const float v = reduce_rows<8>(dot);
-    const int h = lane >> 2;
-    if ((lane & 3) == 0 && h < qpk) sc[h * SUB + t] = __fmul_rn(v, scale);
+  }
+  const int h = lane >> 2;
+  for (int t0 = warp; t0 < len; t0 += 4 * kWarps) {
+    float dot[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u * kWarps;
+      float kv[E];
+      if (t < len) {
+        lds_vec<E>(kb + t * hd + lane * E, kv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < E; ++j) kv[j] = 0.f;
+      }
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) {
+        float d0 = 0.f;
+#pragma unroll
+        for (int j = 0; j < E; ++j) d0 = fmaf(qr[hh][j], kv[j], d0);
+        dot[u][hh] = d0;
+      }
+    }
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = reduce_rows<8>(dot[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u * kWarps;
+      if ((lane & 3) == 0 && h < qpk && t < len) sc[h * stride + t] = __fmul_rn(v[u], scale);
+    }
   }
 }
 
@@ -740,62 +782,79 @@ struct AttnJob {
   const float *rope_cs, *rope_sn;  // RoPE row of pos (hd/2 each), or null outside the table
   float *out, *part;               // head h0 + j of this item at out[(h0 + j) * hd]
   unsigned *counter;               // arrivals of the group's splits
-  unsigned *done;                  // distributed combine: splits that finished combining
   int dist;                        // 1: every split combines a slice of the outputs once all have
-                                   // arrived (the group's CTAs are co-resident); 0: the last one
-                                   // combines them all
+                                   // arrived (the group's CTAs are co-resident; the caller clears
+                                   // the counter after its next grid barrier); 0: the last one
+                                   // combines them all and clears the counter
   int g, s, nsplit, p0, p1, pos, h0;
   int hd, qpk, max_splits;
   float eps, scale;
 };
 
-// Shared memory: asmem holds [2][SUB][hd] K, [2][SUB][hd] V, [qpk][hd] q,
-// [hd] k, [hd] v, [qpk][SUB] scores.  bars[2] are the staging barriers;
-// uses[2] counts their completed phases (kept by the caller across items).
-// Warp h owns head h for the softmax and the weighted sum of V, with its
-// accumulators in registers.  Returns false if a bounded wait expired.
+// Shared memory: asmem holds [kAttnBufs][SUB][hd] staged K or V rows,
+// [qpk][hd] q, [hd] k, [hd] v, [qpk][WIN] scores / weights.  bars[] are the
+// staging barriers (one per buffer); uses[] counts their completed phases
+// (kept by the caller across items).
+//
+// The split is taken in windows of WIN = kAttnBufs * SUB positions; each
+// window is two passes over the staged rows: the scores of every position
+// (K), one softmax over the window per head (warp h owns head h, exp in
+// float64), then the weighted sum of V.  Windows after the first rescale the
+// running (m, l, acc) as in an online softmax; at the split lengths the
+// engine uses (<= WIN) there is one window.  K and V sub-chunks of all
+// windows form one load sequence through the buffers, kAttnBufs in flight.
+// Returns false if a bounded wait expired.
 template <int E>
-__device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[2], unsigned *err) {
+__device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[kAttnBufs], unsigned *err) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int hd = 32 * E;
-  const int qpk = J.qpk, SUB = attn_sub(hd), pos = J.pos, p0 = J.p0, p1 = J.p1;
-  float *kbuf = asmem, *vbuf = kbuf + 2 * SUB * hd, *qs = vbuf + 2 * SUB * hd;
+  constexpr int NB = kAttnBufs;
+  const int qpk = J.qpk, SUB = attn_sub(hd), WIN = NB * SUB, pos = J.pos, p0 = J.p0, p1 = J.p1;
+  float *buf = asmem, *qs = buf + NB * SUB * hd;
   float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd;
-  __shared__ float s_m[8], s_l[8];
   __shared__ int s_last;
-  const int n_sub = (p1 - p0 + SUB - 1) / SUB;
-  // stage the cached rows (positions < pos) of sub-chunk it into buffer it&1
-  auto cached_rows = [&](int it) {
-    const int a = p0 + it * SUB, b = min(p1, a + SUB);
-    return max(0, min(b, pos) - a);
+  const int nwin = (p1 - p0 + WIN - 1) / WIN;
+  // load q of the sequence: window w, K (r < nsw) or V, sub-chunk r mod nsw
+  struct Ld {
+    int a, b, v;  // positions [a, b) of one plane (v: 1 = V)
   };
-  auto issue = [&](int it) {
-    const int cached = cached_rows(it);
-    if (cached > 0) {
-      const int a = p0 + it * SUB;
-      const uint32_t bytes = static_cast<uint32_t>(cached) * hd * 4;
-      uint64_t *bar = &bars[it & 1];
-      mbar_arrive_expect_tx(bar, 2 * bytes);
-      bulk_g2s(kbuf + (it & 1) * SUB * hd, J.kc + static_cast<size_t>(a) * hd, bytes, bar);
-      bulk_g2s(vbuf + (it & 1) * SUB * hd, J.vc + static_cast<size_t>(a) * hd, bytes, bar);
+  auto load_of = [&](int q) {
+    int w = q / (2 * NB);
+    if (w > nwin - 1) w = nwin - 1;
+    const int wa = p0 + w * WIN, wb = min(p1, wa + WIN);
+    const int nsw = (wb - wa + SUB - 1) / SUB, r = q - w * 2 * NB;
+    const int sub = r >= nsw ? r - nsw : r;
+    Ld L;
+    L.a = wa + sub * SUB;
+    L.b = min(wb, L.a + SUB);
+    L.v = r >= nsw ? 1 : 0;
+    return L;
+  };
+  const int last_w = p0 + (nwin - 1) * WIN;
+  const int n_loads = (nwin - 1) * 2 * NB + 2 * ((min(p1, last_w + WIN) - last_w + SUB - 1) / SUB);
+  // rows below pos come from the cache; row pos is this token's k / v
+  auto cached = [&](const Ld &L) { return max(0, min(L.b, pos) - L.a); };
+  auto issue = [&](int q) {
+    const Ld L = load_of(q);
+    const int n = cached(L);
+    if (n > 0) {
+      const uint32_t bytes = static_cast<uint32_t>(n) * hd * 4;
+      uint64_t *bar = &bars[q % NB];
+      mbar_arrive_expect_tx(bar, bytes);
+      bulk_g2s(buf + (q % NB) * SUB * hd, (L.v ? J.vc : J.kc) + static_cast<size_t>(L.a) * hd, bytes, bar);
     }
   };
   if (tid == 0) {
     // cache rows this CTA stored in earlier calls, and staging rows it wrote,
     // are next accessed by the async proxy
     asm volatile("fence.proxy.async;" ::: "memory");
-    issue(0);
-    if (n_sub > 1) issue(1);
+    for (int q = 0; q < NB && q < n_loads; ++q) issue(q);
   }
   // projections: every load in flight at once
   for (int i = tid; i < qpk * hd; i += kThreads) qs[i] = __ldcg(J.q + i);
   for (int i = tid; i < hd; i += kThreads) {
     knew[i] = __ldcg(J.k + i);
     vnew[i] = __ldcg(J.v + i);
-  }
-  if (tid < 8) {
-    s_m[tid] = -INFINITY;
-    s_l[tid] = 0.f;
   }
   csync();
   if (J.q_norm || J.k_norm) {  // Qwen3 per-head QK-norm (engine/forward.go:80-91)
@@ -821,85 +880,115 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
       J.kc[static_cast<size_t>(pos) * hd + i] = knew[i];
       J.vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
     }
-  float acc[E];  // warp h: head h, d = lane*E .. lane*E+E-1
+  // running softmax state of head h = warp (every lane holds m and l)
+  float m = -INFINITY, l = 0.f, acc[E];  // acc: d = lane*E .. lane*E+E-1
 #pragma unroll
   for (int j = 0; j < E; ++j) acc[j] = 0.f;
   bool ok = true;
-  for (int it = 0; it < n_sub; ++it) {
-    const int a = p0 + it * SUB, b = min(p1, a + SUB), len = b - a;
-    float *kb = kbuf + (it & 1) * SUB * hd;
-    float *vb = vbuf + (it & 1) * SUB * hd;
-    if (cached_rows(it) > 0) {  // completions of a buffer's barrier alternate parity
-      ok = mbar_wait_bounded(&bars[it & 1], uses[it & 1] & 1u, err) && ok;
-      uses[it & 1] += 1;
+  // wait for load q (if it reads the cache), complete it with row pos, and
+  // return its buffer
+  auto arrive = [&](int q, const Ld &L) {
+    float *b = buf + (q % NB) * SUB * hd;
+    if (cached(L) > 0) {  // completions of a buffer's barrier alternate parity
+      ok = mbar_wait_bounded(&bars[q % NB], uses[q % NB] & 1u, err) && ok;
+      uses[q % NB] += 1;
     }
-    if (pos >= a && pos < b) {  // this token's k, v complete the staged rows
-      for (int i = tid; i < hd; i += kThreads) {
-        kb[(pos - a) * hd + i] = knew[i];
-        vb[(pos - a) * hd + i] = vnew[i];
-      }
+    if (pos >= L.a && pos < L.b) {
+      const float *src = L.v ? vnew : knew;
+      for (int i = tid; i < hd; i += kThreads) b[(pos - L.a) * hd + i] = src[i];
       csync();
     }
-    attn_scores<E>(qs, kb, len, qpk, J.scale, sc, SUB);
+    return b;
+  };
+  // after every warp is done with load q's buffer: reuse it for load q + NB
+  auto release = [&](int q) {
     csync();
-    if (warp < qpk) {
-      // online softmax of head h = warp (exp in float64), then V
-      const int h = warp;
-      float m = -INFINITY;
-      for (int t = lane; t < len; t += 32) m = fmaxf(m, sc[h * SUB + t]);
-      m = warp_max(m);
-      const float m_old = s_m[h], m_new = fmaxf(m_old, m);
-      float l = 0.f;
-      for (int t = lane; t < len; t += 32) {
-        const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sc[h * SUB + t], m_new))));
-        sc[h * SUB + t] = e;
-        l += e;
-      }
-      l = warp_sum(l);
-      const float scale = static_cast<float>(exp(static_cast<double>(m_old - m_new)));
-      __syncwarp();
-      float a0[E], a1[E];
-#pragma unroll
-      for (int j = 0; j < E; ++j) a0[j] = a1[j] = 0.f;
-      const float *e = sc + h * SUB;
-      int t = 0;
-      for (; t + 1 < len; t += 2) {
-        const float e0 = e[t], e1 = e[t + 1];
-#pragma unroll
-        for (int j = 0; j < E; ++j) {
-          a0[j] = fmaf(e0, vb[t * hd + lane * E + j], a0[j]);
-          a1[j] = fmaf(e1, vb[(t + 1) * hd + lane * E + j], a1[j]);
-        }
-      }
-      if (t < len)
-#pragma unroll
-        for (int j = 0; j < E; ++j) a0[j] = fmaf(e[t], vb[t * hd + lane * E + j], a0[j]);
-#pragma unroll
-      for (int j = 0; j < E; ++j) acc[j] = acc[j] * scale + (a0[j] + a1[j]);
-      if (lane == 0) {
-        s_l[h] = s_l[h] * scale + l;
-        s_m[h] = m_new;
-      }
-    }
-    csync();
-    if (tid == 0 && it + 2 < n_sub) {
+    if (tid == 0 && q + NB < n_loads) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(it + 2);
+      issue(q + NB);
+    }
+  };
+  int q = 0;
+  for (int w = 0; w < nwin; ++w) {
+    const int wa = p0 + w * WIN, wb = min(p1, wa + WIN), len = wb - wa;
+    const int nsw = (len + SUB - 1) / SUB;
+    for (int r = 0; r < nsw; ++r, ++q) {  // pass 1: scores of the window
+      const Ld L = load_of(q);
+      const float *kb = arrive(q, L);
+      attn_scores<E>(qs, kb, L.b - L.a, qpk, J.scale, sc + (L.a - wa), WIN);
+      release(q);
+    }
+    if (warp < qpk) {  // softmax of the window for head h = warp
+      const float *sh = sc + warp * WIN;
+      float mw = -INFINITY;
+#pragma unroll 4
+      for (int t = lane; t < len; t += 32) mw = fmaxf(mw, sh[t]);
+      mw = warp_max(mw);
+      const float m_new = fmaxf(m, mw);
+      float lw = 0.f;
+#pragma unroll 1
+      for (int t = lane; t < len; t += 32) {
+        const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sh[t], m_new))));
+        sc[warp * WIN + t] = e;
+        lw += e;
+      }
+      lw = warp_sum(lw);
+      const float alpha = static_cast<float>(exp(static_cast<double>(m - m_new)));
+      l = l * alpha + lw;
+      m = m_new;
+#pragma unroll
+      for (int j = 0; j < E; ++j) acc[j] *= alpha;
+      __syncwarp();
+    }
+    for (int r = 0; r < nsw; ++r, ++q) {  // pass 2: weighted sum of V
+      const Ld L = load_of(q);
+      const float *vb = arrive(q, L);
+      if (warp < qpk) {
+        const float *e = sc + warp * WIN + (L.a - wa);
+        const int n = L.b - L.a;
+        // four interleaved partial sums (positions t mod 4), then combined
+        float a[4][E];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int j = 0; j < E; ++j) a[u][j] = 0.f;
+        int t = 0;
+        for (; t + 3 < n; t += 4) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float eu = e[t + u];
+            float vu[E];
+            lds_vec<E>(vb + (t + u) * hd + lane * E, vu);
+#pragma unroll
+            for (int j = 0; j < E; ++j) a[u][j] = fmaf(eu, vu[j], a[u][j]);
+          }
+        }
+        for (; t < n; ++t) {
+          const float et = e[t];
+          float vt[E];
+          lds_vec<E>(vb + t * hd + lane * E, vt);
+#pragma unroll
+          for (int j = 0; j < E; ++j) a[0][j] = fmaf(et, vt[j], a[0][j]);
+        }
+#pragma unroll
+        for (int j = 0; j < E; ++j) acc[j] += (a[0][j] + a[1][j]) + (a[2][j] + a[3][j]);
+      }
+      release(q);
     }
   }
   const int h0 = J.h0;
   if (J.nsplit == 1) {  // single split: normalise and write the heads directly
     if (warp < qpk)
 #pragma unroll
-      for (int j = 0; j < E; ++j) J.out[(h0 + warp) * hd + lane * E + j] = acc[j] / s_l[warp];
+      for (int j = 0; j < E; ++j) J.out[(h0 + warp) * hd + lane * E + j] = acc[j] / l;
     return ok;
   }
   // partial (m, l, acc) of this split; the last split of the group combines
   if (warp < qpk) {
     float *pp = J.part + (static_cast<size_t>(h0 + warp) * J.max_splits + J.s) * (hd + 2);
     if (lane == 0) {
-      pp[0] = s_m[warp];
-      pp[1] = s_l[warp];
+      pp[0] = m;
+      pp[1] = l;
     }
 #pragma unroll
     for (int j = 0; j < E; ++j) pp[2 + lane * E + j] = acc[j];
@@ -908,9 +997,8 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
   csync();
   const int ns = J.nsplit;
   if (tid == 0) {
-    const unsigned t = atomicAdd(J.counter, 1u);
-    s_last = (t == static_cast<unsigned>(ns - 1)) ? 1 : 0;
-    if (J.dist) {  // wait (bounded) for every split of the group
+    if (J.dist) {  // arrive, then wait (bounded) for every split of the group
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(J.counter) : "memory");
       const long long t0 = clock64();
       for (uint32_t it = 0; ld_acquire_gpu_u32(J.counter) < static_cast<unsigned>(ns); ++it)
         if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
@@ -919,88 +1007,106 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
           break;
         }
       s_last = 1;
+    } else {
+      const unsigned t = atomicAdd(J.counter, 1u);
+      s_last = (t == static_cast<unsigned>(ns - 1)) ? 1 : 0;
     }
   }
   csync();
   if (!s_last) return ok;
-  __threadfence();
+  if (!J.dist) __threadfence();  // (dist: thread 0's acquire load and the CTA barrier order the reads)
   // outputs combined here: all of them, or this split's slice
   int o_lo = 0, o_hi = qpk * hd;
   if (J.dist) seg_rows(qpk * hd, J.s, ns, o_lo, o_hi);
   // combine the splits: per (head, split) weight w = exp(m_k - M) once, then
-  // each output sums w_k * acc_k[d] over k in split order
-  float *wk = kbuf;  // [qpk][nsplit] weights | [qpk][nsplit] l | [qpk][hd] sums (the staging buffers are free now)
-  __shared__ float s_M[8], s_L[8];
-  float *lk = wk + qpk * ns;
+  // each output sums w_k * acc_k[d] over k in split order.  Shared memory
+  // (the K/V buffers are free now): [nh][ns] m then w | [nh][ns] l |
+  // [qpk * hd] sums | staged partial sums of a block of outputs
+  const int hlo = o_lo / hd, nh = (o_hi - 1) / hd + 1 - hlo;  // heads of the outputs
+  float *wm = buf, *wl = wm + nh * ns, *Os = wl + nh * ns, *stage = Os + qpk * hd;
+  __shared__ float s_L[8];
   auto part_of = [&](int h, int k) {
     return J.part + (static_cast<size_t>(h0 + h) * J.max_splits + k) * (hd + 2);
   };
-  for (int t = tid; t < qpk * ns; t += kThreads) {  // every split's (m, l) in one round of loads
-    const int h = t / ns, k = t - h * ns;
-    wk[t] = __ldcg(part_of(h, k));
-    lk[t] = __ldcg(part_of(h, k) + 1);
-  }
-  csync();
-  if (tid < qpk) {
-    float M = -INFINITY;
-    for (int k = 0; k < ns; ++k) M = fmaxf(M, wk[tid * ns + k]);
-    s_M[tid] = M;
-  }
-  csync();
-  for (int t = tid; t < qpk * ns; t += kThreads) {
-    const int h = t / ns;
-    wk[t] = static_cast<float>(exp(static_cast<double>(__fsub_rn(wk[t], s_M[h]))));
-  }
-  csync();
-  if (tid < qpk) {
-    float L = 0.f;
-    for (int k = 0; k < ns; ++k) L = fmaf(wk[tid * ns + k], lk[tid * ns + k], L);
-    s_L[tid] = L;
-  }
-  for (int i = o_lo + tid; i < o_hi; i += kThreads) {
-    const int h = i / hd, d = i - h * hd;
-    const float *w = wk + h * ns;
-    float O = 0.f;
-    int k = 0;
-    for (; k + 8 <= ns; k += 8) {  // eight loads in flight, then the fixed-order sum
-      float v[8];
+  const int cap = kAttnBufs * attn_sub(hd) * hd - static_cast<int>(stage - wm);
+  const int nbo = max(1, min(o_hi - o_lo, cap / ns));
+  // partial sums of outputs [ob, ob + cnt) of every split -> stage[k * cnt + i]
+  auto stage_block = [&](int ob, int cnt) {
+    const int tot = cnt * ns;
+    // t / cnt = umulhi(t, ceil(2^32 / cnt)) for t * cnt < 2^32 (cnt = 1: t)
+    const uint32_t magic = cnt > 1 ? 0xFFFFFFFFu / static_cast<uint32_t>(cnt) + 1u : 0u;
+    for (int t0 = 0; t0 < tot; t0 += 4 * kThreads) {
+      float v[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __ldcg(part_of(h, k + j) + 2 + d);
+      for (int j = 0; j < 4; ++j) {
+        const int t = t0 + j * kThreads + tid;
+        const int k = cnt > 1 ? static_cast<int>(__umulhi(static_cast<uint32_t>(t), magic)) : t;
+        const int i = ob + (t - k * cnt), h = i / hd;
+        v[j] = t < tot ? __ldcg(part_of(h, k) + 2 + (i - h * hd)) : 0.f;
+      }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) O = fmaf(w[k + j], v[j], O);
+      for (int j = 0; j < 4; ++j)
+        if (t0 + j * kThreads + tid < tot) stage[t0 + j * kThreads + tid] = v[j];
     }
-    for (; k < ns; ++k) O = fmaf(w[k], __ldcg(part_of(h, k) + 2 + d), O);
-    wk[2 * qpk * ns + i] = O;  // staged: L is complete only after the next barrier
+  };
+  // one round of L2 loads: every needed (m, l) and the first block's partials
+  for (int t = tid; t < nh * ns; t += kThreads) {
+    const int hh = t / ns, k = t - hh * ns;
+    wm[t] = __ldcg(part_of(hlo + hh, k));
+    wl[t] = __ldcg(part_of(hlo + hh, k) + 1);
+  }
+  stage_block(o_lo, min(nbo, o_hi - o_lo));
+  csync();
+  if (warp < nh) {  // warp hh: head hlo + hh
+    float *w = wm + warp * ns;
+    const float *lk = wl + warp * ns;
+    float M = -INFINITY;
+    for (int k = lane; k < ns; k += 32) M = fmaxf(M, w[k]);
+    M = warp_max(M);
+    float L = 0.f;
+#pragma unroll 1
+    for (int k = lane; k < ns; k += 32) {
+      const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(w[k], M))));
+      w[k] = e;
+      L = fmaf(e, lk[k], L);
+    }
+    L = warp_sum(L);
+    if (lane == 0) s_L[warp] = L;
   }
   csync();
+  for (int ob = o_lo; ob < o_hi; ob += nbo) {
+    const int cnt = min(nbo, o_hi - ob);
+    if (ob != o_lo) {
+      stage_block(ob, cnt);
+      csync();
+    }
+    for (int i = tid; i < cnt; i += kThreads) {  // each output sums its splits in order
+      const float *w = wm + ((ob + i) / hd - hlo) * ns;
+      float O = 0.f;
+      for (int k = 0; k < ns; ++k) O = fmaf(w[k], stage[k * cnt + i], O);
+      Os[ob + i] = O;
+    }
+    csync();
+  }
   for (int i = o_lo + tid; i < o_hi; i += kThreads) {
     const int h = i / hd;
-    J.out[(h0 + h) * hd + (i - h * hd)] = wk[2 * qpk * ns + i] / s_L[h];
+    J.out[(h0 + h) * hd + (i - h * hd)] = Os[i] / s_L[h - hlo];
   }
-  if (J.dist) {  // the last split to finish returns both counters to zero
-    csync();
-    if (tid == 0 && atomicAdd(J.done, 1u) == static_cast<unsigned>(ns - 1)) {
-      *J.counter = 0;
-      *J.done = 0;
-    }
-  } else if (tid == 0) {
-    *J.counter = 0;
-  }
+  if (!J.dist && tid == 0) *J.counter = 0;
   return ok;
 }
 
-__device__ __forceinline__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[2],
+__device__ __forceinline__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[kAttnBufs],
                                        unsigned *err) {
   return J.hd == 64 ? attend_t<2>(J, asmem, bars, uses, err) : attend_t<4>(J, asmem, bars, uses, err);
 }
 
 __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   extern __shared__ __align__(128) float asmem[];
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[kAttnBufs];
   const int tid = threadIdx.x;
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    for (int i = 0; i < kAttnBufs; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -1040,7 +1146,6 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   J.out = A.out;
   J.part = A.part;
   J.counter = &st->attn_counter[g];
-  J.done = nullptr;
   J.dist = 0;  // the CTAs of a launch are not guaranteed to be co-resident
   J.g = g;
   J.s = s;
@@ -1052,7 +1157,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   J.max_splits = A.max_splits;
   J.eps = A.eps;
   J.scale = A.scale;
-  uint32_t uses[2] = {0, 0};
+  uint32_t uses[kAttnBufs] = {};
   attend(J, asmem, bars, uses, &st->err);
 }
 

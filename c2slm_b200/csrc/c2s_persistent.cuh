@@ -335,7 +335,7 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
 // position ranges, so the CTA that stores a cache row is the one that reads
 // it in later steps.
 // ---------------------------------------------------------------------------
-__device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, uint64_t *abar, uint32_t (&uses)[2],
+__device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, uint64_t *abar, uint32_t (&uses)[kAttnBufs],
                             int item, int pos, const float *rope_row) {
   DevState *st = P.st;
   if (pos < 0 || pos >= P.max_tokens) {
@@ -367,7 +367,6 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   J.out = P.attn_out;
   J.part = P.part;
   J.counter = &st->attn_counter[g];
-  J.done = &st->attn_done[g];
   J.dist = 1;  // cooperative launch: all CTAs are resident
   J.g = g;
   J.s = s;
@@ -470,6 +469,9 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   const Q8KView q8{q8qs, q8d, q8bs};
   PhaseRows R;
   const int nchunks = phase_rows(ph, c, G, R);
+  // the attention's split arrivals of this layer: every split has finished
+  // waiting on them before the grid barrier this phase follows
+  if (ph.kind == K_OPROJ && tid == 0 && c < P.n_kv) st->attn_counter[c] = 0;
   const bool residual = ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN;
   const bool normed = ph.kind == K_QKV || ph.kind == K_FFN_UP || ph.kind == K_LOGITS;
   // ---- loads the epilogue needs, requested first
@@ -854,9 +856,11 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kWarps);  // every compute warp releases the slot
     }
-    mbar_init(&abar[0], 1);
-    mbar_init(&abar[1], 1);
+    for (int i = 0; i < kAttnBufs; ++i) mbar_init(&abar[i], 1);
     fence_mbar_init();
+    // split arrivals start from zero (a launch that stopped on an error may
+    // have left counts); the first attention phase follows a grid barrier
+    if (c < P.n_kv) st->attn_counter[c] = 0;
     s_stop = 0;
   }
   __syncthreads();
@@ -917,7 +921,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
 
   // -------------------------------------------------------------- compute
   uint32_t k_ring = 0;
-  uint32_t abar_uses[2] = {0, 0};
+  uint32_t abar_uses[kAttnBufs] = {};
   unsigned bar_target = 0;
   bool ok = true;
   unsigned xb = static_cast<unsigned>(ldst(reinterpret_cast<const int *>(&st->xbar)));  // cross-GPU barriers so far

@@ -184,6 +184,13 @@ __device__ __forceinline__ float limbs_dot_q5_0(const uint8_t *blk, const XLimbs
   return d * limbs_combine(A, B, C, L.s);
 }
 
+// 4-way dot of unsigned bytes (a) and signed bytes (b), plus c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 // Q4_K unit (superblock sb, sub-block pair j): activation of the unit
 struct Q4Act {
   int4 xa, xb, xc, xd;
@@ -208,36 +215,47 @@ __device__ __forceinline__ void load_q4act(const Q8KView &x, int u, bool ok, Q4A
   A.bs23 = static_cast<float>(bs.z + bs.w);
 }
 
+// Per-lane constants of the Q4_K unit a lane evaluates: sub-block pair
+// j = lane & 3 of its superblock (every row pass starts at a multiple of 32
+// units, so j is fixed for the lane).
+struct Q4Lane {
+  uint32_t sel_ab, sel_c;  // byte_perm selectors of the 6-bit scale/min bytes of pair j
+  uint32_t hi;             // j >= 2: scales split over the low and high bytes
+  int qoff;                // offset of the pair's 32 quant bytes
+};
+
+__device__ __forceinline__ Q4Lane q4_lane() {
+  const int j = threadIdx.x & 3;
+  Q4Lane K;
+  K.sel_ab = (j & 1) ? 0x7632u : 0x5410u;
+  K.sel_c = (j & 1) ? 0x3232u : 0x1010u;
+  K.hi = j >= 2 ? 1u : 0u;
+  K.qoff = 16 + 32 * j;
+  return K;
+}
+
 // f32 term of one Q4_K sub-block pair (internal/simd/
 // c2_tensor_dot_q4_k_q8_k_nosimd_gen.go:20-68); blk is 16-B aligned.
-__device__ __forceinline__ float unit_q4k_reg(const uint8_t *blk, int j, const Q4Act &A) {
+// The 6-bit scales and mins of sub-blocks 2j, 2j+1 (tensor/ops.go:354-361)
+// are unpacked together: W = [sc0, sc1, m0, m1] as bytes.
+__device__ __forceinline__ float unit_q4k_reg(const uint8_t *blk, const Q4Lane &K, const Q4Act &A) {
   const uint4 h = *reinterpret_cast<const uint4 *>(blk);  // d, dmin, scales[0..11]
-  const float d = h2f(static_cast<uint16_t>(h.x & 0xffffu));
-  const float dmin = h2f(static_cast<uint16_t>(h.x >> 16));
-  // scales bytes s[0..11] = h.y, h.z, h.w (tensor/ops.go:354-361)
-  const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
-  auto byte = [](uint32_t w, int k) { return (w >> (8 * k)) & 0xFFu; };
-  int sc0, m0, sc1, m1;
-  if (j < 2) {
-    const uint32_t sw = s03 >> (16 * j), mw = s47 >> (16 * j);
-    sc0 = byte(sw, 0) & 63;
-    sc1 = byte(sw, 1) & 63;
-    m0 = byte(mw, 0) & 63;
-    m1 = byte(mw, 1) & 63;
-  } else {
-    const int k = j - 2;
-    const uint32_t hw = s811 >> (16 * k);     // s[i+4] for i = 2j, 2j+1
-    const uint32_t lw = s03 >> (16 * k);      // s[i-4]
-    const uint32_t mw = s47 >> (16 * k);      // s[i]
-    sc0 = static_cast<int>((byte(hw, 0) & 15) | ((byte(lw, 0) >> 6) << 4));
-    sc1 = static_cast<int>((byte(hw, 1) & 15) | ((byte(lw, 1) >> 6) << 4));
-    m0 = static_cast<int>((byte(hw, 0) >> 4) | ((byte(mw, 0) >> 6) << 4));
-    m1 = static_cast<int>((byte(hw, 1) >> 4) | ((byte(mw, 1) >> 6) << 4));
-  }
-  const uint4 wa = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * j);
-  const uint4 wb = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * j);
-  const uint32_t m4 = 0x0F0F0F0Fu;
-  int lo = 0, hi = 0;
+  const float2 dmn = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+  const float d = dmn.x, dmin = dmn.y;
+  // AB = s[2k], s[2k+1], s[4+2k], s[5+2k]; CC = s[8+2k], s[9+2k] twice (k = j & 1)
+  const uint32_t AB = __byte_perm(h.y, h.z, K.sel_ab);
+  const uint32_t CC = __byte_perm(h.w, 0u, K.sel_c);
+  const uint32_t lowW = AB & 0x3F3F3F3Fu;
+  const uint32_t highW = (CC & 0x00000F0Fu) | ((CC >> 4) & 0x0F0F0000u) | ((AB >> 2) & 0x30303030u);
+  const uint32_t W = K.hi ? highW : lowW;
+  const int sc0 = static_cast<int>(W & 0xFFu), sc1 = static_cast<int>((W >> 8) & 0xFFu);
+  const int m0 = static_cast<int>((W >> 16) & 0xFFu), m1 = static_cast<int>(W >> 24);
+  const uint4 wa = *reinterpret_cast<const uint4 *>(blk + K.qoff);
+  const uint4 wb = *reinterpret_cast<const uint4 *>(blk + K.qoff + 16);
+  const uint32_t m4 = 0x0F0F0F0Fu, h4 = 0xF0F0F0F0u;
+  // low nibbles as they are; high nibbles in place (16 x the nibble, an
+  // unsigned byte) -- their dot is exactly 16 x the nibble dot
+  int lo = 0, hi16 = 0;
   lo = __dp4a(static_cast<int>(wa.x & m4), A.xa.x, lo);
   lo = __dp4a(static_cast<int>(wa.y & m4), A.xa.y, lo);
   lo = __dp4a(static_cast<int>(wa.z & m4), A.xa.z, lo);
@@ -246,14 +264,15 @@ __device__ __forceinline__ float unit_q4k_reg(const uint8_t *blk, int j, const Q
   lo = __dp4a(static_cast<int>(wb.y & m4), A.xb.y, lo);
   lo = __dp4a(static_cast<int>(wb.z & m4), A.xb.z, lo);
   lo = __dp4a(static_cast<int>(wb.w & m4), A.xb.w, lo);
-  hi = __dp4a(static_cast<int>((wa.x >> 4) & m4), A.xc.x, hi);
-  hi = __dp4a(static_cast<int>((wa.y >> 4) & m4), A.xc.y, hi);
-  hi = __dp4a(static_cast<int>((wa.z >> 4) & m4), A.xc.z, hi);
-  hi = __dp4a(static_cast<int>((wa.w >> 4) & m4), A.xc.w, hi);
-  hi = __dp4a(static_cast<int>((wb.x >> 4) & m4), A.xd.x, hi);
-  hi = __dp4a(static_cast<int>((wb.y >> 4) & m4), A.xd.y, hi);
-  hi = __dp4a(static_cast<int>((wb.z >> 4) & m4), A.xd.z, hi);
-  hi = __dp4a(static_cast<int>((wb.w >> 4) & m4), A.xd.w, hi);
+  hi16 = dp4a_us(wa.x & h4, A.xc.x, hi16);
+  hi16 = dp4a_us(wa.y & h4, A.xc.y, hi16);
+  hi16 = dp4a_us(wa.z & h4, A.xc.z, hi16);
+  hi16 = dp4a_us(wa.w & h4, A.xc.w, hi16);
+  hi16 = dp4a_us(wb.x & h4, A.xd.x, hi16);
+  hi16 = dp4a_us(wb.y & h4, A.xd.y, hi16);
+  hi16 = dp4a_us(wb.z & h4, A.xd.z, hi16);
+  hi16 = dp4a_us(wb.w & h4, A.xd.w, hi16);
+  const int hi = hi16 >> 4;  // exact: a multiple of 16
   const float dd = __fmul_rn(d, A.d8), dm = __fmul_rn(dmin, A.d8);
   const float t0 = __fsub_rn(__fmul_rn(static_cast<float>(lo), __fmul_rn(dd, static_cast<float>(sc0))),
                              __fmul_rn(A.bs01, __fmul_rn(dm, static_cast<float>(m0))));
@@ -301,12 +320,14 @@ __device__ __forceinline__ int unit_q6k_reg(const uint8_t *blk, int n, int kp, c
   ld_window<8>(blk + 128 + 32 * n, h);
   const uint32_t sca = ld16(blk + 192 + 8 * n + 2 * kp);
   const uint32_t scb = ld16(blk + 192 + 8 * n + 2 * kp + 4);
-  const int ka = kp, kb = kp + 2;
+  // 6-bit quants of quarters ka = kp and kb = kp + 2: low nibble | 2 high
+  // bits (qh >> 2k) at bits 4-5, i.e. qh << (4 - 2ka) and qh >> (2kb - 4)
+  const uint32_t sha = 4u - 2u * static_cast<uint32_t>(kp), shb = 2u * static_cast<uint32_t>(kp);
   int sa0 = 0, sa1 = 0, sb0 = 0, sb1 = 0;
 #pragma unroll
   for (int t = 0; t < 8; ++t) {
-    const uint32_t va = (l[t] & 0x0F0F0F0Fu) | (((h[t] >> (2 * ka)) & 0x03030303u) << 4);
-    const uint32_t vb = ((l[t] >> 4) & 0x0F0F0F0Fu) | (((h[t] >> (2 * kb)) & 0x03030303u) << 4);
+    const uint32_t va = (l[t] & 0x0F0F0F0Fu) | ((h[t] << sha) & 0x30303030u);
+    const uint32_t vb = ((l[t] >> 4) & 0x0F0F0F0Fu) | ((h[t] >> shb) & 0x30303030u);
     if (t < 4) {
       sa0 = __dp4a(static_cast<int>(va), A.xa[t], sa0);
       sb0 = __dp4a(static_cast<int>(vb), A.xb[t], sb0);
@@ -376,9 +397,10 @@ __device__ __forceinline__ void row_group(const uint8_t *base, size_t rstep, int
       Q4Act A;
       load_q4act(q8, u, true, A);
       const int boff = (u >> 2) * 144;
+      const Q4Lane K = q4_lane();
 #pragma unroll
       for (int i = 0; i < NR; ++i) {
-        const float t = unit_q4k_reg(base + i * rstep + boff, u & 3, A);
+        const float t = unit_q4k_reg(base + i * rstep + boff, K, A);
         acc[i] += ok ? t : 0.f;
       }
     } else if constexpr (TYPE == T_Q6_K) {

@@ -321,3 +321,22 @@ def test_persistent_decode_equals_graph_decode(models, name, monkeypatch):
     g, p = out["graph"], out["persistent"]
     assert np.array_equal(g[0], p[0]) and g[1] == p[1] and np.array_equal(g[2], p[2])
     assert np.array_equal(g[3], p[3])
+
+
+def test_many_split_attention_paths_agree(model_cache, monkeypatch):
+    """A 4096-token context of the 7B shape (head_dim 128, 7 query heads per
+    kv head): 33 attention splits per kv head.  The per-phase kernel's combine
+    (the last split combines every head, in several staged blocks) and the
+    persistent kernel's distributed combine (each split combines a slice)
+    give identical ids and logits."""
+    path = synth.cached_model("qwen7b", layers=2, cache_dir=model_cache)
+    prompt = np.random.default_rng(9).integers(0, 151643, 4096).astype(np.int32)
+    out = {}
+    for mode in ("graph", "persistent"):
+        monkeypatch.setenv("C2S_DECODE", mode)
+        with K.Engine(path, max_tokens=4160) as e:
+            e.ingest_from(0, prompt)
+            toks = e.generate(6, stop_on_special=False)
+            out[mode] = (toks, e.compute_logits())
+    assert np.array_equal(out["graph"][0], out["persistent"][0])
+    assert np.array_equal(out["graph"][1], out["persistent"][1])
