@@ -133,6 +133,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// n arrivals on a barrier in one operation
+__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
+}
+
 // Grid-wide barrier of the compute warps: one monotonically increasing
 // arrival counter (zeroed at launch).  Thread 0 of each CTA arrives with a
 // release add, then polls with acquire loads until all G CTAs of barrier
@@ -602,12 +607,23 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   }
   csync();
   if (tr) tr[1] = globaltimer_ns();
-  // ---- chunks from the ring: each warp takes rows j = warp (mod kWarps) of
-  // the phase and releases each slot itself (empty barriers count kWarps)
+  // ---- chunks from the ring.  Few rows: every warp takes rows
+  // j = warp (mod kWarps) of each chunk.  Many rows in as many chunks as
+  // ring slots or more: the warps split into ng groups of ws; group g takes
+  // chunks g, g + ng, ... and its warps rows j = warp (mod ws) of them, so
+  // that each warp evaluates larger row groups against one activation load.
+  // Each chunk's slot is released by kWarps arrivals either way.
   long long wait_cyc = 0;
   const long long loop_t0 = tr ? clock64() : 0;
+  int my_rows = 0;
+#pragma unroll
+  for (int s = 0; s < kMaxSegs; ++s) my_rows += R.r1[s] - R.r0[s];
+  const int lng = (nchunks >= P.nslot && my_rows >= 16 * kWarps) ? (P.nslot >= 8 ? 3 : P.nslot >= 4 ? 2 : P.nslot >= 2 ? 1 : 0) : 0;
+  const int ng = 1 << lng, lws = 3 - lng, ws = kWarps >> lng;  // kWarps = 8
+  const int grp = warp >> lws, wig = warp & (ws - 1);
+  static_assert(kWarps == 8, "warp groups assume 8 compute warps");
   int jbase = 0;
-  for (int i = 0; i < nchunks; ++i) {
+  for (int i = grp; i < nchunks; i += ng) {
     const uint32_t k = k_ring + static_cast<uint32_t>(i);
     const int slot = static_cast<int>(k % static_cast<uint32_t>(P.nslot));
     const uint32_t parity = (k / static_cast<uint32_t>(P.nslot)) & 1u;
@@ -621,21 +637,21 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     const Seg &S = ph.seg[ch.seg];
     const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
     const uint8_t *rows = smem + static_cast<size_t>(slot) * P.slot_alloc + (src & 15);
-    const int first = ((warp - jbase) % kWarps + kWarps) % kWarps;
+    const int first = (wig - jbase) & (ws - 1);
     if (first < ch.nr) {
-      const int cnt = (ch.nr - first + kWarps - 1) / kWarps;
+      const int cnt = (ch.nr - first + ws - 1) >> lws;
       float *y = ybuf + ch.seg * P.yrows + ch.lr0;
       switch (S.type) {
-        case T_Q8_0: warp_rows<T_Q8_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
-        case T_Q5_0: warp_rows<T_Q5_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
-        case T_Q4_K: warp_rows<T_Q4_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
-        case T_Q6_K: warp_rows<T_Q6_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y); break;
+        case T_Q8_0: warp_rows<T_Q8_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+        case T_Q5_0: warp_rows<T_Q5_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+        case T_Q4_K: warp_rows<T_Q4_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+        case T_Q6_K: warp_rows<T_Q6_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
         default: break;
       }
     }
     jbase += ch.nr;
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (lane == 0) mbar_arrive_n(&empty[slot], static_cast<uint32_t>(ng));
   }
   k_ring += static_cast<uint32_t>(nchunks);
   csync();

@@ -423,26 +423,27 @@ __device__ __forceinline__ void row_group(const uint8_t *base, size_t rstep, int
   if ((lane & (32 / NR - 1)) == 0) y[r * ystep] = v;
 }
 
-// Rows first, first + 8, ... (cnt of them) of a staged chunk -> y[local row],
-// in groups of 8, 4, 2 and 1 rows.  U units per row.
+// Rows first, first + ws, ... (cnt of them) of a staged chunk -> y[local
+// row], in groups of 8, 4, 2 and 1 rows.  U units per row; ws warps share
+// the chunk.
 template <int TYPE>
 __device__ __forceinline__ void warp_rows(const uint8_t *rows, int row_bytes, int U, int first, int cnt,
-                                          const LimbsView &LV, const Q8KView &q8, float *y) {
-  const size_t rstep = static_cast<size_t>(kWarps) * row_bytes;
+                                          const LimbsView &LV, const Q8KView &q8, float *y, int ws = kWarps) {
+  const size_t rstep = static_cast<size_t>(ws) * row_bytes;
   const uint8_t *base = rows + static_cast<size_t>(first) * row_bytes;
   float *yp = y + first;
   int left = cnt;
-  for (; left >= 8; left -= 8, base += 8 * rstep, yp += 8 * kWarps)
-    row_group<TYPE, 8>(base, rstep, U, LV, q8, yp, kWarps);
+  for (; left >= 8; left -= 8, base += 8 * rstep, yp += 8 * ws)
+    row_group<TYPE, 8>(base, rstep, U, LV, q8, yp, ws);
   if (left >= 4) {
-    row_group<TYPE, 4>(base, rstep, U, LV, q8, yp, kWarps);
-    left -= 4, base += 4 * rstep, yp += 4 * kWarps;
+    row_group<TYPE, 4>(base, rstep, U, LV, q8, yp, ws);
+    left -= 4, base += 4 * rstep, yp += 4 * ws;
   }
   if (left >= 2) {
-    row_group<TYPE, 2>(base, rstep, U, LV, q8, yp, kWarps);
-    left -= 2, base += 2 * rstep, yp += 2 * kWarps;
+    row_group<TYPE, 2>(base, rstep, U, LV, q8, yp, ws);
+    left -= 2, base += 2 * rstep, yp += 2 * ws;
   }
-  if (left >= 1) row_group<TYPE, 1>(base, rstep, U, LV, q8, yp, kWarps);
+  if (left >= 1) row_group<TYPE, 1>(base, rstep, U, LV, q8, yp, ws);
 }
 
 }  // namespace c2s
