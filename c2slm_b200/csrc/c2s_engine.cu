@@ -633,8 +633,10 @@ cudaError_t enqueue_forward(c2s_engine *e, cudaStream_t s, bool check_halt, bool
     A.st = e->st;
     A.check_halt = check_halt;
     A.split_len = e->split_len;
+    A.items_cap = e->num_sms;  // the persistent kernel's grid
     if ((err = mark(tm, s, -1))) break;
-    err = launch(k_attention, dim3(pl.g1 - pl.g0, e->max_splits), dim3(kThreads), e->attn_smem, s, A);
+    err = launch(k_attention, dim3(std::max(pl.g1 - pl.g0, pl.h1 - pl.h0), e->max_splits), dim3(kThreads),
+                 e->attn_smem, s, A);
     if (err || (err = mark(tm, s, 7))) break;
     // o_proj + residual (tensor parallel: this rank's heads' columns, then an allreduce)
     P = MatParams{};

@@ -675,6 +675,7 @@ struct AttnParams {
   // rows start at tp_h0) and kv heads tp_g0 .. tp_g0 + n_kv - 1; qpk is the
   // model's query heads per kv head.  One GPU: 0, n_heads, 0.
   int qpk, tp_h0, tp_h1, tp_g0;
+  int items_cap;  // per-head items while they fit in this many CTAs (the persistent grid)
 };
 
 __device__ __forceinline__ void head_rmsnorm_warp(float *v, const float *w, int hd, float eps) {
@@ -720,18 +721,20 @@ __device__ __forceinline__ void lds_vec(const float *p, float (&v)[E]) {
   }
 }
 
-// Scores of positions a .. a+len-1 (rows of kb) for the qpk (<= 8) heads of
-// a group: warp w takes positions w, w + 8, ..., four at a time; lane l
-// holds d = l*E .. l*E+E-1 of q and k; the 8 head dots of a position are
-// reduced together by a transposing butterfly, after which lane 4h holds
-// head h.  The four positions' butterflies are independent and interleave.
-template <int E>
+// Scores of positions a .. a+len-1 (rows of kb) for the qpk (<= QP) heads of
+// an item.  The 8 rows of one transposing butterfly are (position p, head h)
+// pairs, r = p * QP + h, P = 8 / QP consecutive positions: warp w takes
+// positions w*P, w*P + 8P, ..., U butterflies at a time (independent, they
+// interleave); lane l holds d = l*E .. l*E+E-1 of q and k.  After the
+// butterfly lane 4r holds row r.
+template <int E, int QP>
 __device__ __forceinline__ void attn_scores(const float *qs, const float *kb, int len, int qpk, float scale,
                                             float *sc, int stride) {
+  constexpr int P = 8 / QP, U = P >= 4 ? 1 : 4 / P;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, hd = 32 * E;
-  float qr[8][E];
+  float qr[QP][E];
 #pragma unroll
-  for (int h = 0; h < 8; ++h) {
+  for (int h = 0; h < QP; ++h) {
     if (h < qpk) {
       lds_vec<E>(qs + h * hd + lane * E, qr[h]);
     } else {
@@ -739,34 +742,36 @@ __device__ __forceinline__ void attn_scores(const float *qs, const float *kb, in
       for (int j = 0; j < E; ++j) qr[h][j] = 0.f;
     }
   }
-  const int h = lane >> 2;
-  for (int t0 = warp; t0 < len; t0 += 4 * kWarps) {
-    float dot[4][8];
+  const int r = lane >> 2, hq = r % QP, pq = r / QP;
+  for (int t0 = warp * P; t0 < len; t0 += kWarps * P * U) {
+    float v[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + u * kWarps;
-      float kv[E];
-      if (t < len) {
-        lds_vec<E>(kb + t * hd + lane * E, kv);
-      } else {
+    for (int u = 0; u < U; ++u) {
+      float dot[8];
 #pragma unroll
-        for (int j = 0; j < E; ++j) kv[j] = 0.f;
+      for (int p = 0; p < P; ++p) {
+        const int t = t0 + u * kWarps * P + p;
+        float kv[E];
+        if (t < len) {
+          lds_vec<E>(kb + t * hd + lane * E, kv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < E; ++j) kv[j] = 0.f;
+        }
+#pragma unroll
+        for (int h = 0; h < QP; ++h) {
+          float d0 = 0.f;
+#pragma unroll
+          for (int j = 0; j < E; ++j) d0 = fmaf(qr[h][j], kv[j], d0);
+          dot[p * QP + h] = d0;
+        }
       }
-#pragma unroll
-      for (int hh = 0; hh < 8; ++hh) {
-        float d0 = 0.f;
-#pragma unroll
-        for (int j = 0; j < E; ++j) d0 = fmaf(qr[hh][j], kv[j], d0);
-        dot[u][hh] = d0;
-      }
+      v[u] = reduce_rows<8>(dot);
     }
-    float v[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = reduce_rows<8>(dot[u]);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + u * kWarps;
-      if ((lane & 3) == 0 && h < qpk && t < len) sc[h * stride + t] = __fmul_rn(v[u], scale);
+    for (int u = 0; u < U; ++u) {
+      const int t = t0 + u * kWarps * P + pq;
+      if ((lane & 3) == 0 && hq < qpk && t < len) sc[hq * stride + t] = __fmul_rn(v[u], scale);
     }
   }
 }
@@ -788,8 +793,51 @@ struct AttnJob {
                                    // combines them all and clears the counter
   int g, s, nsplit, p0, p1, pos, h0;
   int hd, qpk, max_splits;
+  int store_kv;                    // this item writes the cache row of pos (one item per kv head)
   float eps, scale;
 };
+
+// Work items of the attention of position pos on one rank (nh local query
+// heads in n_kv local kv groups): one item per (query head, split) while
+// they fit in `cap` CTAs, else one per (kv group, split).  The per-phase and
+// persistent kernels choose alike, so both evaluate the same operations.
+struct AttnLayout {
+  int nsplit, per_head, n_items;
+};
+
+__device__ __forceinline__ AttnLayout attn_layout(int pos, int split_len, int n_kv, int nh, int cap) {
+  AttnLayout L;
+  L.nsplit = (pos + split_len) / split_len;  // positions 0..pos
+  L.per_head = (nh <= 64 && nh * L.nsplit <= cap) ? 1 : 0;  // (one counter per head)
+  L.n_items = (L.per_head ? nh : n_kv) * L.nsplit;
+  return L;
+}
+
+// Fill the head range, kv group, store flag and counter of unit x (a local
+// query head, or a local kv group) of the layout; false if it has no heads.
+// The model has qpk query heads per kv head; this rank holds query heads
+// [tp_h0, tp_h1) and kv groups from tp_g0.
+__device__ __forceinline__ bool attn_unit(const AttnLayout &L, int x, int qpk, int tp_h0, int tp_h1, int tp_g0,
+                                          unsigned *counters, AttnJob &J) {
+  int hs, he, gg;
+  if (L.per_head) {
+    hs = tp_h0 + x;
+    he = hs + 1;
+    gg = hs / qpk;
+    J.store_kv = (hs == max(tp_h0, gg * qpk)) ? 1 : 0;  // the group's first head on this rank
+  } else {
+    gg = tp_g0 + x;
+    hs = max(tp_h0, gg * qpk);
+    he = min(tp_h1, (gg + 1) * qpk);
+    J.store_kv = 1;
+  }
+  if (he <= hs) return false;
+  J.g = gg - tp_g0;
+  J.qpk = he - hs;
+  J.h0 = hs - tp_h0;
+  J.counter = counters + x;
+  return true;
+}
 
 // Shared memory: asmem holds [kAttnBufs][SUB][hd] staged K or V rows,
 // [qpk][hd] q, [hd] k, [hd] v, [qpk][WIN] scores / weights.  bars[] are the
@@ -804,11 +852,16 @@ struct AttnJob {
 // engine uses (<= WIN) there is one window.  K and V sub-chunks of all
 // windows form one load sequence through the buffers, kAttnBufs in flight.
 // Returns false if a bounded wait expired.
-template <int E>
+template <int E, int QP>
 __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[kAttnBufs], unsigned *err) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int hd = 32 * E;
   constexpr int NB = kAttnBufs;
+  // softmax and weighted V: WPH warps per head; warp w takes head w / WPH
+  // and every WPH-th position of it from w % WPH
+  constexpr int WPH = kWarps / QP;
+  const int hw = warp / WPH, part = warp % WPH;
+  __shared__ float s_red[2][kWarps];
   const int qpk = J.qpk, SUB = attn_sub(hd), WIN = NB * SUB, pos = J.pos, p0 = J.p0, p1 = J.p1;
   float *buf = asmem, *qs = buf + NB * SUB * hd;
   float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd;
@@ -875,12 +928,15 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
     }
     csync();
   }
-  if (pos >= p0 && pos < p1)  // KVCache.StoreKV (engine/kvcache.go:143-158)
+  if (J.store_kv && pos >= p0 && pos < p1) {  // KVCache.StoreKV (engine/kvcache.go:143-158)
     for (int i = tid; i < hd; i += kThreads) {
       J.kc[static_cast<size_t>(pos) * hd + i] = knew[i];
       J.vc[static_cast<size_t>(pos) * hd + i] = vnew[i];
     }
-  // running softmax state of head h = warp (every lane holds m and l)
+    // later steps stage this row with bulk copies, possibly from another CTA
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  // running softmax state of head hw (every lane of its warps holds m and l)
   float m = -INFINITY, l = 0.f, acc[E];  // acc: d = lane*E .. lane*E+E-1
 #pragma unroll
   for (int j = 0; j < E; ++j) acc[j] = 0.f;
@@ -915,24 +971,40 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
     for (int r = 0; r < nsw; ++r, ++q) {  // pass 1: scores of the window
       const Ld L = load_of(q);
       const float *kb = arrive(q, L);
-      attn_scores<E>(qs, kb, L.b - L.a, qpk, J.scale, sc + (L.a - wa), WIN);
+      attn_scores<E, QP>(qs, kb, L.b - L.a, qpk, J.scale, sc + (L.a - wa), WIN);
       release(q);
     }
-    if (warp < qpk) {  // softmax of the window for head h = warp
-      const float *sh = sc + warp * WIN;
+    {  // softmax of the window for head hw (fixed-order combination of its warps' shares)
+      const float *sh = sc + hw * WIN;
       float mw = -INFINITY;
-#pragma unroll 4
-      for (int t = lane; t < len; t += 32) mw = fmaxf(mw, sh[t]);
+      if (hw < qpk)
+        for (int t = part * 32 + lane; t < len; t += 32 * WPH) mw = fmaxf(mw, sh[t]);
       mw = warp_max(mw);
+      if (WPH > 1) {
+        if (lane == 0) s_red[0][warp] = mw;
+        csync();
+        mw = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < WPH; ++k) mw = fmaxf(mw, s_red[0][hw * WPH + k]);
+      }
       const float m_new = fmaxf(m, mw);
       float lw = 0.f;
+      if (hw < qpk) {
 #pragma unroll 1
-      for (int t = lane; t < len; t += 32) {
-        const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sh[t], m_new))));
-        sc[warp * WIN + t] = e;
-        lw += e;
+        for (int t = part * 32 + lane; t < len; t += 32 * WPH) {
+          const float e = static_cast<float>(exp(static_cast<double>(__fsub_rn(sh[t], m_new))));
+          sc[hw * WIN + t] = e;
+          lw += e;
+        }
       }
       lw = warp_sum(lw);
+      if (WPH > 1) {
+        if (lane == 0) s_red[1][warp] = lw;
+        csync();  // also: every warp's weights are in sc
+        lw = 0.f;
+#pragma unroll
+        for (int k = 0; k < WPH; ++k) lw += s_red[1][hw * WPH + k];
+      }
       const float alpha = static_cast<float>(exp(static_cast<double>(m - m_new)));
       l = l * alpha + lw;
       m = m_new;
@@ -943,9 +1015,10 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
     for (int r = 0; r < nsw; ++r, ++q) {  // pass 2: weighted sum of V
       const Ld L = load_of(q);
       const float *vb = arrive(q, L);
-      if (warp < qpk) {
-        const float *e = sc + warp * WIN + (L.a - wa);
-        const int n = L.b - L.a;
+      if (hw < qpk) {  // positions t = part, part + WPH, ... of the sub-chunk
+        const float *e = sc + hw * WIN + (L.a - wa) + part;
+        const float *vbp = vb + part * hd;
+        const int n = (L.b - L.a - part + WPH - 1) / WPH;
         // four interleaved partial sums (positions t mod 4), then combined
         float a[4][E];
 #pragma unroll
@@ -956,17 +1029,17 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
         for (; t + 3 < n; t += 4) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const float eu = e[t + u];
+            const float eu = e[(t + u) * WPH];
             float vu[E];
-            lds_vec<E>(vb + (t + u) * hd + lane * E, vu);
+            lds_vec<E>(vbp + (t + u) * WPH * hd + lane * E, vu);
 #pragma unroll
             for (int j = 0; j < E; ++j) a[u][j] = fmaf(eu, vu[j], a[u][j]);
           }
         }
         for (; t < n; ++t) {
-          const float et = e[t];
+          const float et = e[t * WPH];
           float vt[E];
-          lds_vec<E>(vb + t * hd + lane * E, vt);
+          lds_vec<E>(vbp + t * WPH * hd + lane * E, vt);
 #pragma unroll
           for (int j = 0; j < E; ++j) a[0][j] = fmaf(et, vt[j], a[0][j]);
         }
@@ -976,16 +1049,32 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
       release(q);
     }
   }
-  const int h0 = J.h0;
-  if (J.nsplit == 1) {  // single split: normalise and write the heads directly
-    if (warp < qpk)
+  if (WPH > 1) {  // the shares of head hw's warps, summed in warp order (the buffers are free)
+    float *red = buf;
 #pragma unroll
-      for (int j = 0; j < E; ++j) J.out[(h0 + warp) * hd + lane * E + j] = acc[j] / l;
+    for (int j = 0; j < E; ++j) red[warp * hd + lane * E + j] = acc[j];
+    csync();
+    if (part == 0)
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        float a = 0.f;
+#pragma unroll
+        for (int k = 0; k < WPH; ++k) a += red[(hw * WPH + k) * hd + lane * E + j];
+        acc[j] = a;
+      }
+    csync();
+  }
+  const int h0 = J.h0;
+  const bool lead = hw < qpk && part == 0;  // the warp that writes head hw
+  if (J.nsplit == 1) {  // single split: normalise and write the heads directly
+    if (lead)
+#pragma unroll
+      for (int j = 0; j < E; ++j) J.out[(h0 + hw) * hd + lane * E + j] = acc[j] / l;
     return ok;
   }
   // partial (m, l, acc) of this split; the last split of the group combines
-  if (warp < qpk) {
-    float *pp = J.part + (static_cast<size_t>(h0 + warp) * J.max_splits + J.s) * (hd + 2);
+  if (lead) {
+    float *pp = J.part + (static_cast<size_t>(h0 + hw) * J.max_splits + J.s) * (hd + 2);
     if (lane == 0) {
       pp[0] = m;
       pp[1] = l;
@@ -1098,7 +1187,9 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
 
 __device__ __forceinline__ bool attend(const AttnJob &J, float *asmem, uint64_t *bars, uint32_t (&uses)[kAttnBufs],
                                        unsigned *err) {
-  return J.hd == 64 ? attend_t<2>(J, asmem, bars, uses, err) : attend_t<4>(J, asmem, bars, uses, err);
+  if (J.qpk == 1)
+    return J.hd == 64 ? attend_t<2, 1>(J, asmem, bars, uses, err) : attend_t<4, 1>(J, asmem, bars, uses, err);
+  return J.hd == 64 ? attend_t<2, 8>(J, asmem, bars, uses, err) : attend_t<4, 8>(J, asmem, bars, uses, err);
 }
 
 __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
@@ -1114,28 +1205,23 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   pdl_wait();
   DevState *st = A.st;
   if (A.check_halt && *reinterpret_cast<volatile int *>(&st->halted)) return;
-  const int g = blockIdx.x, s = blockIdx.y;  // g: local kv head
+  const int x = blockIdx.x, s = blockIdx.y;  // x: local query head or kv group, s: split
   const int pos = st->fwd_pos;
   if (pos < 0 || pos >= A.max_tokens) {
-    if (tid == 0 && s == 0 && g == 0) atomicOr(&st->err, kErrPos);
+    if (tid == 0 && s == 0 && x == 0) atomicOr(&st->err, kErrPos);
     return;
   }
-  const int n = pos + 1, hd = A.hd;
-  const int nsplit = (n + A.split_len - 1) / A.split_len;
-  if (s >= nsplit) return;
-  // query heads of kv head tp_g0 + g that this rank holds
-  const int gg = A.tp_g0 + g;
-  const int hs = max(A.tp_h0, gg * A.qpk), he = min(A.tp_h1, (gg + 1) * A.qpk);
-  if (he <= hs) return;
+  const int hd = A.hd;
+  const AttnLayout AL = attn_layout(pos, A.split_len, A.n_kv, A.tp_h1 - A.tp_h0, A.items_cap);
+  if (s >= AL.nsplit || x >= (AL.per_head ? A.tp_h1 - A.tp_h0 : A.n_kv)) return;
+  AttnJob J;
+  if (!attn_unit(AL, x, A.qpk, A.tp_h0, A.tp_h1, A.tp_g0, st->attn_counter, J)) return;
   // KV layout [L][KVH][max_tokens][hd] per plane (engine/kvcache.go:127-140)
   const size_t head_stride = static_cast<size_t>(A.max_tokens) * hd;
-  const size_t off = static_cast<size_t>(A.layer) * A.n_kv * head_stride + g * head_stride;
-  AttnJob J;
-  J.qpk = he - hs;
-  J.h0 = hs - A.tp_h0;
+  const size_t off = static_cast<size_t>(A.layer) * A.n_kv * head_stride + J.g * head_stride;
   J.q = A.q + static_cast<size_t>(J.h0) * hd;
-  J.k = A.k + g * hd;
-  J.v = A.v + g * hd;
+  J.k = A.k + J.g * hd;
+  J.v = A.v + J.g * hd;
   J.q_norm = A.q_norm;
   J.k_norm = A.k_norm;
   J.kc = A.kcache + off;
@@ -1145,13 +1231,11 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnParams A) {
   J.rope_sn = pos < A.rope_len ? A.rope_sin + static_cast<size_t>(pos) * (hd / 2) : nullptr;
   J.out = A.out;
   J.part = A.part;
-  J.counter = &st->attn_counter[g];
   J.dist = 0;  // the CTAs of a launch are not guaranteed to be co-resident
-  J.g = g;
   J.s = s;
-  J.nsplit = nsplit;
+  J.nsplit = AL.nsplit;
   J.p0 = s * A.split_len;
-  J.p1 = min(n, J.p0 + A.split_len);
+  J.p1 = min(pos + 1, J.p0 + A.split_len);
   J.pos = pos;
   J.hd = hd;
   J.max_splits = A.max_splits;

@@ -347,22 +347,19 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
     if (threadIdx.x == 0 && item == 0) atomicOr(&st->err, kErrPos);
     return true;
   }
-  const int n = pos + 1, hd = P.hd;
-  const int nsplit = (n + P.split_len - 1) / P.split_len;
-  if (item >= P.n_kv * nsplit) return true;
-  const int g = item % P.n_kv, s = item / P.n_kv;  // split-major: (g, s) stays on one CTA as n grows
-  // this rank's query heads of kv head tp_g0 + g (one GPU: all qpk of them)
-  const int gg = P.tp_g0 + g;
-  const int hs = max(P.tp_h0, gg * P.qpk), he = min(P.tp_h1, (gg + 1) * P.qpk);
-  if (he <= hs) return true;
-  const size_t head_stride = static_cast<size_t>(P.max_tokens) * hd;
-  const size_t off = (static_cast<size_t>(ph.layer) * P.n_kv + g) * head_stride;
+  const int hd = P.hd;
+  const AttnLayout AL = attn_layout(pos, P.split_len, P.n_kv, P.tp_h1 - P.tp_h0, static_cast<int>(gridDim.x));
+  if (item >= AL.n_items) return true;
+  // item = (unit x, split s), split-major
+  const int nx = AL.per_head ? P.tp_h1 - P.tp_h0 : P.n_kv;
+  const int x = item % nx, s = item / nx;
   AttnJob J;
-  J.qpk = he - hs;
-  J.h0 = hs - P.tp_h0;
+  if (!attn_unit(AL, x, P.qpk, P.tp_h0, P.tp_h1, P.tp_g0, st->attn_counter, J)) return true;
+  const size_t head_stride = static_cast<size_t>(P.max_tokens) * hd;
+  const size_t off = (static_cast<size_t>(ph.layer) * P.n_kv + J.g) * head_stride;
   J.q = P.q + static_cast<size_t>(J.h0) * hd;
-  J.k = P.k + g * hd;
-  J.v = P.v + g * hd;
+  J.k = P.k + J.g * hd;
+  J.v = P.v + J.g * hd;
   J.q_norm = ph.q_norm;
   J.k_norm = ph.k_norm;
   J.kc = P.kcache + off;
@@ -371,13 +368,11 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   J.rope_sn = pos < P.rope_len ? rope_row + hd / 2 : nullptr;
   J.out = P.attn_out;
   J.part = P.part;
-  J.counter = &st->attn_counter[g];
   J.dist = 1;  // cooperative launch: all CTAs are resident
-  J.g = g;
   J.s = s;
-  J.nsplit = nsplit;
+  J.nsplit = AL.nsplit;
   J.p0 = s * P.split_len;
-  J.p1 = min(n, J.p0 + P.split_len);
+  J.p1 = min(pos + 1, J.p0 + P.split_len);
   J.pos = pos;
   J.hd = hd;
   J.max_splits = P.max_splits;
@@ -476,7 +471,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   const int nchunks = phase_rows(ph, c, G, R);
   // the attention's split arrivals of this layer: every split has finished
   // waiting on them before the grid barrier this phase follows
-  if (ph.kind == K_OPROJ && tid == 0 && c < P.n_kv) st->attn_counter[c] = 0;
+  if (ph.kind == K_OPROJ && tid == 0 && c < 64) st->attn_counter[c] = 0;
   const bool residual = ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN;
   const bool normed = ph.kind == K_QKV || ph.kind == K_FFN_UP || ph.kind == K_LOGITS;
   // ---- loads the epilogue needs, requested first
@@ -876,7 +871,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
     fence_mbar_init();
     // split arrivals start from zero (a launch that stopped on an error may
     // have left counts); the first attention phase follows a grid barrier
-    if (c < P.n_kv) st->attn_counter[c] = 0;
+    if (c < 64) st->attn_counter[c] = 0;
     s_stop = 0;
   }
   __syncthreads();
