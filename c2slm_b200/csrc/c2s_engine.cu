@@ -25,6 +25,7 @@
 
 #include "../../include/c2slm_b200.h"
 #include "c2s_persistent.cuh"
+#include "c2s_prefill.cuh"
 
 using namespace c2s;
 
@@ -448,6 +449,13 @@ struct c2s_engine {
   HostFwdIn *h_in = nullptr;  // ring of forward inputs
   int h_in_next = 0;
   float *h_buf = nullptr;     // staging for normx/logits
+  // multi-token prefill on the tensor cores (c2s_prefill.cuh): buffers for a
+  // chunk of up to pf_cap tokens, allocated on first use
+  int pf_ok = 0, pf_cap = 0, pf_kmax = 0;
+  float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_g = nullptr,
+        *pf_u = nullptr, *pf_d8 = nullptr;
+  int8_t *pf_q8 = nullptr;
+  int *pf_tok = nullptr;
   DevState *h_st = nullptr;
   int *h_tokens = nullptr;
   int host_seq = 0;
@@ -1216,6 +1224,18 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   // ---- kernels: shared-memory limits, graphs
   CK(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(k_pf_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(k_pf_gemm<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
+  CK(cudaFuncSetAttribute(k_pf_gemm<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
+  {  // prefill on the tensor cores: one GPU, every layer projection a K-quant, superblock-aligned widths
+    bool okp = e->plan.world == 1 && d.embd % 256 == 0 && d.ffn % 256 == 0 && (hd == 64 || hd == 128);
+    for (int l = 0; l < d.n_layers && okp; ++l) {
+      const LayerDev &Ld = e->layers[l];
+      for (int t : {Ld.tq, Ld.tk, Ld.tv, Ld.to, Ld.tgate, Ld.tup, Ld.tdown}) okp = okp && is_kquant(t);
+    }
+    const char *pe = getenv("C2S_PREFILL");
+    e->pf_ok = okp && !(pe && strcmp(pe, "0") == 0) ? 1 : 0;
+  }
   if ((rc = capture(e, &e->g_forward, 0)) || (rc = capture(e, &e->g_step, 1)) ||
       (rc = capture(e, &e->g_logits, 2)) || (rc = capture(e, &e->g_fwd_select, 3))) {
     if (!g_use_pdl) return rc;
@@ -1390,6 +1410,11 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->scratch_x), static_cast<void *>(e->st),
                   static_cast<void *>(e->gbar), static_cast<void *>(e->delta),
                   static_cast<void *>(e->logits_full)})
+    if (p) cudaFree(p);
+  for (void *p : {static_cast<void *>(e->pf_x), static_cast<void *>(e->pf_q), static_cast<void *>(e->pf_k),
+                  static_cast<void *>(e->pf_v), static_cast<void *>(e->pf_att), static_cast<void *>(e->pf_g),
+                  static_cast<void *>(e->pf_u), static_cast<void *>(e->pf_d8), static_cast<void *>(e->pf_q8),
+                  static_cast<void *>(e->pf_tok)})
     if (p) cudaFree(p);
   for (int k = 0; k < 8; ++k)
     if (e->peer_shared[k] && e->peer_shared[k] != e->tp_shared) cudaIpcCloseMemHandle(e->peer_shared[k]);
@@ -1776,6 +1801,129 @@ int c2s_kv_get(const c2s_engine *e, int is_value, int layer, int kv_head, int po
   return C2S_OK;
 }
 
+// ---------------------------------------------------------------------------
+// prefill: chunks of up to pf_cap tokens through every layer together
+// ---------------------------------------------------------------------------
+static int pf_alloc(c2s_engine *e) {
+  if (e->pf_cap) return C2S_OK;
+  const c2s_model_desc &d = e->d;
+  const int cap = 1024, H = d.embd, F = d.ffn, nq = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
+  const int kmax = std::max(H, F);
+  auto al = [&](void **p, size_t bytes) -> int {
+    if (cudaMalloc(p, bytes) != cudaSuccess) return fail(C2S_ERR_OOM, "prefill buffers: cudaMalloc(%zu) failed", bytes);
+    return C2S_OK;
+  };
+  const size_t c = cap;
+  int rc;
+  if ((rc = al(reinterpret_cast<void **>(&e->pf_x), c * H * 4)) || (rc = al(reinterpret_cast<void **>(&e->pf_q), c * nq * 4)) ||
+      (rc = al(reinterpret_cast<void **>(&e->pf_k), c * kvd * 4)) || (rc = al(reinterpret_cast<void **>(&e->pf_v), c * kvd * 4)) ||
+      (rc = al(reinterpret_cast<void **>(&e->pf_att), c * nq * 4)) || (rc = al(reinterpret_cast<void **>(&e->pf_g), c * F * 4)) ||
+      (rc = al(reinterpret_cast<void **>(&e->pf_u), c * F * 4)) ||
+      (rc = al(reinterpret_cast<void **>(&e->pf_d8), c * (kmax / 256) * 4)) ||
+      (rc = al(reinterpret_cast<void **>(&e->pf_q8), c * kmax)) || (rc = al(reinterpret_cast<void **>(&e->pf_tok), c * 4)))
+    return rc;
+  e->pf_cap = cap;
+  e->pf_kmax = kmax;
+  return C2S_OK;
+}
+
+// K-quant GEMM of the chunk's n tokens (their Q8_K rows in pf_q8 / pf_d8)
+static int pf_gemm(c2s_engine *e, const uint8_t *w, int type, int rows, int cols, int n, float *out, int ldo, int mode,
+                   const float *bias) {
+  PfGemm G{};
+  G.w = w;
+  G.type = type;
+  G.rows = rows;
+  G.cols = cols;
+  G.row_bytes = static_cast<int>(row_bytes_of(type, cols));
+  G.aq = e->pf_q8;
+  G.ad = e->pf_d8;
+  G.lda = e->pf_kmax;
+  G.ldd = e->pf_kmax / 256;
+  G.M = n;
+  G.out = out;
+  G.ldo = ldo;
+  G.mode = mode;
+  G.bias = bias;
+  G.err = &e->st->err;
+  const dim3 grid((rows + kPfN - 1) / kPfN, (n + kPfM - 1) / kPfM);
+  if (type == T_Q4_K)
+    k_pf_gemm<T_Q4_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(G);
+  else
+    k_pf_gemm<T_Q6_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(G);
+  CK(cudaGetLastError());
+  return C2S_OK;
+}
+
+// n tokens at positions p0.. (p0 + n <= max_tokens): the forward of each, as
+// engine.Forward per token would leave the KV cache, TokenIDs, SeqLen and
+// the last NormX
+static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
+  const c2s_model_desc &d = e->d;
+  const int H = d.embd, F = d.ffn, hd = d.head_dim, nqh = d.n_heads, nkv = d.n_kv_heads;
+  const int nq = nqh * hd, kvd = nkv * hd, L = d.n_layers, qpk = nqh / nkv;
+  const int kmax = e->pf_kmax, ldd = kmax / 256;
+  const size_t head_stride = static_cast<size_t>(d.max_tokens) * hd;
+  const size_t plane = static_cast<size_t>(L) * nkv * head_stride;
+  cudaStream_t s = e->stream;
+  CK(cudaMemcpyAsync(e->pf_tok, tokens, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, s));
+  k_pf_embed<<<n, kThreads, 0, s>>>(e->pf_tok, n, d.vocab, e->tok_type, e->tok_embd,
+                                     static_cast<int>(row_bytes_of(e->tok_type, H)), e->pf_x, H);
+  CK(cudaGetLastError());
+  for (int l = 0; l < L; ++l) {
+    const LayerDev &Ld = e->layers[l];
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.attn_norm, d.eps, H, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
+    int rc;
+    if ((rc = pf_gemm(e, Ld.q, Ld.tq, nq, H, n, e->pf_q, nq, PF_STORE, Ld.qb)) ||
+        (rc = pf_gemm(e, Ld.k, Ld.tk, kvd, H, n, e->pf_k, kvd, PF_STORE, Ld.kb)) ||
+        (rc = pf_gemm(e, Ld.v, Ld.tv, kvd, H, n, e->pf_v, kvd, PF_STORE, Ld.vb)))
+      return rc;
+    float *kc = e->kv + static_cast<size_t>(l) * nkv * head_stride, *vc = kc + plane;
+    k_pf_rope_store<<<n, kThreads, static_cast<size_t>(nqh + nkv) * hd * 4, s>>>(
+        e->pf_q, e->pf_k, e->pf_v, nq, kvd, n, p0, nqh, nkv, hd, e->rope_cos, e->rope_sin, kMaxContext, Ld.qn, Ld.kn,
+        d.eps, kc, vc, head_stride);
+    PfAttn A{};
+    A.q = e->pf_q;
+    A.out = e->pf_att;
+    A.kc = kc;
+    A.vc = vc;
+    A.head_stride = head_stride;
+    A.ldq = nq;
+    A.n = n;
+    A.p0 = p0;
+    A.n_kv = nkv;
+    A.qpk = qpk;
+    A.n_heads = nqh;
+    A.hd = hd;
+    A.max_splits = e->max_splits;
+    A.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
+    A.eps = d.eps;
+    A.err = &e->st->err;
+    k_pf_attention<<<dim3(nkv, n), kThreads, e->attn_smem, s>>>(A);
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
+    if ((rc = pf_gemm(e, Ld.o, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.ffn_norm, d.eps, H, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
+    if ((rc = pf_gemm(e, Ld.gate, Ld.tgate, F, H, n, e->pf_g, F, PF_STORE, nullptr)) ||
+        (rc = pf_gemm(e, Ld.up, Ld.tup, F, H, n, e->pf_u, F, PF_STORE, nullptr)))
+      return rc;
+    const size_t cnt = static_cast<size_t>(n) * F;
+    k_pf_swiglu<<<static_cast<int>(std::min<size_t>((cnt + kThreads - 1) / kThreads, 4096)), kThreads, 0, s>>>(
+        e->pf_g, e->pf_u, cnt);
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
+    if ((rc = pf_gemm(e, Ld.down, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
+    CK(cudaGetLastError());
+  }
+  // the last token's residual stream (read by a following ComputeLogits /
+  // generate step) and its NormX (engine/forward.go:133-137)
+  CK(cudaMemcpyAsync(e->X, e->pf_x + static_cast<size_t>(n - 1) * H, static_cast<size_t>(H) * 4,
+                     cudaMemcpyDeviceToDevice, s));
+  k_pf_norm_q8k<<<1, kThreads, 0, s>>>(e->pf_x + static_cast<size_t>(n - 1) * H, H, e->out_norm, d.eps, H, 1,
+                                       e->pf_q8, kmax, e->pf_d8, ldd, e->normx);
+  k_pf_commit<<<1, kThreads, 0, s>>>(e->st, e->token_ids, e->pf_tok, n, p0, d.max_tokens);
+  CK(cudaGetLastError());
+  return C2S_OK;
+}
+
 int c2s_ingest_from(c2s_engine *e, int pos, const int32_t *tokens, int n, float *last_normx_out) {
   if (!e) return fail(C2S_ERR_ARG, "null engine");
   if (n <= 0) return 0;
@@ -1787,12 +1935,22 @@ int c2s_ingest_from(c2s_engine *e, int pos, const int32_t *tokens, int n, float 
   if (pos < e->host_seq)
     if (int rc = c2s_kv_set_seq_len(e, pos)) return rc;
   int done = 0;
-  for (int i = 0; i < n; ++i) {
-    const int p = pos + i;
-    if (p >= e->d.max_tokens) break;
-    if (int rc = set_fwd_input(e, tokens[i], p, 1)) return rc;
-    CK(cudaGraphLaunch(e->g_forward, e->stream));
-    ++done;
+  if (e->pf_ok && n > 1) {  // the tensor-core prefill, chunk by chunk
+    if (int rc = pf_alloc(e)) return rc;
+    const int total = std::min(n, e->d.max_tokens - pos);
+    for (int c0 = 0; c0 < total; c0 += e->pf_cap) {
+      const int m = std::min(e->pf_cap, total - c0);
+      if (int rc = pf_run(e, pos + c0, tokens + c0, m)) return rc;
+      done += m;
+    }
+  } else {
+    for (int i = 0; i < n; ++i) {
+      const int p = pos + i;
+      if (p >= e->d.max_tokens) break;
+      if (int rc = set_fwd_input(e, tokens[i], p, 1)) return rc;
+      CK(cudaGraphLaunch(e->g_forward, e->stream));
+      ++done;
+    }
   }
   if (done > 0 && last_normx_out)
     CK(cudaMemcpyAsync(e->h_buf, e->normx, e->d.embd * 4, cudaMemcpyDeviceToHost, e->stream));
