@@ -21,6 +21,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <array>
 #include <vector>
 
 #include "../../include/c2slm_b200.h"
@@ -454,8 +455,12 @@ struct c2s_engine {
   int pf_ok = 0, pf_cap = 0, pf_kmax = 0;
   float *pf_x = nullptr, *pf_q = nullptr, *pf_k = nullptr, *pf_v = nullptr, *pf_att = nullptr, *pf_g = nullptr,
         *pf_u = nullptr, *pf_d8 = nullptr;
-  int8_t *pf_q8 = nullptr;
+  uint8_t *pf_q8 = nullptr;   // tokens' Q8_K bytes in the GEMM's A-tile layout
   int *pf_tok = nullptr;
+  int16_t *pf_bs = nullptr;   // tokens' Q8_K sub-block sums
+  uint8_t *pf_planes = nullptr;  // every layer projection's digit planes and row tables
+  std::vector<std::array<const uint8_t *, 7>> pf_pl;  // per layer: q, k, v, o, gate, up, down
+  std::vector<std::array<const uint4 *, 7>> pf_ri;
   DevState *h_st = nullptr;
   int *h_tokens = nullptr;
   int host_seq = 0;
@@ -1414,7 +1419,7 @@ void engine_free(c2s_engine *e) {
   for (void *p : {static_cast<void *>(e->pf_x), static_cast<void *>(e->pf_q), static_cast<void *>(e->pf_k),
                   static_cast<void *>(e->pf_v), static_cast<void *>(e->pf_att), static_cast<void *>(e->pf_g),
                   static_cast<void *>(e->pf_u), static_cast<void *>(e->pf_d8), static_cast<void *>(e->pf_q8),
-                  static_cast<void *>(e->pf_tok)})
+                  static_cast<void *>(e->pf_tok), static_cast<void *>(e->pf_planes), static_cast<void *>(e->pf_bs)})
     if (p) cudaFree(p);
   for (int k = 0; k < 8; ++k)
     if (e->peer_shared[k] && e->peer_shared[k] != e->tp_shared) cudaIpcCloseMemHandle(e->peer_shared[k]);
@@ -1820,33 +1825,71 @@ static int pf_alloc(c2s_engine *e) {
       (rc = al(reinterpret_cast<void **>(&e->pf_att), c * nq * 4)) || (rc = al(reinterpret_cast<void **>(&e->pf_g), c * F * 4)) ||
       (rc = al(reinterpret_cast<void **>(&e->pf_u), c * F * 4)) ||
       (rc = al(reinterpret_cast<void **>(&e->pf_d8), c * (kmax / 256) * 4)) ||
-      (rc = al(reinterpret_cast<void **>(&e->pf_q8), c * kmax)) || (rc = al(reinterpret_cast<void **>(&e->pf_tok), c * 4)))
+      (rc = al(reinterpret_cast<void **>(&e->pf_q8), c * kmax)) || (rc = al(reinterpret_cast<void **>(&e->pf_tok), c * 4)) ||
+      (rc = al(reinterpret_cast<void **>(&e->pf_bs), c * (kmax / 256) * 16)))
     return rc;
+  // the digit planes of every layer projection, converted once
+  auto plane_bytes = [](int, int rows, int cols) {
+    return static_cast<size_t>((rows + kPfM - 1) / kPfM) * (cols / 256) * 2 * kPfPlane;
+  };
+  auto info_bytes = [](int rows, int cols) {
+    return static_cast<size_t>((rows + kPfM - 1) / kPfM) * kPfM * (cols / 256) * sizeof(uint4);
+  };
+  struct M { const uint8_t *w; int type, rows, cols; };
+  std::vector<std::array<M, 7>> mats;
+  size_t total = 0;
+  for (int l = 0; l < d.n_layers; ++l) {
+    const LayerDev &Ld = e->layers[l];
+    std::array<M, 7> m = {M{Ld.q, Ld.tq, nq, H}, M{Ld.k, Ld.tk, kvd, H}, M{Ld.v, Ld.tv, kvd, H}, M{Ld.o, Ld.to, H, nq},
+                          M{Ld.gate, Ld.tgate, F, H}, M{Ld.up, Ld.tup, F, H}, M{Ld.down, Ld.tdown, H, F}};
+    for (auto &x : m) total += plane_bytes(x.type, x.rows, x.cols) + info_bytes(x.rows, x.cols);
+    mats.push_back(m);
+  }
+  if ((rc = al(reinterpret_cast<void **>(&e->pf_planes), total))) return rc;
+  e->pf_pl.assign(d.n_layers, {});
+  e->pf_ri.assign(d.n_layers, {});
+  CK(cudaMemsetAsync(e->pf_planes, 0, total, e->stream));
+  size_t off = 0;
+  for (int l = 0; l < d.n_layers; ++l)
+    for (int i = 0; i < 7; ++i) {
+      const M &x = mats[l][i];
+      uint8_t *dst = e->pf_planes + off;
+      uint4 *info = reinterpret_cast<uint4 *>(dst + plane_bytes(x.type, x.rows, x.cols));
+      e->pf_pl[l][i] = dst;
+      e->pf_ri[l][i] = info;
+      const dim3 grid((x.rows + kPfM - 1) / kPfM, x.cols / 256);
+      const int rb = static_cast<int>(row_bytes_of(x.type, x.cols));
+      if (x.type == T_Q4_K)
+        k_pf_planes<T_Q4_K><<<grid, 128, 0, e->stream>>>(x.w, x.rows, rb, x.cols / 256, dst, info);
+      else
+        k_pf_planes<T_Q6_K><<<grid, 128, 0, e->stream>>>(x.w, x.rows, rb, x.cols / 256, dst, info);
+      CK(cudaGetLastError());
+      off += plane_bytes(x.type, x.rows, x.cols) + info_bytes(x.rows, x.cols);
+    }
   e->pf_cap = cap;
   e->pf_kmax = kmax;
   return C2S_OK;
 }
 
 // K-quant GEMM of the chunk's n tokens (their Q8_K rows in pf_q8 / pf_d8)
-static int pf_gemm(c2s_engine *e, const uint8_t *w, int type, int rows, int cols, int n, float *out, int ldo, int mode,
+static int pf_gemm(c2s_engine *e, int l, int which, int type, int rows, int cols, int n, float *out, int ldo, int mode,
                    const float *bias) {
   PfGemm G{};
-  G.w = w;
+  G.planes = e->pf_pl[l][which];
+  G.rowinfo = e->pf_ri[l][which];
   G.type = type;
   G.rows = rows;
   G.cols = cols;
-  G.row_bytes = static_cast<int>(row_bytes_of(type, cols));
-  G.aq = e->pf_q8;
+  G.a = e->pf_q8;
   G.ad = e->pf_d8;
-  G.lda = e->pf_kmax;
-  G.ldd = e->pf_kmax / 256;
+  G.abs = e->pf_bs;
   G.M = n;
   G.out = out;
   G.ldo = ldo;
   G.mode = mode;
   G.bias = bias;
   G.err = &e->st->err;
-  const dim3 grid((rows + kPfN - 1) / kPfN, (n + kPfM - 1) / kPfM);
+  const dim3 grid((rows + kPfM - 1) / kPfM, (n + kPfN - 1) / kPfN);
   if (type == T_Q4_K)
     k_pf_gemm<T_Q4_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(G);
   else
@@ -1862,7 +1905,7 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
   const c2s_model_desc &d = e->d;
   const int H = d.embd, F = d.ffn, hd = d.head_dim, nqh = d.n_heads, nkv = d.n_kv_heads;
   const int nq = nqh * hd, kvd = nkv * hd, L = d.n_layers, qpk = nqh / nkv;
-  const int kmax = e->pf_kmax, ldd = kmax / 256;
+
   const size_t head_stride = static_cast<size_t>(d.max_tokens) * hd;
   const size_t plane = static_cast<size_t>(L) * nkv * head_stride;
   cudaStream_t s = e->stream;
@@ -1872,11 +1915,11 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
   CK(cudaGetLastError());
   for (int l = 0; l < L; ++l) {
     const LayerDev &Ld = e->layers[l];
-    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.attn_norm, d.eps, H, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.attn_norm, d.eps, H, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
     int rc;
-    if ((rc = pf_gemm(e, Ld.q, Ld.tq, nq, H, n, e->pf_q, nq, PF_STORE, Ld.qb)) ||
-        (rc = pf_gemm(e, Ld.k, Ld.tk, kvd, H, n, e->pf_k, kvd, PF_STORE, Ld.kb)) ||
-        (rc = pf_gemm(e, Ld.v, Ld.tv, kvd, H, n, e->pf_v, kvd, PF_STORE, Ld.vb)))
+    if ((rc = pf_gemm(e, l, 0, Ld.tq, nq, H, n, e->pf_q, nq, PF_STORE, Ld.qb)) ||
+        (rc = pf_gemm(e, l, 1, Ld.tk, kvd, H, n, e->pf_k, kvd, PF_STORE, Ld.kb)) ||
+        (rc = pf_gemm(e, l, 2, Ld.tv, kvd, H, n, e->pf_v, kvd, PF_STORE, Ld.vb)))
       return rc;
     float *kc = e->kv + static_cast<size_t>(l) * nkv * head_stride, *vc = kc + plane;
     k_pf_rope_store<<<n, kThreads, static_cast<size_t>(nqh + nkv) * hd * 4, s>>>(
@@ -1900,17 +1943,17 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     A.eps = d.eps;
     A.err = &e->st->err;
     k_pf_attention<<<dim3(nkv, n), kThreads, e->attn_smem, s>>>(A);
-    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
-    if ((rc = pf_gemm(e, Ld.o, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
-    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.ffn_norm, d.eps, H, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
-    if ((rc = pf_gemm(e, Ld.gate, Ld.tgate, F, H, n, e->pf_g, F, PF_STORE, nullptr)) ||
-        (rc = pf_gemm(e, Ld.up, Ld.tup, F, H, n, e->pf_u, F, PF_STORE, nullptr)))
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
+    if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.ffn_norm, d.eps, H, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
+    if ((rc = pf_gemm(e, l, 4, Ld.tgate, F, H, n, e->pf_g, F, PF_STORE, nullptr)) ||
+        (rc = pf_gemm(e, l, 5, Ld.tup, F, H, n, e->pf_u, F, PF_STORE, nullptr)))
       return rc;
     const size_t cnt = static_cast<size_t>(n) * F;
     k_pf_swiglu<<<static_cast<int>(std::min<size_t>((cnt + kThreads - 1) / kThreads, 4096)), kThreads, 0, s>>>(
         e->pf_g, e->pf_u, cnt);
-    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, kmax, e->pf_d8, ldd, nullptr);
-    if ((rc = pf_gemm(e, Ld.down, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
+    if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
     CK(cudaGetLastError());
   }
   // the last token's residual stream (read by a following ComputeLogits /
@@ -1918,7 +1961,7 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
   CK(cudaMemcpyAsync(e->X, e->pf_x + static_cast<size_t>(n - 1) * H, static_cast<size_t>(H) * 4,
                      cudaMemcpyDeviceToDevice, s));
   k_pf_norm_q8k<<<1, kThreads, 0, s>>>(e->pf_x + static_cast<size_t>(n - 1) * H, H, e->out_norm, d.eps, H, 1,
-                                       e->pf_q8, kmax, e->pf_d8, ldd, e->normx);
+                                       e->pf_q8, e->pf_d8, e->pf_bs, e->normx);
   k_pf_commit<<<1, kThreads, 0, s>>>(e->st, e->token_ids, e->pf_tok, n, p0, d.max_tokens);
   CK(cudaGetLastError());
   return C2S_OK;

@@ -129,14 +129,6 @@ __device__ __forceinline__ float ldstf(const float *p) { return __ldcg(p); }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
-// n arrivals on a barrier in one operation
-__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t n) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(n) : "memory");
-}
 
 // Grid-wide barrier of the compute warps: one monotonically increasing
 // arrival counter (zeroed at launch).  Thread 0 of each CTA arrives with a

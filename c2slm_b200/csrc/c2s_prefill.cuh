@@ -71,26 +71,46 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
-// K-quant x Q8_K GEMM: out[t][r] (+)= sum_k W[r][k] x[t][k] for a tile of
-// 128 tokens x 64 weight rows per CTA, one superblock (K = 256) per round:
-//   A (tokens' Q8_K bytes)   8 K-steps x [128 rows x 32 B]   32 KB
-//   B planes hi, lo (, m)    8 K-steps x [64 rows x 32 B]    16 KB each
-//   TMEM accumulators        hi | lo | m, 64 columns each
+// K-quant x Q8_K GEMM: out[t][r] (+)= sum_k W[r][k] x[t][k], one CTA per tile
+// of 128 weight rows (the MMA's M, TMEM lanes) x 128 tokens (N, columns),
+// one superblock (K = 256) per round.
+//
+// Operands sit in HBM already in the tensor cores' shared-memory layout
+// (K-major, no swizzle: core matrices of 8 rows x 16 B; per 32-B K step the
+// two 16-B halves 128 B apart, 8-row groups 256 B apart), so a round is a few
+// 1-D bulk copies:
+//   weight planes [row tile][superblock][hi, lo] 8 K steps x [128 x 32 B]  64 KB
+//   token tile    [token tile][superblock]       8 K steps x [128 x 32 B]  32 KB
+//   token scales  d8 [token tile][superblock][128] f32, sub-block sums
+//                 bs [token tile][superblock][128][8] int16
+// (planes by k_pf_planes once per weight matrix, tokens by k_pf_norm_q8k).
+// Per row the block scales (d, dmin) and the 6-bit mins m_j come from a
+// table rowinfo[row][superblock]; the Q4_K min term sum_j m_j * bs_j is an
+// integer dot on the CUDA cores.
+// Warps 0-7: epilogue (warp w: TMEM lanes 32 (w % 4) .. (the rows), tokens
+// 64 (w / 4) ..), warp 8 lane 0: copies, warp 9 lane 0: MMAs.  Two
+// shared-memory stages and two TMEM accumulator sets overlap the copies of
+// round s+1, the MMAs of round s and the epilogue of round s-1.
 // ---------------------------------------------------------------------------
-constexpr int kPfM = 128, kPfN = 64, kPfThreads = 128;
-constexpr int kPfAStep = kPfM * 32, kPfBStep = kPfN * 32;
-constexpr int kPfABytes = 8 * kPfAStep, kPfBPlane = 8 * kPfBStep;
-constexpr int kPfSmem = kPfABytes + 3 * kPfBPlane + 2 * kPfN * 4 + 1024;
+constexpr int kPfM = 128, kPfN = 128, kPfThreads = 320;
+constexpr int kPfKStep = 128 * 32, kPfPlane = 8 * kPfKStep;  // per superblock: 32 KB
+constexpr int kPfTokTile = kPfPlane;                          // token tile per superblock
+constexpr int kPfD8Bytes = kPfN * 4, kPfBsBytes = kPfN * 16;
+constexpr int kPfStage = 2 * kPfPlane + kPfTokTile + kPfD8Bytes + kPfBsBytes;
+constexpr int kPfStages = 2;
+constexpr int kPfSmem = kPfStages * kPfStage + 128;
 
 enum PfMode { PF_STORE = 0, PF_ADD = 1 };
 
 struct PfGemm {
-  const uint8_t *w;  // weight rows (GGML blocks), row_bytes each
-  int type, rows, cols, row_bytes;
-  const int8_t *aq;  // tokens' Q8_K bytes [M][lda]
-  const float *ad;   // tokens' superblock scales [M][ldd]
-  int lda, ldd, M;
-  float *out;        // [M][ldo]
+  const uint8_t *planes;  // [row tile][superblock][2][32 KB]
+  const uint4 *rowinfo;   // [row tile * 128 + r][superblock]: d, dmin (f32 bits), m[8] bytes
+  int type, rows, cols;
+  const uint8_t *a;    // token tiles [token tile][superblock][32 KB]
+  const float *ad;     // [token tile][superblock][128]
+  const int16_t *abs;  // [token tile][superblock][128][8]
+  int M;
+  float *out;  // [M][ldo]
   int ldo, mode;
   const float *bias;  // [rows] or null (PF_STORE)
   unsigned *err;
@@ -98,7 +118,9 @@ struct PfGemm {
 
 // byte offset of (row r, byte kb of a 32-B K step) in one K step of the
 // interleaved layout
-__device__ __forceinline__ int pf_off(int r, int kb) { return (r >> 3) * 256 + (kb >> 4) * 128 + (r & 7) * 16 + (kb & 15); }
+__host__ __device__ __forceinline__ int pf_off(int r, int kb) {
+  return (r >> 3) * 256 + (kb >> 4) * 128 + (r & 7) * 16 + (kb & 15);
+}
 
 // 16 int8 digits (hi, lo) of v = q * s for 16 weights of one row
 __device__ __forceinline__ void pf_digits16(const int (&v)[16], uint4 &hi, uint4 &lo) {
@@ -117,188 +139,251 @@ __device__ __forceinline__ void pf_digits16(const int (&v)[16], uint4 &hi, uint4
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// Digit planes and row table of one weight matrix: CTA (row tile, superblock).
+// Rows past the matrix are zero.
+template <int TYPE>
+__global__ void __launch_bounds__(128) k_pf_planes(const uint8_t *w, int rows, int row_bytes, int nsb, uint8_t *planes,
+                                                   uint4 *rowinfo) {
+  const int R = blockIdx.x, s = blockIdx.y, r0 = R * kPfM;
+  uint8_t *dst = planes + (static_cast<size_t>(R) * nsb + s) * 2 * kPfPlane;
+  if constexpr (TYPE == T_Q4_K) {
+    // task (row rr, sub-block pair p): sub-blocks 2p (low nibbles), 2p+1 (high)
+    for (int task = threadIdx.x; task < kPfM * 4; task += 128) {
+      const int rr = task >> 2, p = task & 3;
+      const bool valid = r0 + rr < rows;
+      const uint8_t *blk = w + static_cast<size_t>(valid ? r0 + rr : 0) * row_bytes + s * 144;
+      const uint4 hd = __ldg(reinterpret_cast<const uint4 *>(blk));
+      const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * p));
+      const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * p));
+      // 6-bit scales / mins of sub-blocks 2p, 2p+1 (tensor/ops.go:354-361)
+      const uint32_t sc8[3] = {hd.y, hd.z, hd.w};
+      auto sbyte = [&](int i) { return static_cast<int>((sc8[i >> 2] >> (8 * (i & 3))) & 0xFFu); };
+      int sc[2], mn[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int j = 2 * p + u;
+        if (j < 4) {
+          sc[u] = sbyte(j) & 63;
+          mn[u] = sbyte(j + 4) & 63;
+        } else {
+          sc[u] = (sbyte(j + 4) & 15) | ((sbyte(j - 4) >> 6) << 4);
+          mn[u] = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+        }
+        if (!valid) sc[u] = mn[u] = 0;
+      }
+      const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int j = 2 * p + u;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          int v[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const uint32_t byte = (qw[half * 4 + (e >> 2)] >> (8 * (e & 3))) & 0xFFu;
+            v[e] = static_cast<int>(u == 0 ? (byte & 15u) : (byte >> 4)) * sc[u];
+          }
+          uint4 hi, lo;
+          pf_digits16(v, hi, lo);
+          const int off = j * kPfKStep + pf_off(rr, half * 16);
+          *reinterpret_cast<uint4 *>(dst + off) = hi;
+          *reinterpret_cast<uint4 *>(dst + kPfPlane + off) = lo;
+        }
+      }
+      uint8_t *ri = reinterpret_cast<uint8_t *>(rowinfo + (static_cast<size_t>(r0) + rr) * nsb + s);
+      ri[8 + 2 * p] = static_cast<uint8_t>(mn[0]);
+      ri[9 + 2 * p] = static_cast<uint8_t>(mn[1]);
+      if (p == 0) {
+        const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
+        reinterpret_cast<float *>(ri)[0] = valid ? dd.x : 0.f;
+        reinterpret_cast<float *>(ri)[1] = valid ? dd.y : 0.f;
+      }
+    }
+  } else {
+    // Q6_K task (row rr, half n, quarter k): K step j = 4n + k, elements
+    // l = 0..31 of q6u = low 4 bits | 2 high bits << 4, group scale
+    // sc[8n + 2k + l / 16] (c2_tensor_gemv2_q6_k_q8_k_nosimd_gen.go:80-237)
+    for (int task = threadIdx.x; task < kPfM * 8; task += 128) {
+      const int rr = task >> 3, n = (task >> 2) & 1, k = task & 3;
+      const bool valid = r0 + rr < rows;
+      const uint8_t *blk = w + static_cast<size_t>(valid ? r0 + rr : 0) * row_bytes + s * 210;
+      uint32_t ql[8], qh[8];
+      ld_window<8>(blk + 64 * n + 32 * (k & 1), ql);
+      ld_window<8>(blk + 128 + 32 * n, qh);
+      const int g0 = 8 * n + 2 * k;
+      const int s0 = valid ? static_cast<int8_t>(blk[192 + g0]) : 0;
+      const int s1 = valid ? static_cast<int8_t>(blk[192 + g0 + 1]) : 0;
+      const int j = 4 * n + k;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        int v[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int wi = half * 4 + (e >> 2), b = e & 3;
+          const uint32_t lb = (ql[wi] >> (8 * b)) & 0xFFu, hb = (qh[wi] >> (8 * b)) & 0xFFu;
+          const int q6 = static_cast<int>(((k >> 1) ? (lb >> 4) : (lb & 15u)) | (((hb >> (2 * k)) & 3u) << 4));
+          v[e] = (q6 - 32) * (half ? s1 : s0);
+        }
+        uint4 hi, lo;
+        pf_digits16(v, hi, lo);
+        const int off = j * kPfKStep + pf_off(rr, half * 16);
+        *reinterpret_cast<uint4 *>(dst + off) = hi;
+        *reinterpret_cast<uint4 *>(dst + kPfPlane + off) = lo;
+      }
+      if (n == 0 && k == 0) {
+        const float d6 = valid ? h2f(ld16(blk + 208)) : 0.f;
+        rowinfo[(static_cast<size_t>(r0) + rr) * nsb + s] = make_uint4(__float_as_uint(d6), 0u, 0u, 0u);
+      }
+    }
+  }
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfGemm G) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bar;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages], tfull[2], tempty[2];
   __shared__ uint32_t s_tmem;
-  constexpr int NPL = TYPE == T_Q4_K ? 3 : 2;  // digit planes (+ min plane)
-  uint8_t *sA = smem;
-  uint8_t *sB = smem + kPfABytes;  // plane p at sB + p * kPfBPlane
-  float *rowd = reinterpret_cast<float *>(sB + 3 * kPfBPlane);
-  float *rowdm = rowd + kPfN;
+  constexpr uint32_t kStageBytes = kPfStage;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int r0 = blockIdx.x * kPfN, t0 = blockIdx.y * kPfM;
+  const int R = blockIdx.x, T = blockIdx.y, r0 = R * kPfM, t0 = T * kPfN;
   const int nsb = G.cols / 256;
   if (tid == 0) {
-    mbar_init(&bar, 1);
+    for (int i = 0; i < kPfStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1 + 8);  // the MMAs' commit and the eight epilogue warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);
+    }
     fence_mbar_init();
   }
-  if (warp == 0) {  // 4 x 64 columns: hi, lo, m (and one spare)
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_addr(&s_tmem)));
+  if (warp == 0) {  // two accumulator sets of hi | lo, 128 columns each
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(&s_tmem)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tmem_fence_before();
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = s_tmem;
-  const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
-  const int tok = t0 + tid;  // this thread's token in the epilogue (TMEM lane tid)
-  float acc[kPfN];
-#pragma unroll
-  for (int r = 0; r < kPfN; ++r) acc[r] = 0.f;
   bool ok = true;
-  for (int s = 0; s < nsb && ok; ++s) {
-    // ---- A: 128 tokens x 256 Q8_K bytes of superblock s (zeros past M)
-    for (int i = tid; i < kPfM * 16; i += kPfThreads) {
-      const int r = i >> 4, c = i & 15;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (t0 + r < G.M)
-        v = __ldg(reinterpret_cast<const uint4 *>(G.aq + static_cast<size_t>(t0 + r) * G.lda + s * 256 + c * 16));
-      *reinterpret_cast<uint4 *>(sA + (c >> 1) * kPfAStep + pf_off(r, (c & 1) * 16)) = v;
-    }
-    // ---- B: 64 rows of superblock s as digit planes
-    if constexpr (TYPE == T_Q4_K) {
-      // task (row rr, sub-block pair p): sub-blocks 2p (low nibbles), 2p+1 (high)
-      for (int task = tid; task < kPfN * 4; task += kPfThreads) {
-        const int rr = task >> 2, p = task & 3;
-        const bool valid = r0 + rr < G.rows;
-        const uint8_t *blk = G.w + static_cast<size_t>(valid ? r0 + rr : 0) * G.row_bytes + s * 144;
-        const uint4 hd = __ldg(reinterpret_cast<const uint4 *>(blk));
-        const uint4 qa = __ldg(reinterpret_cast<const uint4 *>(blk + 16 + 32 * p));
-        const uint4 qb = __ldg(reinterpret_cast<const uint4 *>(blk + 32 + 32 * p));
-        // 6-bit scales / mins of sub-blocks 2p, 2p+1 (tensor/ops.go:354-361)
-        const uint32_t sc8[3] = {hd.y, hd.z, hd.w};
-        auto sbyte = [&](int i) { return static_cast<int>((sc8[i >> 2] >> (8 * (i & 3))) & 0xFFu); };
-        int sc[2], mn[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int j = 2 * p + u;
-          if (j < 4) {
-            sc[u] = sbyte(j) & 63;
-            mn[u] = sbyte(j + 4) & 63;
-          } else {
-            sc[u] = (sbyte(j + 4) & 15) | ((sbyte(j - 4) >> 6) << 4);
-            mn[u] = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
-          }
-          if (!valid) sc[u] = mn[u] = 0;
-        }
-        const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int j = 2 * p + u;
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            int v[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const uint32_t byte = (qw[half * 4 + (e >> 2)] >> (8 * (e & 3))) & 0xFFu;
-              v[e] = static_cast<int>(u == 0 ? (byte & 15u) : (byte >> 4)) * sc[u];
-            }
-            uint4 hi, lo;
-            pf_digits16(v, hi, lo);
-            const int off = j * kPfBStep + pf_off(rr, half * 16);
-            *reinterpret_cast<uint4 *>(sB + off) = hi;
-            *reinterpret_cast<uint4 *>(sB + kPfBPlane + off) = lo;
-            const uint32_t m4 = static_cast<uint32_t>(mn[u]) * 0x01010101u;
-            *reinterpret_cast<uint4 *>(sB + 2 * kPfBPlane + off) = make_uint4(m4, m4, m4, m4);
-          }
-        }
-        if (p == 0) {
-          const float2 dd = __half22float2(*reinterpret_cast<const __half2 *>(&hd.x));
-          rowd[rr] = valid ? dd.x : 0.f;
-          rowdm[rr] = valid ? dd.y : 0.f;
-        }
-      }
-    } else {
-      // Q6_K task (row rr, half n, quarter k): K step j = 4n + k, elements
-      // l = 0..31 of q6u = low 4 bits | 2 high bits << 4, group scale
-      // sc[8n + 2k + l / 16] (c2_tensor_gemv2_q6_k_q8_k_nosimd_gen.go:80-237)
-      for (int task = tid; task < kPfN * 8; task += kPfThreads) {
-        const int rr = task >> 3, n = (task >> 2) & 1, k = task & 3;
-        const bool valid = r0 + rr < G.rows;
-        const uint8_t *blk = G.w + static_cast<size_t>(valid ? r0 + rr : 0) * G.row_bytes + s * 210;
-        uint32_t ql[8], qh[8];
-        ld_window<8>(blk + 64 * n + 32 * (k & 1), ql);
-        ld_window<8>(blk + 128 + 32 * n, qh);
-        const int g0 = 8 * n + 2 * k;
-        const int s0 = valid ? static_cast<int8_t>(blk[192 + g0]) : 0;
-        const int s1 = valid ? static_cast<int8_t>(blk[192 + g0 + 1]) : 0;
-        const int j = 4 * n + k;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          int v[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int w = half * 4 + (e >> 2), b = e & 3;
-            const uint32_t lb = (ql[w] >> (8 * b)) & 0xFFu, hb = (qh[w] >> (8 * b)) & 0xFFu;
-            const int q6 = static_cast<int>(((k >> 1) ? (lb >> 4) : (lb & 15u)) | (((hb >> (2 * k)) & 3u) << 4));
-            v[e] = (q6 - 32) * (half ? s1 : s0);
-          }
-          uint4 hi, lo;
-          pf_digits16(v, hi, lo);
-          const int off = j * kPfBStep + pf_off(rr, half * 16);
-          *reinterpret_cast<uint4 *>(sB + off) = hi;
-          *reinterpret_cast<uint4 *>(sB + kPfBPlane + off) = lo;
-        }
-        if (n == 0 && k == 0) rowd[rr] = valid ? h2f(ld16(blk + 208)) : 0.f;
+  if (warp == 8) {
+    // ---------------------------------------------------------- copies
+    if (lane == 0) {
+      const uint8_t *pw = G.planes + static_cast<size_t>(R) * nsb * 2 * kPfPlane;
+      const size_t tb0 = static_cast<size_t>(T) * nsb;
+      for (int s = 0; s < nsb && ok; ++s) {
+        const int st = s % kPfStages;
+        if (s >= kPfStages) ok = mbar_wait_bounded(&empty[st], static_cast<uint32_t>((s / kPfStages - 1) & 1), G.err);
+        if (!ok) break;
+        uint8_t *dst = smem + st * kPfStage;
+        mbar_arrive_expect_tx(&full[st], kStageBytes);
+        bulk_g2s(dst, pw + static_cast<size_t>(s) * 2 * kPfPlane, 2 * kPfPlane, &full[st]);
+        bulk_g2s(dst + 2 * kPfPlane, G.a + (tb0 + s) * kPfTokTile, kPfTokTile, &full[st]);
+        bulk_g2s(dst + 2 * kPfPlane + kPfTokTile, G.ad + (tb0 + s) * kPfN, kPfD8Bytes, &full[st]);
+        bulk_g2s(dst + 2 * kPfPlane + kPfTokTile + kPfD8Bytes, G.abs + (tb0 + s) * kPfN * 8, kPfBsBytes, &full[st]);
       }
     }
-    // ---- the MMAs of this superblock (one thread), then the epilogue
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tmem_fence_before();
-    __syncthreads();
-    tmem_fence_after();
-    if (tid == 0) {
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMAs
+    if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_i8(kPfM, kPfN);
+      for (int s = 0; s < nsb && ok; ++s) {
+        const int st = s % kPfStages, tb = s & 1;
+        ok = mbar_wait_bounded(&full[st], static_cast<uint32_t>((s / kPfStages) & 1), G.err);
+        if (ok && s >= 2) ok = mbar_wait_bounded(&tempty[tb], static_cast<uint32_t>(((s >> 1) - 1) & 1), G.err);
+        if (!ok) break;
+        tmem_fence_after();
+        const uint8_t *sw = smem + st * kPfStage, *sx = sw + 2 * kPfPlane;
+        const uint32_t td = tmem + static_cast<uint32_t>(tb * 2 * kPfN);
 #pragma unroll
-      for (int pl = 0; pl < NPL; ++pl)
-        for (int j = 0; j < 8; ++j)
-          umma_i8(tmem + pl * kPfN, umma_sdesc(smem_addr(sA + j * kPfAStep), 128, 256),
-                  umma_sdesc(smem_addr(sB + pl * kPfBPlane + j * kPfBStep), 128, 256), idesc, j > 0 ? 1u : 0u);
-      umma_commit(&bar);
+        for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            umma_i8(td + pl * kPfN, umma_sdesc(smem_addr(sw + pl * kPfPlane + j * kPfKStep), 128, 256),
+                    umma_sdesc(smem_addr(sx + j * kPfKStep), 128, 256), idesc, j > 0 ? 1u : 0u);
+        umma_commit(&empty[st]);  // the stage's operands are read
+        umma_commit(&tfull[tb]);  // the accumulators are complete
+      }
     }
-    ok = mbar_wait_bounded(&bar, static_cast<uint32_t>(s & 1), G.err);
-    tmem_fence_after();
-    if (ok) {
-      const float d8 = tok < G.M ? __ldg(G.ad + static_cast<size_t>(tok) * G.ldd + s) : 0.f;
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const int quad = warp & 3, th = warp >> 2;  // rows 32 quad + lane, tokens 64 th ..
+    const int row = r0 + 32 * quad + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * quad) << 16;
+    float acc[64];
 #pragma unroll
-      for (int c0 = 0; c0 < kPfN; c0 += 16) {
-        uint32_t hi[16], lo[16], mm[16];
-        tmem_ld16(tmem + lane_base + c0, hi);
-        tmem_ld16(tmem + lane_base + kPfN + c0, lo);
-        if constexpr (TYPE == T_Q4_K) tmem_ld16(tmem + lane_base + 2 * kPfN + c0, mm);
+    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    const uint4 *ri = G.rowinfo + static_cast<size_t>(row) * nsb;
+    uint4 rin = __ldg(ri);  // this row's table entry, one superblock ahead
+    for (int s = 0; s < nsb && ok; ++s) {
+      const int st = s % kPfStages, tb = s & 1;
+      const uint4 rv = rin;
+      if (s + 1 < nsb) rin = __ldg(ri + s + 1);
+      ok = mbar_wait_bounded(&tfull[tb], static_cast<uint32_t>((s >> 1) & 1), G.err);
+      {  // ok made uniform over the epilogue warps (all leave together)
+        uint32_t all;
+        asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 2, 256, q;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(all) : "r"(ok ? 1u : 0u) : "memory");
+        ok = all != 0;
+      }
+      if (!ok) break;
+      tmem_fence_after();
+      const float dr = __uint_as_float(rv.x), dmr = __uint_as_float(rv.y);
+      const uint8_t *stg = smem + st * kPfStage + 2 * kPfPlane + kPfTokTile;
+      const float *sd8 = reinterpret_cast<const float *>(stg);
+      const uint4 *sbs = reinterpret_cast<const uint4 *>(stg + kPfD8Bytes);
+      const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(tb * 2 * kPfN + 64 * th);
+#pragma unroll
+      for (int c0 = 0; c0 < 64; c0 += 16) {
+        uint32_t hi[16], lo[16];
+        tmem_ld16(ta + c0, hi);
+        tmem_ld16(ta + kPfN + c0, lo);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int r = c0 + i;
+          const int tk = 64 * th + c0 + i;
+          const float d8 = sd8[tk];
           const int isum = static_cast<int>(hi[i]) * 128 + static_cast<int>(lo[i]);
-          const float dd = __fmul_rn(rowd[r], d8);
-          float t = __fmul_rn(static_cast<float>(isum), dd);
-          if constexpr (TYPE == T_Q4_K)
-            t = __fsub_rn(t, __fmul_rn(static_cast<float>(static_cast<int>(mm[i])), __fmul_rn(rowdm[r], d8)));
-          acc[r] = __fadd_rn(acc[r], t);
+          if constexpr (TYPE == T_Q4_K) {
+            const uint4 b = sbs[tk];  // sub-block sums 0..7 as int16 pairs
+            int msum = __dp2a_lo(static_cast<int>(b.x), static_cast<int>(rv.z), 0);
+            msum = __dp2a_hi(static_cast<int>(b.y), static_cast<int>(rv.z), msum);
+            msum = __dp2a_lo(static_cast<int>(b.z), static_cast<int>(rv.w), msum);
+            msum = __dp2a_hi(static_cast<int>(b.w), static_cast<int>(rv.w), msum);
+            const float t = __fsub_rn(__fmul_rn(static_cast<float>(isum), __fmul_rn(dr, d8)),
+                                      __fmul_rn(static_cast<float>(msum), __fmul_rn(dmr, d8)));
+            acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
+          } else {
+            acc[c0 + i] = __fadd_rn(acc[c0 + i], __fmul_rn(static_cast<float>(isum), __fmul_rn(dr, d8)));
+          }
+        }
+      }
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&tempty[tb]);
+        mbar_arrive(&empty[st]);
+      }
+    }
+    if (ok && row < G.rows) {
+      const float bias = (G.mode == PF_STORE && G.bias) ? __ldg(G.bias + row) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const int tok = t0 + 64 * th + i;
+        if (tok < G.M) {
+          float *o = G.out + static_cast<size_t>(tok) * G.ldo + row;
+          if (G.mode == PF_ADD)
+            *o = __fadd_rn(*o, acc[i]);
+          else
+            *o = G.bias ? __fadd_rn(acc[i], bias) : acc[i];
         }
       }
     }
-    tmem_fence_before();
-    __syncthreads();  // smem and TMEM free for the next superblock
-    tmem_fence_after();
-  }
-  if (ok && tok < G.M) {
-    float *o = G.out + static_cast<size_t>(tok) * G.ldo + r0;
-#pragma unroll
-    for (int r = 0; r < kPfN; ++r)
-      if (r0 + r < G.rows) {
-        if (G.mode == PF_ADD)
-          o[r] = __fadd_rn(o[r], acc[r]);
-        else
-          o[r] = G.bias ? __fadd_rn(acc[r], __ldg(G.bias + r0 + r)) : acc[r];
-      }
   }
   tmem_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
 
 // ---------------------------------------------------------------------------
@@ -315,14 +400,18 @@ __global__ void __launch_bounds__(kThreads) k_pf_embed(const int *tok, int n, in
 }
 
 // One token's row x[t][0..K) -> optional RMSNorm with weight nw (tensor/ops.go:
-// 207-218) -> Q8_K (internal/simd/c2_quantize_q8_k_gen.go:11-91): bytes
-// q[t][0..K), superblock scales d[t][0..K/256).  xn (optional) receives the
+// 207-218) -> Q8_K (internal/simd/c2_quantize_q8_k_gen.go:11-91), written for
+// the GEMM: bytes into the token tiles q [token tile][superblock][32 KB],
+// superblock scales d [token tile][superblock][128], sub-block sums bs
+// [token tile][superblock][128][8] (int16).  xn (optional) receives the
 // normalised f32 row.
 __global__ void __launch_bounds__(kThreads) k_pf_norm_q8k(const float *x, int ldx, const float *nw, float eps, int K,
-                                                          int n, int8_t *q, int ldq, float *d, int ldd, float *xn) {
+                                                          int n, uint8_t *q, float *d, int16_t *bs, float *xn) {
   __shared__ float scratch[kWarps];
+  __shared__ int32_t s_bsum[kWarps][16];
   const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (t >= n) return;
+  const int nsb = K / 256, T = t / kPfN, tr = t % kPfN;
   const float *xr = x + static_cast<size_t>(t) * ldx;
   float inv = 1.f;
   if (nw) {
@@ -338,7 +427,7 @@ __global__ void __launch_bounds__(kThreads) k_pf_norm_q8k(const float *x, int ld
     const float mean = __fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps);
     inv = static_cast<float>(1.0 / sqrt(static_cast<double>(mean)));
   }
-  for (int sb = warp; sb < K / 256; sb += kWarps) {
+  for (int sb = warp; sb < nsb; sb += kWarps) {
     float v[8];
     const float4 a = *reinterpret_cast<const float4 *>(xr + sb * 256 + lane * 8);
     const float4 b = *reinterpret_cast<const float4 *>(xr + sb * 256 + lane * 8 + 4);
@@ -352,16 +441,22 @@ __global__ void __launch_bounds__(kThreads) k_pf_norm_q8k(const float *x, int ld
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = v[i];
     }
-    int32_t bs[16];
-    quantize_sb_warp(v, d + static_cast<size_t>(t) * ldd + sb, bs, [&](int ln, const int (&qv)[8]) {
+    const size_t tile = static_cast<size_t>(T) * nsb + sb;
+    quantize_sb_warp(v, d + tile * kPfN + tr, s_bsum[warp], [&](int ln, const int (&qv)[8]) {
       uint32_t w0 = 0, w1 = 0;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         w0 |= (static_cast<uint32_t>(qv[k]) & 0xFFu) << (8 * k);
         w1 |= (static_cast<uint32_t>(qv[4 + k]) & 0xFFu) << (8 * k);
       }
-      *reinterpret_cast<uint2 *>(q + static_cast<size_t>(t) * ldq + sb * 256 + ln * 8) = make_uint2(w0, w1);
+      // 8 bytes = elements 8ln .. 8ln+7: K step ln / 4, bytes (ln % 4) * 8 of it
+      *reinterpret_cast<uint2 *>(q + tile * kPfTokTile + (ln >> 2) * kPfKStep + pf_off(tr, (ln & 3) * 8)) =
+          make_uint2(w0, w1);
     });
+    __syncwarp();
+    if (lane < 8)  // sub-block sums: two 16-element sums each (|sum| <= 4064)
+      bs[(tile * kPfN + tr) * 8 + lane] = static_cast<int16_t>(s_bsum[warp][2 * lane] + s_bsum[warp][2 * lane + 1]);
+    __syncwarp();
   }
 }
 
