@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B tensor-parallel line (config 3)")
     ap.add_argument("--tp-ctx", type=int, default=4096, help="config 3 context length before decoding")
     ap.add_argument("--tp-steps", type=int, default=256, help="config 3 decode steps")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill line (config 4)")
+    ap.add_argument("--prefill-tokens", type=int, default=2048, help="config 4 prompt length")
     return ap.parse_args()
 
 
@@ -80,6 +82,9 @@ def stage_bytes(path: str) -> dict:
             out["o_proj"] += len(T[p + "attn_output.weight"].data)
             out["gate_up"] += sum(len(T[p + n].data) for n in ("ffn_norm.weight", "ffn_gate.weight", "ffn_up.weight"))
             out["down"] += len(T[p + "ffn_down.weight"].data)
+            for n in ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"):
+                d = T[p + n + ".weight"].dimensions
+                out["proj_weights"] = out.get("proj_weights", 0) + int(d[0]) * int(d[1])
         te = T["token_embd.weight"]
         out["qkv"] += len(te.data) // int(te.dimensions[1])  # one embedding row
         ow = T.get("output.weight", te)
@@ -354,9 +359,14 @@ def run_ours(args) -> None:
     tp7b = None
     if not args.no_tp7b:
         tp7b = run_tp7b(args, world, rank, local, dist)
+    prefill = None
+    if not args.no_prefill and rank == 0:
+        prefill = run_prefill(args, local)
     if rank == 0:
         if tp7b is not None:
             line["tp7b"] = tp7b
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -414,6 +424,46 @@ def run_tp7b(args, world: int, rank: int, local: int, dist) -> dict:
             "gpu_launches": launches, "prefill_s": round(prefill_s, 1),
             "decode": "persistent kernel, partial sums exchanged over NVLink peer memory" if launches == 1
                       else "per-phase kernels with NCCL collectives"}
+
+
+INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 (nominal; 8.1k MACs/clk/SM measured with tcgen05 kind::i8)
+
+
+def run_prefill(args, local: int) -> dict:
+    """Config 4's prefill: a uniform-random prompt of --prefill-tokens ids
+    ingested by a Qwen2.5-1.5B-shaped Q4_K_M model (all projections K-quant)
+    through IngestFrom -- K-quant x Q8_K projections as tcgen05 int8 GEMMs.
+    Timed end to end through the public API (host ids in, NormX back), after
+    one warm-up ingest that also builds the weight planes."""
+    import numpy as np
+    import c2slm_b200 as K
+    from c2slm_b200 import synth
+    n = args.prefill_tokens
+    path = synth.cached_model("qwen15b")
+    prompt = np.random.default_rng(3).integers(0, 151643, n).astype(np.int32)
+    eng = K.Engine(path, device=local, max_tokens=n + 64)
+    eng.ingest_from(0, prompt[:256])
+    eng.sync()
+    times = []
+    for _ in range(3):
+        eng.reset()
+        t0 = time.perf_counter()
+        eng.ingest_from(0, prompt)
+        eng.sync()
+        times.append(time.perf_counter() - t0)
+    eng.close()
+    dt = statistics.median(times)
+    sb = stage_bytes(path)
+    macs = sb.get("proj_weights")  # multiply-adds of the layer projections per token
+    out = {"metric": "prefill tokens/s (config 4: Qwen2.5-1.5B-shaped Q4_K_M, uniform-random prompt)",
+           "value": round(n / dt, 1), "unit": "tokens/s", "tokens": n, "ms": round(dt * 1000.0, 2),
+           "api": "c2s_ingest_from (host ids in, NormX out)",
+           "kernels": "tcgen05 kind::i8 GEMM per K-quant projection (128 rows x 128 tokens per CTA)"}
+    if macs:
+        tops = 2.0 * macs * n / dt / 1e12
+        out.update({"int8_tops_projections": round(tops, 1), "int8_nominal_tops": INT8_NOMINAL_TOPS,
+                    "frac_of_nominal_int8": round(tops / INT8_NOMINAL_TOPS, 4)})
+    return out
 
 
 def eng_seq_wrap(i: int) -> bool:
