@@ -1230,6 +1230,8 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   CK(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(k_pf_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+  CK(cudaFuncSetAttribute(k_pf_flash<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pf_flash_smem(128))));
+  CK(cudaFuncSetAttribute(k_pf_flash<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pf_flash_smem(64))));
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   {  // prefill on the tensor cores: one GPU, every layer projection a K-quant, superblock-aligned widths
@@ -1925,7 +1927,7 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     k_pf_rope_store<<<n, kThreads, static_cast<size_t>(nqh + nkv) * hd * 4, s>>>(
         e->pf_q, e->pf_k, e->pf_v, nq, kvd, n, p0, nqh, nkv, hd, e->rope_cos, e->rope_sin, kMaxContext, Ld.qn, Ld.kn,
         d.eps, kc, vc, head_stride);
-    PfAttn A{};
+    PfFlash A{};
     A.q = e->pf_q;
     A.out = e->pf_att;
     A.kc = kc;
@@ -1934,15 +1936,14 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     A.ldq = nq;
     A.n = n;
     A.p0 = p0;
-    A.n_kv = nkv;
     A.qpk = qpk;
     A.n_heads = nqh;
-    A.hd = hd;
-    A.max_splits = e->max_splits;
     A.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
-    A.eps = d.eps;
-    A.err = &e->st->err;
-    k_pf_attention<<<dim3(nkv, n), kThreads, e->attn_smem, s>>>(A);
+    const dim3 fgrid(nkv, (n * qpk + kFqN - 1) / kFqN);
+    if (hd == 128)
+      k_pf_flash<128><<<fgrid, kThreads, pf_flash_smem(128), s>>>(A);
+    else
+      k_pf_flash<64><<<fgrid, kThreads, pf_flash_smem(64), s>>>(A);
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
     if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.ffn_norm, d.eps, H, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);

@@ -577,4 +577,192 @@ __global__ void k_pf_commit(DevState *st, int *token_ids, const int *tok, int n,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Causal attention of a prefill chunk, tiled: CTA (kv group g, block of 64
+// query vectors v = token * qpk + head of the group's heads).  Key tiles of
+// 64 positions are staged once per CTA (K transposed), then
+//   S = Q K^T * scale   (4 queries x 4 keys per thread, f32)
+//   online softmax per query (exp in float64 as tensor.Softmax,
+//                        tensor/ops.go:317-339; keys past the query's position
+//                        excluded)
+//   O = O * alpha + P V (4 queries x 8 dims per thread)
+// and O / l at the end (engine/forward.go:143-155 per head and position).
+// ---------------------------------------------------------------------------
+struct PfFlash {
+  const float *q;        // [n][ldq] rotated queries
+  float *out;            // [n][ldq]
+  const float *kc, *vc;  // this layer's planes: group g row p at [g * head_stride + p * hd]
+  size_t head_stride;
+  int ldq, n, p0, qpk, n_heads;
+  float scale;
+};
+
+constexpr int kFqN = 64, kFkN = 64, kFpad = 4;
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
+  extern __shared__ __align__(16) float fsm[];
+  float *Qt = fsm;                        // [HD][kFqN]
+  float *Kt = Qt + HD * kFqN;             // [HD][kFkN + pad]
+  float *Vs = Kt + HD * (kFkN + kFpad);   // [kFkN][HD]
+  float *Pt = Vs + kFkN * HD;             // [kFkN][kFqN + pad] probabilities, key-major
+  float *s_m = Pt + kFkN * (kFqN + kFpad), *s_l = s_m + kFqN, *s_alpha = s_l + kFqN;
+  int *s_lim = reinterpret_cast<int *>(s_alpha + kFqN);  // last key position of each query
+  const int tid = threadIdx.x, g = blockIdx.x;
+  const int nv = A.n * A.qpk, v0 = blockIdx.y * kFqN;
+  if (v0 >= nv) return;
+  const int h0 = g * A.qpk;
+  // ---- queries of the block, transposed; their causal limits
+  for (int i = tid; i < kFqN * (HD / 4); i += kThreads) {  // a warp: 32 queries, one d4 (conflict-free)
+    const int qi = i % kFqN, d4 = (i / kFqN) * 4, v = v0 + qi;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (v < nv) {
+      const int t = v / A.qpk, h = v - t * A.qpk;
+      x = *reinterpret_cast<const float4 *>(A.q + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + d4);
+    }
+    Qt[(d4 + 0) * kFqN + qi] = x.x;
+    Qt[(d4 + 1) * kFqN + qi] = x.y;
+    Qt[(d4 + 2) * kFqN + qi] = x.z;
+    Qt[(d4 + 3) * kFqN + qi] = x.w;
+  }
+  if (tid < kFqN) {
+    const int v = v0 + tid;
+    s_lim[tid] = v < nv ? A.p0 + v / A.qpk : -1;
+    s_m[tid] = -INFINITY;
+    s_l[tid] = 0.f;
+  }
+  const int vlast = min(nv, v0 + kFqN) - 1;
+  const int kend = A.p0 + vlast / A.qpk + 1;  // keys 0 .. kend-1
+  // thread tiles
+  const int sq = (tid >> 4) * 4, sk = (tid & 15) * 4;  // S: 4 queries x 4 keys
+  const int oq = (tid >> 4) * 4, od = (tid & 15) * (HD / 16);  // O: 4 queries x HD/16 dims
+  constexpr int OD = HD / 16;
+  float o[4][OD];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < OD; ++b) o[a][b] = 0.f;
+  const float *kg = A.kc + g * A.head_stride, *vg = A.vc + g * A.head_stride;
+  for (int kb = 0; kb < kend; kb += kFkN) {
+    const int nk = min(kFkN, kend - kb);
+    __syncthreads();  // previous tile fully consumed
+    for (int i = tid; i < kFkN * (HD / 4); i += kThreads) {
+      {  // K transposed: a warp covers 32 keys of one d4 (conflict-free stores)
+        const int kr = i % kFkN, d4 = (i / kFkN) * 4;
+        float4 kx = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kr < nk) kx = __ldcg(reinterpret_cast<const float4 *>(kg + static_cast<size_t>(kb + kr) * HD + d4));
+        Kt[(d4 + 0) * (kFkN + kFpad) + kr] = kx.x;
+        Kt[(d4 + 1) * (kFkN + kFpad) + kr] = kx.y;
+        Kt[(d4 + 2) * (kFkN + kFpad) + kr] = kx.z;
+        Kt[(d4 + 3) * (kFkN + kFpad) + kr] = kx.w;
+      }
+      {  // V as rows
+        const int kr = i / (HD / 4), d4 = (i % (HD / 4)) * 4;
+        float4 vx = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kr < nk) vx = __ldcg(reinterpret_cast<const float4 *>(vg + static_cast<size_t>(kb + kr) * HD + d4));
+        *reinterpret_cast<float4 *>(Vs + kr * HD + d4) = vx;
+      }
+    }
+    __syncthreads();
+    // ---- S = Q K^T for the thread's 4 x 4 tile
+    float sacc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) sacc[a][b] = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < HD; ++d) {
+      const float4 qv = *reinterpret_cast<const float4 *>(Qt + d * kFqN + sq);
+      const float4 kv = *reinterpret_cast<const float4 *>(Kt + d * (kFkN + kFpad) + sk);
+      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) sacc[a][b] = fmaf(qa[a], ka[b], sacc[a][b]);
+    }
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int key = kb + sk + b;
+      float4 w;
+      w.x = key <= s_lim[sq + 0] ? __fmul_rn(sacc[0][b], A.scale) : -INFINITY;
+      w.y = key <= s_lim[sq + 1] ? __fmul_rn(sacc[1][b], A.scale) : -INFINITY;
+      w.z = key <= s_lim[sq + 2] ? __fmul_rn(sacc[2][b], A.scale) : -INFINITY;
+      w.w = key <= s_lim[sq + 3] ? __fmul_rn(sacc[3][b], A.scale) : -INFINITY;
+      if (sk + b >= nk) w = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      *reinterpret_cast<float4 *>(Pt + (sk + b) * (kFqN + kFpad) + sq) = w;
+    }
+    __syncthreads();
+    // ---- online softmax: 4 threads per query, 16 keys each
+    {
+      const int qi = tid >> 2, part = tid & 3;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) mx = fmaxf(mx, Pt[(part * 16 + j) * (kFqN + kFpad) + qi]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_old = s_m[qi], m_new = fmaxf(m_old, mx);
+      float ls = 0.f;
+#pragma unroll 1
+      for (int j = 0; j < 16; ++j) {
+        float *pp = Pt + (part * 16 + j) * (kFqN + kFpad) + qi;
+        const float sv = *pp;
+        const float e = sv == -INFINITY ? 0.f : static_cast<float>(exp(static_cast<double>(__fsub_rn(sv, m_new))));
+        *pp = e;
+        ls += e;
+      }
+      ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+      if (part == 0) {
+        const float alpha = m_new == -INFINITY ? 1.f : static_cast<float>(exp(static_cast<double>(m_old - m_new)));
+        s_alpha[qi] = alpha;
+        s_l[qi] = __fadd_rn(__fmul_rn(s_l[qi], alpha), ls);
+        s_m[qi] = m_new;
+      }
+    }
+    __syncthreads();
+    // ---- O = O * alpha + P V for the thread's 4 queries x OD dims
+    {
+      float al[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) al[a] = s_alpha[oq + a];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < OD; ++b) o[a][b] *= al[a];
+#pragma unroll 4
+      for (int k = 0; k < nk; ++k) {
+        const float4 pv = *reinterpret_cast<const float4 *>(Pt + k * (kFqN + kFpad) + oq);
+        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+        float vv[OD];
+#pragma unroll
+        for (int b = 0; b < OD; b += 4) {
+          const float4 x = *reinterpret_cast<const float4 *>(Vs + k * HD + od + b);
+          vv[b] = x.x, vv[b + 1] = x.y, vv[b + 2] = x.z, vv[b + 3] = x.w;
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < OD; ++b) o[a][b] = fmaf(pa[a], vv[b], o[a][b]);
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int v = v0 + oq + a;
+    if (v < nv) {
+      const int t = v / A.qpk, h = v - t * A.qpk;
+      const float l = s_l[oq + a];
+      float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + od;
+#pragma unroll
+      for (int b = 0; b < OD; ++b) dst[b] = o[a][b] / l;
+    }
+  }
+}
+
+__host__ __device__ inline size_t pf_flash_smem(int hd) {
+  return (static_cast<size_t>(hd) * kFqN + static_cast<size_t>(hd) * (kFkN + kFpad) + static_cast<size_t>(kFkN) * hd +
+          static_cast<size_t>(kFkN) * (kFqN + kFpad) + 3 * kFqN + kFqN) * 4;
+}
+
 }  // namespace c2s
