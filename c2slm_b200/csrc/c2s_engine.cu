@@ -1229,7 +1229,6 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   // ---- kernels: shared-memory limits, graphs
   CK(cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-  CK(cudaFuncSetAttribute(k_pf_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(k_pf_flash<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pf_flash_smem(128))));
   CK(cudaFuncSetAttribute(k_pf_flash<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pf_flash_smem(64))));
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));

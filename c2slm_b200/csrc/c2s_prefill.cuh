@@ -6,7 +6,8 @@
 // own and its attention is causal.  Here the tokens of a chunk go through
 // each layer together: the K-quant projections become int8 GEMMs of the
 // tokens' Q8_K rows against the weights on tcgen05 (kind::i8, accumulators in
-// TMEM), the rest (norms, RoPE, attention, SwiGLU) runs per token.
+// TMEM); norms, RoPE and SwiGLU run per token, the causal attention as a
+// tiled kernel over the chunk's query vectors.
 //
 // Integer contract of a K-quant row dot (A8/A9): per superblock, Q4_K adds
 //   sum_j d*d8*sc_j*dot_j - dmin*d8*m_j*bsum_j   (j: 8 sub-blocks of 32)
@@ -501,59 +502,6 @@ __global__ void __launch_bounds__(kThreads) k_pf_rope_store(float *q, const floa
     kc[g * head_stride + static_cast<size_t>(pos) * hd + j] = buf[nqh * hd + i];
     vc[g * head_stride + static_cast<size_t>(pos) * hd + j] = v[static_cast<size_t>(t) * ldkv + i];
   }
-}
-
-// Causal attention of token t (position p0 + t) for the query heads of kv
-// group blockIdx.x, over cache rows 0 .. p0 + t (rows already stored and
-// rotated): the decode attention of one split, no RoPE, no store.
-struct PfAttn {
-  const float *q;  // [n][ldq] rotated
-  float *out;      // [n][ldq]
-  float *kc, *vc;  // this layer's planes: group g row p at [g * head_stride + p * hd]
-  size_t head_stride;
-  int ldq, n, p0, n_kv, qpk, n_heads, hd, max_splits;
-  float scale, eps;
-  unsigned *err;
-};
-
-__global__ void __launch_bounds__(kThreads) k_pf_attention(const PfAttn A) {
-  extern __shared__ __align__(128) float asmem[];
-  __shared__ __align__(8) uint64_t bars[kAttnBufs];
-  const int tid = threadIdx.x, g = blockIdx.x, t = blockIdx.y;
-  if (tid == 0) {
-    for (int i = 0; i < kAttnBufs; ++i) mbar_init(&bars[i], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (t >= A.n) return;
-  const int pos = A.p0 + t, hd = A.hd;
-  AttnJob J;
-  J.g = g;
-  J.h0 = g * A.qpk;
-  J.qpk = min(A.qpk, A.n_heads - J.h0);
-  J.store_kv = 0;
-  J.counter = nullptr;
-  J.q = A.q + static_cast<size_t>(t) * A.ldq + static_cast<size_t>(J.h0) * hd;
-  J.k = A.kc + g * A.head_stride + static_cast<size_t>(pos) * hd;
-  J.v = A.vc + g * A.head_stride + static_cast<size_t>(pos) * hd;
-  J.q_norm = J.k_norm = nullptr;
-  J.kc = A.kc + g * A.head_stride;
-  J.vc = A.vc + g * A.head_stride;
-  J.rope_cs = J.rope_sn = nullptr;
-  J.out = A.out + static_cast<size_t>(t) * A.ldq;
-  J.part = nullptr;
-  J.dist = 0;
-  J.s = 0;
-  J.nsplit = 1;
-  J.p0 = 0;
-  J.p1 = pos + 1;
-  J.pos = pos;
-  J.hd = hd;
-  J.max_splits = A.max_splits;
-  J.eps = A.eps;
-  J.scale = A.scale;
-  uint32_t uses[kAttnBufs] = {};
-  attend(J, asmem, bars, uses, A.err);
 }
 
 // SwiGLU in place (internal/simd/c2_tensor_swiglu_nosimd_gen.go:11-19)
