@@ -372,3 +372,29 @@ def test_prefill_on_tensor_cores_matches_token_by_token(model_cache, monkeypatch
     assert np.all(r[:6] <= 1e-5)
     assert np.median(r) <= 1e-5 and np.max(r) <= 1e-2
     assert g1[0] == g0[0]
+
+
+def test_prefill_suffix_and_rewind_match_token_by_token(model_cache, monkeypatch):
+    """IngestFrom of a suffix after an earlier ingest (the chunk attends to the
+    cached prefix) and after a rewind into the prefix: the tensor-core prefill
+    against the per-token path on the same calls."""
+    path = synth.cached_model("qwen15b", layers=2, cache_dir=model_cache)
+    rng = np.random.default_rng(11)
+    a = rng.integers(0, 151643, 200).astype(np.int32)
+    b = rng.integers(0, 151643, 300).astype(np.int32)
+    c = rng.integers(0, 151643, 150).astype(np.int32)
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("C2S_PREFILL", mode)
+        with K.Engine(path, max_tokens=1024) as e:
+            e.ingest_from(0, a)
+            nx_b = e.ingest_from(200, b)          # suffix after the prefix
+            sl_b = e.seq_len
+            nx_c = e.ingest_from(120, c)          # rewinds to 120, then 150 tokens
+            out[mode] = (nx_b, sl_b, nx_c, e.seq_len, e.token_ids()[:e.seq_len].copy(),
+                         e.get_key(0, 1, 121), e.generate(4, stop_on_special=False))
+    t, r = out["1"], out["0"]
+    assert t[1] == r[1] == 500 and t[3] == r[3] == 270 and np.array_equal(t[4], r[4])
+    assert rel(t[0], r[0]) <= TOL and rel(t[2], r[2]) <= TOL
+    assert rel(t[5], r[5]) <= 1e-5  # a layer-0 row the rewound ingest rewrote
+    assert t[6][0] == r[6][0]
