@@ -378,7 +378,18 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
 // ---------------------------------------------------------------------------
 struct PhaseRows {
   int r0[kMaxSegs], r1[kMaxSegs];
+  // packed: the rows of all segments fit one ring slot and travel as one
+  // chunk (one copy per segment, segment s at byte off[s] of the slot)
+  int packed, total;
+  int off[kMaxSegs];
 };
+
+// 16-B aligned byte span [a0, a1) of rows r0 .. r1-1 of a segment
+__device__ __forceinline__ void seg_span(const Seg &S, int r0, int r1, uintptr_t &a0, uintptr_t &a1) {
+  const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(r0) * S.row_bytes;
+  a0 = src & ~uintptr_t(15);
+  a1 = (src + static_cast<uintptr_t>(r1 - r0) * S.row_bytes + 15) & ~uintptr_t(15);
+}
 
 // chunk i of the phase for this CTA: segment, first row, row count, offset
 // of the first row in the CTA's rows of that segment (same enumeration on
@@ -387,18 +398,26 @@ struct PChunk {
   int seg, r0, nr, lr0;
 };
 
-__device__ __forceinline__ int phase_rows(const PPhase &ph, int c, int G, PhaseRows &R) {
-  int n = 0;
+__device__ __forceinline__ int phase_rows(const PPhase &ph, int c, int G, int slot_bytes, PhaseRows &R) {
+  int n = 0, total = 0;
 #pragma unroll
   for (int s = 0; s < kMaxSegs; ++s) {
     R.r0[s] = R.r1[s] = 0;
+    R.off[s] = total;
     if (s < ph.nseg) {
       seg_rows(ph.seg[s].rows, c, G, R.r0[s], R.r1[s]);
       const int cpr = ph.seg[s].rows_per_chunk;
       n += (R.r1[s] - R.r0[s] + cpr - 1) / cpr;
+      if (R.r1[s] > R.r0[s]) {
+        uintptr_t a0, a1;
+        seg_span(ph.seg[s], R.r0[s], R.r1[s], a0, a1);
+        total += static_cast<int>(a1 - a0);
+      }
     }
   }
-  return n;
+  R.total = total;
+  R.packed = (ph.nseg > 1 && n > 1 && total <= slot_bytes) ? 1 : 0;
+  return R.packed ? 1 : n;
 }
 
 __device__ __forceinline__ PChunk phase_chunk(const PPhase &ph, const PhaseRows &R, int i) {
@@ -460,7 +479,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   const LimbsView LV{la, lb, lc, ls, nb};
   const Q8KView q8{q8qs, q8d, q8bs};
   PhaseRows R;
-  const int nchunks = phase_rows(ph, c, G, R);
+  const int nchunks = phase_rows(ph, c, G, P.slot_bytes, R);
   // the attention's split arrivals of this layer: every split has finished
   // waiting on them before the grid barrier this phase follows
   if (ph.kind == K_OPROJ && tid == 0 && c < 64) st->attn_counter[c] = 0;
@@ -620,23 +639,39 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       break;
     }
     if (tr) wait_cyc += clock64() - w0;
-    const PChunk ch = phase_chunk(ph, R, i);
-    const Seg &S = ph.seg[ch.seg];
-    const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
-    const uint8_t *rows = smem + static_cast<size_t>(slot) * P.slot_alloc + (src & 15);
-    const int first = (wig - jbase) & (ws - 1);
-    if (first < ch.nr) {
-      const int cnt = (ch.nr - first + ws - 1) >> lws;
-      float *y = ybuf + ch.seg * P.yrows + ch.lr0;
-      switch (S.type) {
-        case T_Q8_0: warp_rows<T_Q8_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
-        case T_Q5_0: warp_rows<T_Q5_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
-        case T_Q4_K: warp_rows<T_Q4_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
-        case T_Q6_K: warp_rows<T_Q6_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
-        default: break;
+    // the chunk's pieces: every segment of a packed chunk, else one piece
+    const int npiece = R.packed ? ph.nseg : 1;
+    for (int pc = 0; pc < npiece; ++pc) {
+      PChunk ch;
+      int off;
+      if (R.packed) {
+        ch.seg = pc;
+        ch.r0 = R.r0[pc];
+        ch.nr = R.r1[pc] - R.r0[pc];
+        ch.lr0 = 0;
+        off = R.off[pc];
+      } else {
+        ch = phase_chunk(ph, R, i);
+        off = 0;
       }
+      if (ch.nr <= 0) continue;
+      const Seg &S = ph.seg[ch.seg];
+      const uintptr_t src = reinterpret_cast<uintptr_t>(S.w) + static_cast<uintptr_t>(ch.r0) * S.row_bytes;
+      const uint8_t *rows = smem + static_cast<size_t>(slot) * P.slot_alloc + off + (src & 15);
+      const int first = (wig - jbase) & (ws - 1);
+      if (first < ch.nr) {
+        const int cnt = (ch.nr - first + ws - 1) >> lws;
+        float *y = ybuf + ch.seg * P.yrows + ch.lr0;
+        switch (S.type) {
+          case T_Q8_0: warp_rows<T_Q8_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+          case T_Q5_0: warp_rows<T_Q5_0>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+          case T_Q4_K: warp_rows<T_Q4_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+          case T_Q6_K: warp_rows<T_Q6_K>(rows, S.row_bytes, S.units, first, cnt, LV, q8, y, ws); break;
+          default: break;
+        }
+      }
+      jbase += ch.nr;
     }
-    jbase += ch.nr;
     __syncwarp();
     if (lane == 0) mbar_arrive_n(&empty[slot], static_cast<uint32_t>(ng));
   }
@@ -881,7 +916,7 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
         const PPhase &ph = s_pph;
         if (ph.kind == K_ATTN) continue;
         PhaseRows R;
-        const int nch = phase_rows(ph, c, G, R);
+        const int nch = phase_rows(ph, c, G, P.slot_bytes, R);
         for (int i = 0; i < nch; ++i, ++k) {
           const int slot = static_cast<int>(k % static_cast<uint32_t>(P.nslot));
           const uint32_t use = k / static_cast<uint32_t>(P.nslot);
@@ -900,8 +935,20 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
             }
             if (stopped) break;
           }
-          const PChunk ch = phase_chunk(ph, R, i);
-          issue_chunk_rows(ph.seg[ch.seg], ch, smem + static_cast<size_t>(slot) * P.slot_alloc, &full[slot]);
+          uint8_t *dst = smem + static_cast<size_t>(slot) * P.slot_alloc;
+          if (R.packed) {  // every segment's rows into the one slot
+            mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(R.total));
+#pragma unroll
+            for (int sg = 0; sg < kMaxSegs; ++sg)
+              if (sg < ph.nseg && R.r1[sg] > R.r0[sg]) {
+                uintptr_t a0, a1;
+                seg_span(ph.seg[sg], R.r0[sg], R.r1[sg], a0, a1);
+                bulk_g2s(dst + R.off[sg], reinterpret_cast<const void *>(a0), static_cast<uint32_t>(a1 - a0), &full[slot]);
+              }
+          } else {
+            const PChunk ch = phase_chunk(ph, R, i);
+            issue_chunk_rows(ph.seg[ch.seg], ch, dst, &full[slot]);
+          }
         }
       }
     }
