@@ -998,6 +998,7 @@ int persistent_setup(c2s_engine *e) {
   P.token_ids = e->token_ids;
   P.out_tokens = e->out_tokens;
   P.gbar = e->gbar;
+  P.ll = tp ? 1 : 0;  // one GPU: grid barriers and X (tagged words measured slower there)
   CK(cudaFuncSetAttribute(k_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(e->p_smem)));
   int blocks = 0;
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_persistent, kPThreads, e->p_smem));
@@ -1313,6 +1314,7 @@ int tp_exchange_setup(c2s_engine *e) {
     e->peer_shared[k] = static_cast<uint8_t *>(p);
   }
   PParams &P = e->pp;
+  P.ll = 1;
   P.xbuf = e->xbuf;
   P.recv = reinterpret_cast<const unsigned long long *>(e->tp_shared);
   P.argbuf = reinterpret_cast<const unsigned long long *>(e->tp_shared + off_arg);

@@ -81,6 +81,10 @@ struct PParams {
   // The next normed phase adds the received partials to the residual
   // xbuf[2][H] (each CTA stores its share of the new residual).
   int world, rank, qpk, tp_h0, tp_h1, tp_g0, tp_v0;
+  // 1: o-proj / down hand their output rows to the next phase as tagged words
+  // instead of a grid barrier and X (the tensor-parallel exchange; on one GPU
+  // the barrier is faster)
+  int ll;
   float *xbuf;
   const unsigned long long *recv, *argbuf;
   unsigned long long *peer_recv[8], *peer_arg[8];
@@ -487,8 +491,8 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   const bool normed = ph.kind == K_QKV || ph.kind == K_FFN_UP || ph.kind == K_LOGITS;
   // ---- loads the epilogue needs, requested first
   float xres = 0.f, bias[kMaxSegs] = {0.f, 0.f, 0.f};
-  const bool tp = P.world > 1;
-  if (residual && !tp && R.r0[0] + tid < R.r1[0]) xres = __ldcg(P.X + R.r0[0] + tid);
+  const bool tp = P.world > 1, ll = P.ll != 0;
+  if (residual && !ll && R.r0[0] + tid < R.r1[0]) xres = __ldcg(P.X + R.r0[0] + tid);
 #pragma unroll
   for (int s = 0; s < kMaxSegs; ++s)
     if (s < ph.nseg && ph.seg[s].bias && R.r0[s] + tid < R.r1[s]) bias[s] = __ldg(ph.seg[s].bias + R.r0[s] + tid);
@@ -526,7 +530,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     // The first phase of a launch reads the residual the per-phase kernels
     // left in X (from_X).
     const int par = ph.kind == K_FFN_UP ? 0 : 1;
-    const bool reduce = tp && !embed && !from_X;
+    const bool reduce = ll && !embed && !from_X;
     const float4 *xs4 = reduce ? reinterpret_cast<const float4 *>(P.xbuf + static_cast<size_t>(par) * P.H) : x4;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -550,7 +554,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       }
       if (!got) *reinterpret_cast<volatile int *>(&s_fail) = 1;
     }
-    if (tp && (embed || reduce)) {  // this CTA's share of the new residual (logits: back in X)
+    if (ll && (embed || reduce)) {  // this CTA's share of the new residual (logits: back in X)
       float4 *xd = ph.kind == K_LOGITS ? reinterpret_cast<float4 *>(P.X)
                                        : reinterpret_cast<float4 *>(P.xbuf + static_cast<size_t>(embed ? 0 : 1 - par) * P.H);
       const int a = static_cast<int>((static_cast<unsigned>(c) * n4) / G);
@@ -690,7 +694,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       if (s < ph.nseg && R.r0[s] + tid < R.r1[s])
         ph.seg[s].out[R.r0[s] + tid] = __fadd_rn(ybuf[s * P.yrows + tid], bias[s]);
   } else if (residual) {
-    if (tp) {  // partial rows to every rank, tagged as exchange xb + 1 (summed by the next normed phase)
+    if (ll) {  // partial rows to every rank, tagged as exchange xb + 1 (summed by the next normed phase)
       const int par = ph.kind == K_OPROJ ? 0 : 1;
       if (R.r0[0] + tid < R.r1[0]) {
         const uint32_t v = __float_as_uint(ybuf[tid]);
@@ -1027,14 +1031,14 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
       // tensor parallel: o-proj / down sent exchange xb + 1; the next phase
       // polls its tagged words instead of waiting at a grid barrier (except
       // logits, which reads the state the down phase committed)
-      if (P.world > 1 && (ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN)) {
+      if (P.ll && (ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN)) {
         xb += 1;
         crossed = true;
       }
       last_kind = ph.kind;
     }
   }
-  if (P.world > 1 && ok && last_kind == K_FFN_DOWN) {
+  if (P.ll && ok && last_kind == K_FFN_DOWN) {
     // the launch ends after a forward: leave its residual in X for the
     // per-phase kernels and the next launch (X = xbuf[1] + the down partials)
     const int n4 = P.H / 4;
