@@ -459,6 +459,9 @@ struct c2s_engine {
   int *pf_tok = nullptr;
   int16_t *pf_bs = nullptr;   // tokens' Q8_K sub-block sums
   uint8_t *pf_planes = nullptr;  // every layer projection's digit planes and row tables
+  float *pf_fpart = nullptr;     // attention split partials (PfFlash::part)
+  unsigned *pf_fcount = nullptr; // attention split arrivals (PfFlash::count)
+  int pf_fsplit = 0, pf_fns = 0; // keys per attention split, most splits of a block
   std::vector<std::array<const uint8_t *, 7>> pf_pl;  // per layer: q, k, v, o, gate, up, down
   std::vector<std::array<const uint4 *, 7>> pf_ri;
   DevState *h_st = nullptr;
@@ -920,6 +923,10 @@ int persistent_setup(c2s_engine *e) {
   nslot = std::min(nslot, 8);
   if (nslot < 2) return fail(C2S_ERR_UNSUPPORTED, "persistent decode: activation set too large for shared memory");
   P.nslot = nslot;
+  // warp groups of the many-row phases: each group holds one slot while it
+  // computes, so fewer groups than slots leave slots to fill meanwhile
+  P.lng = nslot >= 8 ? 3 : nslot >= 4 ? 2 : nslot >= 2 ? 1 : 0;
+  if (const char *lg = getenv("C2S_LNG")) P.lng = std::max(0, std::min(3, atoi(lg)));
   P.slot_bytes = static_cast<int>(slot_bytes);
   P.slot_alloc = static_cast<int>(slot_bytes + 64);
   size_t off = static_cast<size_t>(nslot) * P.slot_alloc;
@@ -1422,7 +1429,8 @@ void engine_free(c2s_engine *e) {
   for (void *p : {static_cast<void *>(e->pf_x), static_cast<void *>(e->pf_q), static_cast<void *>(e->pf_k),
                   static_cast<void *>(e->pf_v), static_cast<void *>(e->pf_att), static_cast<void *>(e->pf_g),
                   static_cast<void *>(e->pf_u), static_cast<void *>(e->pf_d8), static_cast<void *>(e->pf_q8),
-                  static_cast<void *>(e->pf_tok), static_cast<void *>(e->pf_planes), static_cast<void *>(e->pf_bs)})
+                  static_cast<void *>(e->pf_tok), static_cast<void *>(e->pf_planes), static_cast<void *>(e->pf_bs),
+                  static_cast<void *>(e->pf_fpart), static_cast<void *>(e->pf_fcount)})
     if (p) cudaFree(p);
   for (int k = 0; k < 8; ++k)
     if (e->peer_shared[k] && e->peer_shared[k] != e->tp_shared) cudaIpcCloseMemHandle(e->peer_shared[k]);
@@ -1831,6 +1839,19 @@ static int pf_alloc(c2s_engine *e) {
       (rc = al(reinterpret_cast<void **>(&e->pf_q8), c * kmax)) || (rc = al(reinterpret_cast<void **>(&e->pf_tok), c * 4)) ||
       (rc = al(reinterpret_cast<void **>(&e->pf_bs), c * (kmax / 256) * 16)))
     return rc;
+  // attention splits: keys of a query block in splits of pf_fsplit (a
+  // multiple of the 64-key tile), at most 16 per block at max_tokens
+  {
+    const int mt = d.max_tokens, hd = d.head_dim;
+    e->pf_fsplit = std::max(512, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
+    e->pf_fns = (mt + e->pf_fsplit - 1) / e->pf_fsplit;
+    const size_t nblk = (c * (d.n_heads / d.n_kv_heads) + kFqN - 1) / kFqN;
+    const size_t blocks = static_cast<size_t>(d.n_kv_heads) * nblk;
+    if ((rc = al(reinterpret_cast<void **>(&e->pf_fpart), blocks * e->pf_fns * kFqN * (hd + 2) * 4)) ||
+        (rc = al(reinterpret_cast<void **>(&e->pf_fcount), blocks * 4)))
+      return rc;
+    CK(cudaMemsetAsync(e->pf_fcount, 0, blocks * 4, e->stream));
+  }
   // the digit planes of every layer projection, converted once
   auto plane_bytes = [](int, int rows, int cols) {
     return static_cast<size_t>((rows + kPfM - 1) / kPfM) * (cols / 256) * 2 * kPfPlane;
@@ -1940,7 +1961,11 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     A.qpk = qpk;
     A.n_heads = nqh;
     A.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
-    const dim3 fgrid(nkv, (n * qpk + kFqN - 1) / kFqN);
+    A.part = e->pf_fpart;
+    A.count = e->pf_fcount;
+    A.split_keys = e->pf_fsplit;
+    A.max_splits = e->pf_fns;
+    const dim3 fgrid(nkv, (n * qpk + kFqN - 1) / kFqN, (p0 + n + e->pf_fsplit - 1) / e->pf_fsplit);
     if (hd == 128)
       k_pf_flash<128><<<fgrid, kThreads, pf_flash_smem(128), s>>>(A);
     else

@@ -49,6 +49,7 @@ struct PParams {
   int qrows, vrows;                        // this rank's attn_q rows and vocabulary rows
   int nphase, n_steps;
   int nslot;
+  int lng;  // phases with many rows per CTA: the compute warps form 2^lng groups (kWarps >> lng warps each)
   int off_full, off_empty, off_abar, off_act;
   int off_xn, off_limbs, off_q8, off_y, yrows;  // relative to off_act
   int slot_bytes, slot_alloc;  // weight ring: payload per slot, slot stride
@@ -628,7 +629,7 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   int my_rows = 0;
 #pragma unroll
   for (int s = 0; s < kMaxSegs; ++s) my_rows += R.r1[s] - R.r0[s];
-  const int lng = (nchunks >= P.nslot && my_rows >= 16 * kWarps) ? (P.nslot >= 8 ? 3 : P.nslot >= 4 ? 2 : P.nslot >= 2 ? 1 : 0) : 0;
+  const int lng = (nchunks >= P.nslot && my_rows >= 16 * kWarps) ? P.lng : 0;
   const int ng = 1 << lng, lws = 3 - lng, ws = kWarps >> lng;  // kWarps = 8
   const int grp = warp >> lws, wig = warp & (ws - 1);
   static_assert(kWarps == 8, "warp groups assume 8 compute warps");

@@ -527,14 +527,21 @@ __global__ void k_pf_commit(DevState *st, int *token_ids, const int *tok, int n,
 
 // ---------------------------------------------------------------------------
 // Causal attention of a prefill chunk, tiled: CTA (kv group g, block of 64
-// query vectors v = token * qpk + head of the group's heads).  Key tiles of
-// 64 positions are staged once per CTA (K transposed), then
+// query vectors v = token * qpk + head of the group's heads, key split s; the
+// blocks of the latest tokens, which see the most keys, are scheduled first).
+// A block's keys 0 .. kend-1 are cut into splits of split_keys (a multiple of
+// the 64-key tile) so that the grid's CTAs carry similar work.  Key tiles of
+// 64 positions are staged once per CTA (K transposed; the next tile's loads
+// are in flight in registers while the current one is computed), then
 //   S = Q K^T * scale   (4 queries x 4 keys per thread, f32)
 //   online softmax per query (exp in float64 as tensor.Softmax,
 //                        tensor/ops.go:317-339; keys past the query's position
 //                        excluded)
 //   O = O * alpha + P V (4 queries x 8 dims per thread)
 // and O / l at the end (engine/forward.go:143-155 per head and position).
+// A block of one split writes O / l; otherwise each split writes its
+// (m, l, O) and the last split of the block to arrive combines them in split
+// order (weights exp(m_s - max m) in float64) and clears the block's counter.
 // ---------------------------------------------------------------------------
 struct PfFlash {
   const float *q;        // [n][ldq] rotated queries
@@ -543,6 +550,9 @@ struct PfFlash {
   size_t head_stride;
   int ldq, n, p0, qpk, n_heads;
   float scale;
+  float *part;           // [group][block][max_splits][kFqN][hd + 2]: (m, l, O) of a split
+  unsigned *count;       // [group][block]: arrivals of the block's splits (0 between launches)
+  int split_keys, max_splits;
 };
 
 constexpr int kFqN = 64, kFkN = 64, kFpad = 4;
@@ -557,8 +567,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   float *s_m = Pt + kFkN * (kFqN + kFpad), *s_l = s_m + kFqN, *s_alpha = s_l + kFqN;
   int *s_lim = reinterpret_cast<int *>(s_alpha + kFqN);  // last key position of each query
   const int tid = threadIdx.x, g = blockIdx.x;
-  const int nv = A.n * A.qpk, v0 = blockIdx.y * kFqN;
+  const int nblk = gridDim.y, blk = nblk - 1 - blockIdx.y, sp = blockIdx.z;
+  const int nv = A.n * A.qpk, v0 = blk * kFqN;
   if (v0 >= nv) return;
+  {
+    const int kend0 = A.p0 + (min(nv, v0 + kFqN) - 1) / A.qpk + 1;
+    if (sp * A.split_keys >= kend0) return;  // this block has fewer splits
+  }
   const int h0 = g * A.qpk;
   // ---- queries of the block, transposed; their causal limits
   for (int i = tid; i < kFqN * (HD / 4); i += kThreads) {  // a warp: 32 queries, one d4 (conflict-free)
@@ -580,7 +595,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     s_l[tid] = 0.f;
   }
   const int vlast = min(nv, v0 + kFqN) - 1;
-  const int kend = A.p0 + vlast / A.qpk + 1;  // keys 0 .. kend-1
+  const int kall = A.p0 + vlast / A.qpk + 1;  // the block's keys 0 .. kall-1
+  const int nsplit = (kall + A.split_keys - 1) / A.split_keys;
+  const int kbeg = sp * A.split_keys, kend = min(kall, kbeg + A.split_keys);  // this split's keys
   // thread tiles
   const int sq = (tid >> 4) * 4, sk = (tid & 15) * 4;  // S: 4 queries x 4 keys
   const int oq = (tid >> 4) * 4, od = (tid & 15) * (HD / 16);  // O: 4 queries x HD/16 dims
@@ -591,27 +608,42 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
 #pragma unroll
     for (int b = 0; b < OD; ++b) o[a][b] = 0.f;
   const float *kg = A.kc + g * A.head_stride, *vg = A.vc + g * A.head_stride;
-  for (int kb = 0; kb < kend; kb += kFkN) {
+  // tile loads: NL float4 of K and of V per thread; K element i = (key i %
+  // kFkN, d4 (i / kFkN) * 4) so that a warp's transposed stores cover 32 keys
+  // of one d4 (conflict-free); V element i = (key i / (HD/4), d4 (i % (HD/4)) * 4)
+  constexpr int NL = kFkN * (HD / 4) / kThreads;
+  static_assert(NL * kThreads == kFkN * (HD / 4), "tile loads");
+  float4 kx[NL], vx[NL];
+  auto fetch = [&](int kb) {
+    const int nk = min(kFkN, kend - kb);
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int i = tid + j * kThreads;
+      const int kr = i % kFkN, d4 = (i / kFkN) * 4;
+      kx[j] = kr < nk ? __ldcg(reinterpret_cast<const float4 *>(kg + static_cast<size_t>(kb + kr) * HD + d4))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int vr = i / (HD / 4), v4 = (i % (HD / 4)) * 4;
+      vx[j] = vr < nk ? __ldcg(reinterpret_cast<const float4 *>(vg + static_cast<size_t>(kb + vr) * HD + v4))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  fetch(kbeg);  // kend > kbeg
+  for (int kb = kbeg; kb < kend; kb += kFkN) {
     const int nk = min(kFkN, kend - kb);
     __syncthreads();  // previous tile fully consumed
-    for (int i = tid; i < kFkN * (HD / 4); i += kThreads) {
-      {  // K transposed: a warp covers 32 keys of one d4 (conflict-free stores)
-        const int kr = i % kFkN, d4 = (i / kFkN) * 4;
-        float4 kx = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (kr < nk) kx = __ldcg(reinterpret_cast<const float4 *>(kg + static_cast<size_t>(kb + kr) * HD + d4));
-        Kt[(d4 + 0) * (kFkN + kFpad) + kr] = kx.x;
-        Kt[(d4 + 1) * (kFkN + kFpad) + kr] = kx.y;
-        Kt[(d4 + 2) * (kFkN + kFpad) + kr] = kx.z;
-        Kt[(d4 + 3) * (kFkN + kFpad) + kr] = kx.w;
-      }
-      {  // V as rows
-        const int kr = i / (HD / 4), d4 = (i % (HD / 4)) * 4;
-        float4 vx = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (kr < nk) vx = __ldcg(reinterpret_cast<const float4 *>(vg + static_cast<size_t>(kb + kr) * HD + d4));
-        *reinterpret_cast<float4 *>(Vs + kr * HD + d4) = vx;
-      }
+#pragma unroll
+    for (int j = 0; j < NL; ++j) {
+      const int i = tid + j * kThreads;
+      const int kr = i % kFkN, d4 = (i / kFkN) * 4;
+      Kt[(d4 + 0) * (kFkN + kFpad) + kr] = kx[j].x;
+      Kt[(d4 + 1) * (kFkN + kFpad) + kr] = kx[j].y;
+      Kt[(d4 + 2) * (kFkN + kFpad) + kr] = kx[j].z;
+      Kt[(d4 + 3) * (kFkN + kFpad) + kr] = kx[j].w;
+      const int vr = i / (HD / 4), v4 = (i % (HD / 4)) * 4;
+      *reinterpret_cast<float4 *>(Vs + vr * HD + v4) = vx[j];
     }
     __syncthreads();
+    if (kb + kFkN < kend) fetch(kb + kFkN);  // lands while this tile is computed
     // ---- S = Q K^T for the thread's 4 x 4 tile
     float sacc[4][4];
 #pragma unroll
@@ -650,8 +682,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       const float m_old = s_m[qi], m_new = fmaxf(m_old, mx);
       float ls = 0.f;
-#pragma unroll 1
-      for (int j = 0; j < 16; ++j) {
+#pragma unroll 4
+      for (int j = 0; j < 16; ++j) {  // four exponentials in flight
         float *pp = Pt + (part * 16 + j) * (kFqN + kFpad) + qi;
         const float sv = *pp;
         const float e = sv == -INFINITY ? 0.f : static_cast<float>(exp(static_cast<double>(__fsub_rn(sv, m_new))));
@@ -695,16 +727,70 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     }
   }
   __syncthreads();
+  if (nsplit == 1) {
 #pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    const int v = v0 + oq + a;
-    if (v < nv) {
-      const int t = v / A.qpk, h = v - t * A.qpk;
-      const float l = s_l[oq + a];
-      float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + od;
+    for (int a = 0; a < 4; ++a) {
+      const int v = v0 + oq + a;
+      if (v < nv) {
+        const int t = v / A.qpk, h = v - t * A.qpk;
+        const float l = s_l[oq + a];
+        float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + od;
 #pragma unroll
-      for (int b = 0; b < OD; ++b) dst[b] = o[a][b] / l;
+        for (int b = 0; b < OD; ++b) dst[b] = o[a][b] / l;
+      }
     }
+    return;
+  }
+  // ---- partial (m, l, O) of this split; the block's last split combines
+  constexpr int PW = HD + 2;
+  float *pblk = A.part + (static_cast<size_t>(g) * nblk + blk) * A.max_splits * kFqN * PW;
+  {
+    float *pp = pblk + static_cast<size_t>(sp) * kFqN * PW;
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < OD; ++b) pp[(oq + a) * PW + 2 + od + b] = o[a][b];
+    if (tid < kFqN) {
+      pp[tid * PW] = s_m[tid];
+      pp[tid * PW + 1] = s_l[tid];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  int *s_last = s_lim;  // the causal limits are no longer needed
+  if (tid == 0) {
+    unsigned *cnt = A.count + static_cast<size_t>(g) * nblk + blk;
+    const unsigned prev = atomicAdd(cnt, 1u);
+    const int last = prev == static_cast<unsigned>(nsplit - 1) ? 1 : 0;
+    if (last) *cnt = 0u;  // for the next launch (every split of this one has arrived)
+    *s_last = last;
+  }
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  // weights of the splits for each query: w_s = exp(m_s - M) (float64), over s in order
+  float *s_w = Pt;  // [max_splits][kFqN]
+  if (tid < kFqN) {
+    float M = -INFINITY;
+    for (int j = 0; j < nsplit; ++j) M = fmaxf(M, __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW));
+    float L = 0.f;
+    for (int j = 0; j < nsplit; ++j) {
+      const float mj = __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW);
+      const float w = mj == -INFINITY ? 0.f : static_cast<float>(exp(static_cast<double>(__fsub_rn(mj, M))));
+      s_w[j * kFqN + tid] = w;
+      L = __fadd_rn(L, __fmul_rn(w, __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW + 1)));
+    }
+    s_l[tid] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < kFqN * HD; i += kThreads) {
+    const int qi = i / HD, dd = i - qi * HD, v = v0 + qi;
+    if (v >= nv) continue;
+    float acc = 0.f;
+    for (int j = 0; j < nsplit; ++j)
+      acc = __fadd_rn(acc, __fmul_rn(s_w[j * kFqN + qi], __ldcg(pblk + (static_cast<size_t>(j) * kFqN + qi) * PW + 2 + dd)));
+    const int t = v / A.qpk, h = v - t * A.qpk;
+    A.out[static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + dd] = acc / s_l[qi];
   }
 }
 
