@@ -1840,10 +1840,10 @@ static int pf_alloc(c2s_engine *e) {
       (rc = al(reinterpret_cast<void **>(&e->pf_bs), c * (kmax / 256) * 16)))
     return rc;
   // attention splits: keys of a query block in splits of pf_fsplit (a
-  // multiple of the 64-key tile), at most 16 per block at max_tokens
+  // multiple of the key tile), at most 16 per block at max_tokens
   {
     const int mt = d.max_tokens, hd = d.head_dim;
-    e->pf_fsplit = std::max(512, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
+    e->pf_fsplit = std::max(2 * kFkN, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
     e->pf_fns = (mt + e->pf_fsplit - 1) / e->pf_fsplit;
     const size_t nblk = (c * (d.n_heads / d.n_kv_heads) + kFqN - 1) / kFqN;
     const size_t blocks = static_cast<size_t>(d.n_kv_heads) * nblk;

@@ -344,7 +344,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfGemm G) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int tk = 64 * th + c0 + i;
-          const float d8 = sd8[tk];
+          // token scales four at a time (one broadcast load)
+          const float4 d84 = *reinterpret_cast<const float4 *>(sd8 + (tk & ~3));
+          const float d8i = (i & 3) == 0 ? d84.x : (i & 3) == 1 ? d84.y : (i & 3) == 2 ? d84.z : d84.w;
           const int isum = static_cast<int>(hi[i]) * 128 + static_cast<int>(lo[i]);
           if constexpr (TYPE == T_Q4_K) {
             const uint4 b = sbs[tk];  // sub-block sums 0..7 as int16 pairs
@@ -352,11 +354,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfGemm G) {
             msum = __dp2a_hi(static_cast<int>(b.y), static_cast<int>(rv.z), msum);
             msum = __dp2a_lo(static_cast<int>(b.z), static_cast<int>(rv.w), msum);
             msum = __dp2a_hi(static_cast<int>(b.w), static_cast<int>(rv.w), msum);
-            const float t = __fsub_rn(__fmul_rn(static_cast<float>(isum), __fmul_rn(dr, d8)),
-                                      __fmul_rn(static_cast<float>(msum), __fmul_rn(dmr, d8)));
-            acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
+            // d8 (d isum - dmin msum): the integer dots are exact; the float
+            // terms are those of the per-token matvec, associated differently
+            const float u = fmaf(dr, static_cast<float>(isum), -__fmul_rn(dmr, static_cast<float>(msum)));
+            acc[c0 + i] = fmaf(d8i, u, acc[c0 + i]);
           } else {
-            acc[c0 + i] = __fadd_rn(acc[c0 + i], __fmul_rn(static_cast<float>(isum), __fmul_rn(dr, d8)));
+            acc[c0 + i] = fmaf(__fmul_rn(dr, d8i), static_cast<float>(isum), acc[c0 + i]);
           }
         }
       }
@@ -526,19 +529,21 @@ __global__ void k_pf_commit(DevState *st, int *token_ids, const int *tok, int n,
 }
 
 // ---------------------------------------------------------------------------
-// Causal attention of a prefill chunk, tiled: CTA (kv group g, block of 64
+// Causal attention of a prefill chunk, tiled: CTA (kv group g, block of 128
 // query vectors v = token * qpk + head of the group's heads, key split s; the
 // blocks of the latest tokens, which see the most keys, are scheduled first).
-// A block's keys 0 .. kend-1 are cut into splits of split_keys (a multiple of
-// the 64-key tile) so that the grid's CTAs carry similar work.  Key tiles of
-// 64 positions are staged once per CTA (K transposed; the next tile's loads
-// are in flight in registers while the current one is computed), then
-//   S = Q K^T * scale   (4 queries x 4 keys per thread, f32)
+// A block's keys 0 .. kall-1 are cut into splits of split_keys (a multiple
+// of the 128-key tile) so that the grid's CTAs carry similar work.  Per key
+// tile (K transposed and V staged in shared memory):
+//   S = Q K^T * scale   (8 queries x 8 keys per thread, f32)
 //   online softmax per query (exp in float64 as tensor.Softmax,
 //                        tensor/ops.go:317-339; keys past the query's position
 //                        excluded)
-//   O = O * alpha + P V (4 queries x 8 dims per thread)
+//   O = O * alpha + P V (8 queries x HD/16 dims per thread)
 // and O / l at the end (engine/forward.go:143-155 per head and position).
+// Shared-memory loads move 16 B per lane and cost one wavefront per 8 lanes
+// whether or not lanes share an address, so the 8 x 8 register tiles (4 FMA
+// per loaded float) are what keeps the FMA pipe, not shared memory, the bound.
 // A block of one split writes O / l; otherwise each split writes its
 // (m, l, O) and the last split of the block to arrive combines them in split
 // order (weights exp(m_s - max m) in float64) and clears the block's counter.
@@ -555,28 +560,40 @@ struct PfFlash {
   int split_keys, max_splits;
 };
 
-constexpr int kFqN = 64, kFkN = 64, kFpad = 4;
+constexpr int kFqN = 128, kFkN = 128;
+// probabilities [key][query], rows of kFqN + 16 floats: the S tile stores
+// (8 lanes on 32 consecutive queries) and the softmax reads (lane = query +
+// 16 x key parity) are conflict-free
+constexpr int kFps = kFqN + 16;
+
+// shared memory of k_pf_flash<HD>, in floats: Qt [HD][kFqN] | Kt [HD][kFkN]
+// sharing its space with Pt [kFkN][kFps] | Vs [kFkN][HD] | s_m, s_l,
+// s_alpha, s_lim [kFqN]
+__host__ __device__ constexpr int pf_flash_kp(int hd) { return hd * kFkN > kFkN * kFps ? hd * kFkN : kFkN * kFps; }
+__host__ __device__ constexpr size_t pf_flash_smem(int hd) {
+  return (static_cast<size_t>(hd) * kFqN + pf_flash_kp(hd) + static_cast<size_t>(kFkN) * hd + 4 * kFqN) * 4;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   extern __shared__ __align__(16) float fsm[];
-  float *Qt = fsm;                        // [HD][kFqN]
-  float *Kt = Qt + HD * kFqN;             // [HD][kFkN + pad]
-  float *Vs = Kt + HD * (kFkN + kFpad);   // [kFkN][HD]
-  float *Pt = Vs + kFkN * HD;             // [kFkN][kFqN + pad] probabilities, key-major
-  float *s_m = Pt + kFkN * (kFqN + kFpad), *s_l = s_m + kFqN, *s_alpha = s_l + kFqN;
+  float *Qt = fsm;                         // [HD][kFqN]
+  float *Kt = Qt + HD * kFqN, *Pt = Kt;    // [HD][kFkN], then [kFkN][kFps]
+  float *Vs = Kt + pf_flash_kp(HD);        // [kFkN][HD]
+  float *s_m = Vs + kFkN * HD, *s_l = s_m + kFqN, *s_alpha = s_l + kFqN;
   int *s_lim = reinterpret_cast<int *>(s_alpha + kFqN);  // last key position of each query
   const int tid = threadIdx.x, g = blockIdx.x;
   const int nblk = gridDim.y, blk = nblk - 1 - blockIdx.y, sp = blockIdx.z;
   const int nv = A.n * A.qpk, v0 = blk * kFqN;
   if (v0 >= nv) return;
-  {
-    const int kend0 = A.p0 + (min(nv, v0 + kFqN) - 1) / A.qpk + 1;
-    if (sp * A.split_keys >= kend0) return;  // this block has fewer splits
-  }
+  const int vlast = min(nv, v0 + kFqN) - 1;
+  const int kall = A.p0 + vlast / A.qpk + 1;  // the block's keys 0 .. kall-1
+  const int nsplit = (kall + A.split_keys - 1) / A.split_keys;
+  if (sp >= nsplit) return;  // this block has fewer splits
+  const int kbeg = sp * A.split_keys, kend = min(kall, kbeg + A.split_keys);  // this split's keys
   const int h0 = g * A.qpk;
-  // ---- queries of the block, transposed; their causal limits
-  for (int i = tid; i < kFqN * (HD / 4); i += kThreads) {  // a warp: 32 queries, one d4 (conflict-free)
+  // ---- queries of the block, transposed (a warp: 32 queries of one d4); causal limits
+  for (int i = tid; i < kFqN * (HD / 4); i += kThreads) {
     const int qi = i % kFqN, d4 = (i / kFqN) * 4, v = v0 + qi;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (v < nv) {
@@ -594,104 +611,92 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     s_m[tid] = -INFINITY;
     s_l[tid] = 0.f;
   }
-  const int vlast = min(nv, v0 + kFqN) - 1;
-  const int kall = A.p0 + vlast / A.qpk + 1;  // the block's keys 0 .. kall-1
-  const int nsplit = (kall + A.split_keys - 1) / A.split_keys;
-  const int kbeg = sp * A.split_keys, kend = min(kall, kbeg + A.split_keys);  // this split's keys
-  // thread tiles
-  const int sq = (tid >> 4) * 4, sk = (tid & 15) * 4;  // S: 4 queries x 4 keys
-  const int oq = (tid >> 4) * 4, od = (tid & 15) * (HD / 16);  // O: 4 queries x HD/16 dims
+  // thread tiles: queries tq*4 + e and 64 + tq*4 + e (S and O); keys tk*4 + e
+  // and 64 + tk*4 + e (S); dims tk*4 + 64 c + e (O)
+  const int tq = tid & 15, tk = tid >> 4;
   constexpr int OD = HD / 16;
-  float o[4][OD];
+  auto qof = [&](int a) { return (a < 4 ? 0 : 64) + tq * 4 + (a & 3); };
+  auto dof = [&](int b) { return tk * 4 + 16 * (b & ~3) + (b & 3); };
+  float o[8][OD];
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int a = 0; a < 8; ++a)
 #pragma unroll
     for (int b = 0; b < OD; ++b) o[a][b] = 0.f;
   const float *kg = A.kc + g * A.head_stride, *vg = A.vc + g * A.head_stride;
-  // tile loads: NL float4 of K and of V per thread; K element i = (key i %
-  // kFkN, d4 (i / kFkN) * 4) so that a warp's transposed stores cover 32 keys
-  // of one d4 (conflict-free); V element i = (key i / (HD/4), d4 (i % (HD/4)) * 4)
-  constexpr int NL = kFkN * (HD / 4) / kThreads;
-  static_assert(NL * kThreads == kFkN * (HD / 4), "tile loads");
-  float4 kx[NL], vx[NL];
-  auto fetch = [&](int kb) {
-    const int nk = min(kFkN, kend - kb);
-#pragma unroll
-    for (int j = 0; j < NL; ++j) {
-      const int i = tid + j * kThreads;
-      const int kr = i % kFkN, d4 = (i / kFkN) * 4;
-      kx[j] = kr < nk ? __ldcg(reinterpret_cast<const float4 *>(kg + static_cast<size_t>(kb + kr) * HD + d4))
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-      const int vr = i / (HD / 4), v4 = (i % (HD / 4)) * 4;
-      vx[j] = vr < nk ? __ldcg(reinterpret_cast<const float4 *>(vg + static_cast<size_t>(kb + vr) * HD + v4))
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-  };
-  fetch(kbeg);  // kend > kbeg
   for (int kb = kbeg; kb < kend; kb += kFkN) {
     const int nk = min(kFkN, kend - kb);
-    __syncthreads();  // previous tile fully consumed
-#pragma unroll
-    for (int j = 0; j < NL; ++j) {
-      const int i = tid + j * kThreads;
-      const int kr = i % kFkN, d4 = (i / kFkN) * 4;
-      Kt[(d4 + 0) * (kFkN + kFpad) + kr] = kx[j].x;
-      Kt[(d4 + 1) * (kFkN + kFpad) + kr] = kx[j].y;
-      Kt[(d4 + 2) * (kFkN + kFpad) + kr] = kx[j].z;
-      Kt[(d4 + 3) * (kFkN + kFpad) + kr] = kx[j].w;
-      const int vr = i / (HD / 4), v4 = (i % (HD / 4)) * 4;
-      *reinterpret_cast<float4 *>(Vs + vr * HD + v4) = vx[j];
+    __syncthreads();  // Pt and Vs of the previous tile consumed
+    for (int i = tid; i < kFkN * (HD / 4); i += kThreads) {
+      {  // K transposed: a warp covers 32 keys of one d4 (conflict-free stores)
+        const int kr = i % kFkN, d4 = (i / kFkN) * 4;
+        float4 kx = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kr < nk) kx = __ldcg(reinterpret_cast<const float4 *>(kg + static_cast<size_t>(kb + kr) * HD + d4));
+        Kt[(d4 + 0) * kFkN + kr] = kx.x;
+        Kt[(d4 + 1) * kFkN + kr] = kx.y;
+        Kt[(d4 + 2) * kFkN + kr] = kx.z;
+        Kt[(d4 + 3) * kFkN + kr] = kx.w;
+      }
+      {  // V as rows
+        const int vr = i / (HD / 4), v4 = (i % (HD / 4)) * 4;
+        float4 vx = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (vr < nk) vx = __ldcg(reinterpret_cast<const float4 *>(vg + static_cast<size_t>(kb + vr) * HD + v4));
+        *reinterpret_cast<float4 *>(Vs + vr * HD + v4) = vx;
+      }
     }
     __syncthreads();
-    if (kb + kFkN < kend) fetch(kb + kFkN);  // lands while this tile is computed
-    // ---- S = Q K^T for the thread's 4 x 4 tile
-    float sacc[4][4];
+    // ---- S = Q K^T for the thread's 8 x 8 tile
+    float sacc[8][8];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 8; ++a)
 #pragma unroll
-      for (int b = 0; b < 4; ++b) sacc[a][b] = 0.f;
-#pragma unroll 8
+      for (int b = 0; b < 8; ++b) sacc[a][b] = 0.f;
+#pragma unroll 2
     for (int d = 0; d < HD; ++d) {
-      const float4 qv = *reinterpret_cast<const float4 *>(Qt + d * kFqN + sq);
-      const float4 kv = *reinterpret_cast<const float4 *>(Kt + d * (kFkN + kFpad) + sk);
-      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+      const float4 q0 = *reinterpret_cast<const float4 *>(Qt + d * kFqN + tq * 4);
+      const float4 q1 = *reinterpret_cast<const float4 *>(Qt + d * kFqN + 64 + tq * 4);
+      const float4 k0 = *reinterpret_cast<const float4 *>(Kt + d * kFkN + tk * 4);
+      const float4 k1 = *reinterpret_cast<const float4 *>(Kt + d * kFkN + 64 + tk * 4);
+      const float qa[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+      const float ka[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int a = 0; a < 8; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) sacc[a][b] = fmaf(qa[a], ka[b], sacc[a][b]);
+        for (int b = 0; b < 8; ++b) sacc[a][b] = fmaf(qa[a], ka[b], sacc[a][b]);
     }
+    __syncthreads();  // every thread is done with Kt: Pt takes its space
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int key = kb + sk + b;
-      float4 w;
-      w.x = key <= s_lim[sq + 0] ? __fmul_rn(sacc[0][b], A.scale) : -INFINITY;
-      w.y = key <= s_lim[sq + 1] ? __fmul_rn(sacc[1][b], A.scale) : -INFINITY;
-      w.z = key <= s_lim[sq + 2] ? __fmul_rn(sacc[2][b], A.scale) : -INFINITY;
-      w.w = key <= s_lim[sq + 3] ? __fmul_rn(sacc[3][b], A.scale) : -INFINITY;
-      if (sk + b >= nk) w = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      *reinterpret_cast<float4 *>(Pt + (sk + b) * (kFqN + kFpad) + sq) = w;
+    for (int b = 0; b < 8; ++b) {
+      const int kl = (b < 4 ? 0 : 64) + tk * 4 + (b & 3), key = kb + kl;
+#pragma unroll
+      for (int hq = 0; hq < 2; ++hq) {
+        float w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int a = 4 * hq + e;
+          w[e] = (kl < nk && key <= s_lim[qof(a)]) ? __fmul_rn(sacc[a][b], A.scale) : -INFINITY;
+        }
+        *reinterpret_cast<float4 *>(Pt + kl * kFps + 64 * hq + tq * 4) = make_float4(w[0], w[1], w[2], w[3]);
+      }
     }
     __syncthreads();
-    // ---- online softmax: 4 threads per query, 16 keys each
+    // ---- online softmax: 2 threads per query, keys 2 j + part
     {
-      const int qi = tid >> 2, part = tid & 3;
+      const int qi = tid >> 1, part = tid & 1;
       float mx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) mx = fmaxf(mx, Pt[(part * 16 + j) * (kFqN + kFpad) + qi]);
+#pragma unroll 8
+      for (int j = 0; j < kFkN / 2; ++j) mx = fmaxf(mx, Pt[(2 * j + part) * kFps + qi]);
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       const float m_old = s_m[qi], m_new = fmaxf(m_old, mx);
       float ls = 0.f;
 #pragma unroll 4
-      for (int j = 0; j < 16; ++j) {  // four exponentials in flight
-        float *pp = Pt + (part * 16 + j) * (kFqN + kFpad) + qi;
+      for (int j = 0; j < kFkN / 2; ++j) {  // four exponentials in flight
+        float *pp = Pt + (2 * j + part) * kFps + qi;
         const float sv = *pp;
         const float e = sv == -INFINITY ? 0.f : static_cast<float>(exp(static_cast<double>(__fsub_rn(sv, m_new))));
         *pp = e;
         ls += e;
       }
       ls += __shfl_xor_sync(0xffffffffu, ls, 1);
-      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
       if (part == 0) {
         const float alpha = m_new == -INFINITY ? 1.f : static_cast<float>(exp(static_cast<double>(m_old - m_new)));
         s_alpha[qi] = alpha;
@@ -700,27 +705,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
       }
     }
     __syncthreads();
-    // ---- O = O * alpha + P V for the thread's 4 queries x OD dims
+    // ---- O = O * alpha + P V for the thread's 8 queries x OD dims
     {
-      float al[4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) al[a] = s_alpha[oq + a];
+      for (int a = 0; a < 8; ++a) {
+        const float al = s_alpha[qof(a)];
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < OD; ++b) o[a][b] *= al[a];
-#pragma unroll 4
+        for (int b = 0; b < OD; ++b) o[a][b] *= al;
+      }
+#pragma unroll 2
       for (int k = 0; k < nk; ++k) {
-        const float4 pv = *reinterpret_cast<const float4 *>(Pt + k * (kFqN + kFpad) + oq);
-        const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+        const float4 p0 = *reinterpret_cast<const float4 *>(Pt + k * kFps + tq * 4);
+        const float4 p1 = *reinterpret_cast<const float4 *>(Pt + k * kFps + 64 + tq * 4);
+        const float pa[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
         float vv[OD];
 #pragma unroll
         for (int b = 0; b < OD; b += 4) {
-          const float4 x = *reinterpret_cast<const float4 *>(Vs + k * HD + od + b);
+          const float4 x = *reinterpret_cast<const float4 *>(Vs + k * HD + tk * 4 + 16 * b);
           vv[b] = x.x, vv[b + 1] = x.y, vv[b + 2] = x.z, vv[b + 3] = x.w;
         }
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < 8; ++a)
 #pragma unroll
           for (int b = 0; b < OD; ++b) o[a][b] = fmaf(pa[a], vv[b], o[a][b]);
       }
@@ -729,14 +734,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   __syncthreads();
   if (nsplit == 1) {
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-      const int v = v0 + oq + a;
+    for (int a = 0; a < 8; ++a) {
+      const int q = qof(a), v = v0 + q;
       if (v < nv) {
         const int t = v / A.qpk, h = v - t * A.qpk;
-        const float l = s_l[oq + a];
-        float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + od;
+        const float l = s_l[q];
+        float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD;
 #pragma unroll
-        for (int b = 0; b < OD; ++b) dst[b] = o[a][b] / l;
+        for (int b = 0; b < OD; ++b) dst[dof(b)] = o[a][b] / l;
       }
     }
     return;
@@ -747,9 +752,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   {
     float *pp = pblk + static_cast<size_t>(sp) * kFqN * PW;
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 8; ++a)
 #pragma unroll
-      for (int b = 0; b < OD; ++b) pp[(oq + a) * PW + 2 + od + b] = o[a][b];
+      for (int b = 0; b < OD; ++b) pp[qof(a) * PW + 2 + dof(b)] = o[a][b];
     if (tid < kFqN) {
       pp[tid * PW] = s_m[tid];
       pp[tid * PW + 1] = s_l[tid];
@@ -792,11 +797,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     const int t = v / A.qpk, h = v - t * A.qpk;
     A.out[static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + dd] = acc / s_l[qi];
   }
-}
-
-__host__ __device__ inline size_t pf_flash_smem(int hd) {
-  return (static_cast<size_t>(hd) * kFqN + static_cast<size_t>(hd) * (kFkN + kFpad) + static_cast<size_t>(kFkN) * hd +
-          static_cast<size_t>(kFkN) * (kFqN + kFpad) + 3 * kFqN + kFqN) * 4;
 }
 
 }  // namespace c2s
