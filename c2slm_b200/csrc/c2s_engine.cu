@@ -1976,10 +1976,9 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     if ((rc = pf_gemm(e, l, 4, Ld.tgate, F, H, n, e->pf_g, F, PF_STORE, nullptr)) ||
         (rc = pf_gemm(e, l, 5, Ld.tup, F, H, n, e->pf_u, F, PF_STORE, nullptr)))
       return rc;
-    const size_t cnt = static_cast<size_t>(n) * F;
-    k_pf_swiglu<<<static_cast<int>(std::min<size_t>((cnt + kThreads - 1) / kThreads, 4096)), kThreads, 0, s>>>(
-        e->pf_g, e->pf_u, cnt);
-    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
+    // SwiGLU(gate, up) quantised straight into the down projection's token tiles
+    k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr,
+                                         e->pf_u);
     if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
     CK(cudaGetLastError());
   }

@@ -408,9 +408,12 @@ __global__ void __launch_bounds__(kThreads) k_pf_embed(const int *tok, int n, in
 // the GEMM: bytes into the token tiles q [token tile][superblock][32 KB],
 // superblock scales d [token tile][superblock][128], sub-block sums bs
 // [token tile][superblock][128][8] (int16).  xn (optional) receives the
-// normalised f32 row.
+// normalised f32 row.  With u (the FFN's up projection, same layout as x = its
+// gate), the row quantised is SwiGLU(x, u) instead
+// (internal/simd/c2_tensor_swiglu_nosimd_gen.go:11-19; no norm then).
 __global__ void __launch_bounds__(kThreads) k_pf_norm_q8k(const float *x, int ldx, const float *nw, float eps, int K,
-                                                          int n, uint8_t *q, float *d, int16_t *bs, float *xn) {
+                                                          int n, uint8_t *q, float *d, int16_t *bs, float *xn,
+                                                          const float *u = nullptr) {
   __shared__ float scratch[kWarps];
   __shared__ int32_t s_bsum[kWarps][16];
   const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -436,6 +439,16 @@ __global__ void __launch_bounds__(kThreads) k_pf_norm_q8k(const float *x, int ld
     const float4 a = *reinterpret_cast<const float4 *>(xr + sb * 256 + lane * 8);
     const float4 b = *reinterpret_cast<const float4 *>(xr + sb * 256 + lane * 8 + 4);
     v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    if (u) {
+      const float *ur = u + static_cast<size_t>(t) * ldx + sb * 256 + lane * 8;
+      const float4 ua = *reinterpret_cast<const float4 *>(ur), ub = *reinterpret_cast<const float4 *>(ur + 4);
+      const float uv[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const double g = static_cast<double>(v[i]);
+        v[i] = __fmul_rn(static_cast<float>(g / (1.0 + exp(-g))), uv[i]);
+      }
+    }
     if (nw) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), __ldg(nw + sb * 256 + lane * 8 + i));
@@ -504,15 +517,6 @@ __global__ void __launch_bounds__(kThreads) k_pf_rope_store(float *q, const floa
     const int g = i / hd, j = i - g * hd;
     kc[g * head_stride + static_cast<size_t>(pos) * hd + j] = buf[nqh * hd + i];
     vc[g * head_stride + static_cast<size_t>(pos) * hd + j] = v[static_cast<size_t>(t) * ldkv + i];
-  }
-}
-
-// SwiGLU in place (internal/simd/c2_tensor_swiglu_nosimd_gen.go:11-19)
-__global__ void __launch_bounds__(kThreads) k_pf_swiglu(float *g, const float *u, size_t count) {
-  for (size_t i = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; i < count;
-       i += static_cast<size_t>(gridDim.x) * kThreads) {
-    const double x = static_cast<double>(g[i]);
-    g[i] = __fmul_rn(static_cast<float>(x / (1.0 + exp(-x))), u[i]);
   }
 }
 
