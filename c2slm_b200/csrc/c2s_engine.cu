@@ -927,6 +927,10 @@ int persistent_setup(c2s_engine *e) {
   // computes, so fewer groups than slots leave slots to fill meanwhile
   P.lng = nslot >= 8 ? 3 : nslot >= 4 ? 2 : nslot >= 2 ? 1 : 0;
   if (const char *lg = getenv("C2S_LNG")) P.lng = std::max(0, std::min(3, atoi(lg)));
+  // never more groups than slots: each group holds one slot at a time, and
+  // two groups waiting on one slot's barrier at different phases would
+  // consume a chunk that has not arrived and over-release the slot
+  while ((1 << P.lng) > nslot) --P.lng;
   P.slot_bytes = static_cast<int>(slot_bytes);
   P.slot_alloc = static_cast<int>(slot_bytes + 64);
   size_t off = static_cast<size_t>(nslot) * P.slot_alloc;
