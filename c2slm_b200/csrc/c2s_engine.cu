@@ -804,6 +804,19 @@ int set_fwd_input(c2s_engine *e, int token, int pos, int commit) {
 // ---------------------------------------------------------------------------
 // persistent decode kernel: phase table, shared-memory layout, launch
 // ---------------------------------------------------------------------------
+
+// Warp groups of the many-row matvec phases (2^lng of them): group g
+// consumes ring chunks g, g + ng, ... and chunk k sits in slot k % nslot.  A
+// slot must belong to one group only -- two groups waiting on one slot's
+// full barrier at different uses would see the older phase's parity as
+// complete, read a chunk that has not arrived and over-release the slot --
+// so ng must divide nslot (then chunks k and k + nslot have the same group).
+int ring_groups_log2(int nslot, int lng) {
+  lng = std::max(0, std::min(3, lng));
+  while (lng > 0 && (nslot < (1 << lng) || nslot % (1 << lng) != 0)) --lng;
+  return lng;
+}
+
 int persistent_setup(c2s_engine *e) {
   const c2s_model_desc &d = e->d;
   const TpPlan &pl = e->plan;
@@ -925,12 +938,9 @@ int persistent_setup(c2s_engine *e) {
   P.nslot = nslot;
   // warp groups of the many-row phases: each group holds one slot while it
   // computes, so fewer groups than slots leave slots to fill meanwhile
-  P.lng = nslot >= 8 ? 3 : nslot >= 4 ? 2 : nslot >= 2 ? 1 : 0;
-  if (const char *lg = getenv("C2S_LNG")) P.lng = std::max(0, std::min(3, atoi(lg)));
-  // never more groups than slots: each group holds one slot at a time, and
-  // two groups waiting on one slot's barrier at different phases would
-  // consume a chunk that has not arrived and over-release the slot
-  while ((1 << P.lng) > nslot) --P.lng;
+  int lng = nslot >= 8 ? 3 : nslot >= 4 ? 2 : nslot >= 2 ? 1 : 0;
+  if (const char *lg = getenv("C2S_LNG")) lng = atoi(lg);
+  P.lng = ring_groups_log2(nslot, lng);
   P.slot_bytes = static_cast<int>(slot_bytes);
   P.slot_alloc = static_cast<int>(slot_bytes + 64);
   size_t off = static_cast<size_t>(nslot) * P.slot_alloc;
@@ -2199,6 +2209,8 @@ int c2s_profile_step(c2s_engine *e, int n_steps, float penalty, int window, floa
   return read_status(e);
 }
 
+int c2s_ring_groups(int nslot, int lng) { return ring_groups_log2(nslot, lng); }
+
 // ---- op-level entry points ------------------------------------------------
 int c2s_quantize_row_q8_k(const float *x, uint8_t *y, int cols) {
   if (!x || !y) return fail(C2S_ERR_ARG, "null argument");
@@ -2250,11 +2262,12 @@ int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, i
 //   - The first call on a device does the set-up (it looks up the array's
 //     device address, which may load this library's device code onto that
 //     device); make that first call before any stream capture.
-//   - Weights + x + y + 1 KB must fit in the array (4 MiB); larger calls are
+//   - Weights + x + y + 1.5 KB must fit in the array (4 MiB); larger calls are
 //     rejected with C2S_ERR_ARG before any device work.
-//   - The array's first 256 bytes are the kernel's status block, whose error
-//     word must be zero when a call starts: it is zero when the library
-//     loads, and a call that finds it set clears it before returning.
+//   - The array starts with the kernel's status block (a DevState, padded to
+//     a 256-byte boundary), whose error word must be zero when a call
+//     starts: it is zero when the library loads, and a call that finds it
+//     set clears it before returning.
 //     Nothing else needs an initial value (each call writes x and the
 //     weights before the kernel reads them).
 //   - All calls on one device share the array: calls that overlap in time
@@ -2262,6 +2275,8 @@ int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, i
 //     caller.
 // ---------------------------------------------------------------------------
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+// the status block must stay small next to the array (x starts after it)
+static_assert(sizeof(DevState) <= 512, "c2s_gemv_noalloc: status block outgrew its reservation");
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 static uint8_t *g_noalloc_base[64];  // device address of the array, per device (set-up done)
 static std::mutex g_noalloc_mu;
@@ -2281,7 +2296,7 @@ int c2s_gemv_noalloc(int type, const void *weight, const float *x, float *y, int
   auto a256 = [](size_t v) { return (v + 255) & ~size_t(255); };
   const size_t wb = row_bytes_of(type, cols) * rows;
   // [status block | x | y | weights], each 256-byte aligned, 64 B of slack after each
-  const size_t off_x = 256, off_y = off_x + a256(static_cast<size_t>(cols) * 4 + 64);
+  const size_t off_x = a256(sizeof(DevState)), off_y = off_x + a256(static_cast<size_t>(cols) * 4 + 64);
   const size_t off_w = off_y + a256(static_cast<size_t>(rows) * 4 + 64);
   const size_t need = off_w + a256(wb + 64);
   if (need > kNoAllocScratchBytes)

@@ -53,6 +53,7 @@ SIGNATURES = {
     "c2s_profile_step": (I, [P, I, F, I, P, P]),
     "c2s_trace_decode": (I, [P, I, F, I, P, C.POINTER(I)]),
     "c2s_decode_launches": (I, [P, I]),
+    "c2s_ring_groups": (I, [I, I]),
     "c2s_quantize_row_q8_k": (I, [P, P, I]),
     "c2s_gemv": (I, [I, P, P, P, I, I]),
     "c2s_gemv_noalloc": (I, [I, P, P, P, I, I]),

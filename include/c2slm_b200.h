@@ -5,7 +5,7 @@
  * engine.ComputeLogits -> repetition penalty -> greedy argmax, driven by
  * c2slm.Engine (c2slm.go).  This library replaces that path behind plain C
  * types (no CUDA or torch types in any signature) so the Go packages can bind
- * it through cgo; INTEGRATION.md shows the binding.
+ * it through cgo.
  *
  * Conventions
  *   - Every call returns C2S_OK (0) or a negative c2s_status; the reason is
@@ -194,6 +194,12 @@ int c2s_kernels_per_step(const c2s_engine *e);
  * n_steps issues: 1 when the persistent decode kernel is in use, else
  * c2s_kernels_per_step(e) * n_steps.  No counterpart in the reference. */
 int c2s_decode_launches(const c2s_engine *e, int n_steps);
+/* Warp groups of the persistent kernel's weight ring: the log2 of the group
+ * count the engine uses for a ring of nslot slots when lng is asked for
+ * (clamped so that the group count divides nslot: every slot is consumed by
+ * one group only).  Host-only arithmetic, no device call.  No counterpart in
+ * the reference (its row split is WorkerPool's, engine/pool.go:98-99). */
+int c2s_ring_groups(int nslot, int lng);
 
 /* ------------------------------------------------------------------------ */
 /* Kernel-level entry points (tensor.* of the reference), host buffers       */
@@ -218,7 +224,7 @@ int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x
  * allocate when they need the matvec (device memory held by another
  * allocator; loops that must not take cudaFree's device-wide
  * synchronisation).  The operands are staged in a 4 MiB statically reserved
- * device array: weights + x + y + 1 KB must fit, larger calls return
+ * device array: weights + x + y + 1.5 KB must fit, larger calls return
  * C2S_ERR_ARG.  Runs on the calling thread's default stream and returns when
  * y is written.  The first call on a device does the set-up and should come
  * before any stream capture; calls on one device share the array and must

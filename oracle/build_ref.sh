@@ -5,9 +5,11 @@
 # source is piped to gcc on stdin, so nothing of it is written into this
 # repository; only the binaries land in oracle/_ref/ (git-ignored).
 # Flags follow the reference tests (oracle_q4_k_test.go:135, oracle_c_test.go:101).
+# The reference tree: the first argument, else $C2S_REFERENCE, else a
+# directory named "reference" beside this repository.
 set -euo pipefail
-REF="${1:-/root/reference}"
 HERE="$(cd "$(dirname "$0")" && pwd)"
+REF="${1:-${C2S_REFERENCE:-$HERE/../../reference}}"
 OUT="$HERE/_ref"
 if [ ! -d "$REF/tensor" ]; then
   echo "reference tree not found at $REF; skipping _ref build" >&2

@@ -11,7 +11,7 @@
  * compiled with -O2 -ffp-contract=off (no FMA contraction: Go on amd64 never
  * fuses a*b+c, so neither may the oracle).
  *
- * Deliberate deviations from the reference (each also listed in DESIGN.md):
+ * Deliberate deviations from the reference (each forced by the build):
  *   - Q8_K scratch is sized from cols (the reference's pool scratch holds
  *     16384 cols, engine/pool.go:59, and overflows on 18944-col ffn_down).
  *   - Q6_K token embeddings are dequantised (engine/model.go:221-247 has no

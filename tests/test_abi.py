@@ -63,3 +63,23 @@ def test_host_rejects_bad_arguments_before_any_launch(lib):
     assert L.c2s_forward(None, 1, 0, None) == -1
     assert L.c2s_kv_rewind(None, 1) == -1
     assert L.c2s_generate(None, 4, 1.15, 64, 1, None, None) == -1
+
+
+def test_ring_warp_groups_own_whole_slots(lib):
+    """The persistent kernel's many-row phases split the compute warps into
+    2^lng groups; group g consumes ring chunks g, g + ng, ... and chunk k uses
+    slot k % nslot.  For every ring the engine can build (2..8 slots) and
+    every group count it can ask for, the count it uses must give each slot
+    to one group only: chunks k and k + nslot belong to the same group."""
+    from c2slm_b200 import engine as E
+    L = E.load_library()
+    for nslot in range(2, 9):
+        for want in range(0, 4):
+            lng = L.c2s_ring_groups(nslot, want)
+            ng = 1 << lng
+            assert 0 <= lng <= want and ng <= nslot
+            for k in range(4 * nslot * ng):
+                assert k % ng == (k + nslot) % ng, (nslot, want, lng, k)
+            # the largest count that keeps the property is the one used
+            best = max(l for l in range(want + 1) if nslot % (1 << l) == 0)
+            assert lng == best
