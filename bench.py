@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--tp-steps", type=int, default=256, help="config 3 decode steps")
     ap.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill line (config 4)")
     ap.add_argument("--prefill-tokens", type=int, default=2048, help="config 4 prompt length")
+    ap.add_argument("--no-config0", action="store_true", help="skip the single-op matvec line (config 0)")
+    ap.add_argument("--no-config2", action="store_true", help="skip the 1.5B decode line (config 2)")
+    ap.add_argument("--no-serving", action="store_true", help="skip the data-parallel serving line (config 4)")
     return ap.parse_args()
 
 
@@ -362,11 +365,25 @@ def run_ours(args) -> None:
     prefill = None
     if not args.no_prefill and rank == 0:
         prefill = run_prefill(args, local)
+    serving = None
+    if not args.no_serving:
+        serving = run_serving(args, world, rank, local, dist)
+    config0 = config2 = None
+    if rank == 0 and not args.no_config0:
+        config0 = run_config0(local)
+    if rank == 0 and not args.no_config2:
+        config2 = run_config2(args, local)
     if rank == 0:
         if tp7b is not None:
             line["tp7b"] = tp7b
         if prefill is not None:
             line["prefill"] = prefill
+        if serving is not None:
+            line["serving"] = serving
+        if config0 is not None:
+            line["config0"] = config0
+        if config2 is not None:
+            line["config2"] = config2
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -465,6 +482,145 @@ def run_prefill(args, local: int) -> dict:
         out.update({"int8_tops_projections": round(tops, 1), "int8_nominal_tops": INT8_NOMINAL_TOPS,
                     "frac_of_nominal_int8": round(tops / INT8_NOMINAL_TOPS, 4)})
     return out
+
+
+def run_config0(local: int) -> dict:
+    """one Q4_K x Q8_K matvec of the ffn_down shape (896
+    rows x 4864 columns, seed 0; x ~ N(0,1) quantised to Q8_K inside the op),
+    10,000 repetitions through c2s_bench_gemv (device pointers, one CUDA graph
+    of 1000 launches per replay): L2-hot (one weight copy) and HBM-cold (128
+    rotated copies, 314 MB > L2).  The reference's counterpart is
+    BenchmarkGEMVQ4_K_Q8_K_Cols896 (tensor/ops_test.go:143-156)."""
+    import numpy as np
+    import torch
+    import c2slm_b200.engine as KE
+    from c2slm_b200 import synth
+    rows, cols, reps, copies = 896, 4864, 10000, 128
+    rng = np.random.default_rng(0)
+    w = synth.gen_blocks(rng, KE.Q4_K, rows, cols)
+    x = rng.normal(0, 1, cols).astype(np.float32)
+    stride = (w.nbytes + 255) // 256 * 256
+    dev = torch.device("cuda", local)
+    dw = torch.zeros(stride * copies + 256, dtype=torch.uint8, device=dev)
+    one = torch.from_numpy(w).to(dev)
+    for k in range(copies):
+        dw[k * stride:k * stride + w.nbytes].copy_(one)
+    dx = torch.from_numpy(x).to(dev)
+    dy = torch.zeros(rows, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    algo = w.nbytes + cols * 4 + rows * 4  # weights + f32 x + f32 y per matvec
+    peak, kind = measured_peaks()
+    out = {"metric": "single-op Q4_K x Q8_K matvec (config 0: 896 x 4864, ffn_down shape)", "unit": "us/op",
+           "higher_is_better": False, "reps": reps, "bytes_per_op": algo,
+           "api": "c2s_bench_gemv (c2s_gemv_device launches in a CUDA graph, Q8_K of x inside each launch)"}
+    for name, n in (("l2_hot", 1), ("hbm_cold", copies)):
+        ms = KE.bench_gemv(local, KE.Q4_K, dw.data_ptr(), stride, n, dx.data_ptr(), dy.data_ptr(), rows, cols, reps)
+        us = ms * 1000.0 / reps
+        gbs = algo / (us * 1e-6) / 1e9
+        out[name] = {"value": round(us, 3), "unit": "us/op", "copies": n, "achieved_gbs": round(gbs, 1)}
+        if n > 1:
+            out[name]["roofline"] = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                     "frac": round(gbs / peak, 4), "peak_kind": f"{kind} hbm_gbs"}
+    out["value"] = out["hbm_cold"]["value"]
+    return out
+
+
+def run_config2(args, local: int) -> dict:
+    """the 1.5B-shaped Q4_K_M model (Q4_K/Q6_K, tied Q6_K
+    vocabulary projection), KV cache prefilled to 1024 positions from a
+    1024-token uniform-random prompt (seed 1, tensor-core prefill), then 256
+    greedy decode steps in one persistent launch, timed with CUDA events."""
+    import numpy as np
+    import c2slm_b200 as K
+    from c2slm_b200 import synth
+    ctx, steps = 1024, 256
+    path = synth.cached_model("qwen15b")
+    prompt = np.random.default_rng(1).integers(0, 151643, ctx).astype(np.int32)
+    eng = K.Engine(path, device=local, max_tokens=ctx + steps + 16)
+    eng.ingest_from(0, prompt)
+    eng.bench_decode_timed(3, PENALTY, WINDOW, period=0)
+    eng.seq_len = ctx
+    ms = eng.bench_decode_timed(steps, PENALTY, WINDOW, period=steps)
+    launches = eng.decode_launches(steps)
+    eng.close()
+    sb = stage_bytes(path)
+    per_token = sum(sb[k] for k in ("qkv", "o_proj", "gate_up", "down", "logits")) + \
+        sb["kv_per_pos"] * (ctx + steps / 2.0 + 1)
+    peak, kind = measured_peaks()
+    tok_s = steps / (ms / 1000.0)
+    gbs = per_token * tok_s / 1e9
+    return {"metric": "batch-1 greedy decode tokens/s (config 2: Qwen2.5-1.5B-shaped Q4_K_M, 1024-token context)",
+            "value": round(tok_s, 2), "unit": "tokens/s", "ms_per_step": round(ms / steps, 4), "context": ctx,
+            "steps": steps, "bytes_per_token": int(per_token), "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": "k_persistent", "achieved": round(gbs, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_kind": f"{kind} hbm_gbs"}}
+
+
+SERVING_STREAMS, SERVING_PROMPT, SERVING_STEPS, SERVING_PENALTY = 8, 512, 256, 1.1
+
+
+def run_serving(args, world: int, rank: int, local: int, dist) -> dict | None:
+    """BASELINE config 4's serving mode: 8 independent request streams of the
+    1.5B-shaped model (seeds 3..10), stream s on rank s % world (one per GPU
+    at 8 GPUs).  Each stream: IngestFrom of a 512-token uniform-random prompt
+    (tensor-core prefill), then 256 greedy steps with repetition penalty 1.1
+    over the last 64 tokens (stop tokens do not end a stream, so every stream
+    decodes 256 tokens).  Timed end to end through the public API on the host
+    (ids in, ids out), max over ranks; no collective on the data path."""
+    import numpy as np
+    import torch
+    import c2slm_b200 as K
+    from c2slm_b200 import synth
+    if rank == 0:
+        synth.cached_model("qwen15b")
+    if dist is not None:
+        dist.barrier()
+    path = synth.cached_model("qwen15b")
+    eng = K.Engine(path, device=local, max_tokens=SERVING_PROMPT + SERVING_STEPS + 16)
+    warm = np.random.default_rng(99).integers(0, 151643, SERVING_PROMPT).astype(np.int32)
+    eng.ingest_from(0, warm)
+    eng.generate(8, penalty=SERVING_PENALTY, window=WINDOW, stop_on_special=False)
+    mine = [s for s in range(SERVING_STREAMS) if s % world == rank]
+    pre_s = dec_s = 0.0
+    n_dec = 0
+    torch.cuda.synchronize()
+    for s in mine:
+        prompt = np.random.default_rng(3 + s).integers(0, 151643, SERVING_PROMPT).astype(np.int32)
+        eng.reset()
+        t0 = time.perf_counter()
+        eng.ingest_from(0, prompt)
+        eng.sync()
+        t1 = time.perf_counter()
+        toks = eng.generate(SERVING_STEPS, penalty=SERVING_PENALTY, window=WINDOW, stop_on_special=False)
+        t2 = time.perf_counter()
+        pre_s += t1 - t0
+        dec_s += t2 - t1
+        n_dec += len(toks)
+    eng.close()
+    tot = torch.tensor([pre_s, dec_s, float(n_dec)], dtype=torch.float64, device="cuda")
+    if dist is not None:
+        mx = tot.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        pre_s, dec_s = float(mx[0].item()), float(mx[1].item())
+        n_dec = int(tot[2].item())
+    if rank != 0:
+        return None
+    sb = stage_bytes(path)
+    per_token = sum(sb[k] for k in ("qkv", "o_proj", "gate_up", "down", "logits")) + \
+        sb["kv_per_pos"] * (SERVING_PROMPT + SERVING_STEPS / 2.0 + 1)
+    peak, kind = measured_peaks()
+    dec_rate = n_dec / dec_s
+    per_gpu_gbs = per_token * dec_rate / min(world, SERVING_STREAMS) / 1e9
+    return {"metric": "aggregate decode tokens/s (config 4 serving: 8 streams of the 1.5B shape, 512-token prompts, "
+                      "256 greedy steps, penalty 1.1 over 64)",
+            "value": round(dec_rate, 1), "unit": "tokens/s", "n_gpus": world, "streams": SERVING_STREAMS,
+            "scaling": "strong", "decode_tokens": n_dec,
+            "prefill_tokens_per_s": round(SERVING_STREAMS * SERVING_PROMPT / pre_s, 1),
+            "timing": "host wall clock around c2s_ingest_from / c2s_generate (ids in, ids out), max over ranks",
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(per_gpu_gbs / peak, 4), "peak_kind": f"{kind} hbm_gbs",
+                         "per": "GPU, decode"}}
 
 
 def eng_seq_wrap(i: int) -> bool:

@@ -406,4 +406,135 @@ __device__ __forceinline__ void dequant_row_cta(int type, const uint8_t *row, fl
   }
 }
 
+// ---- tagged words of the one-GPU dataflow hand-off (gpu scope) ----------
+__device__ __forceinline__ void st_tag(unsigned long long *p, unsigned tag, float v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p),
+               "l"((static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v))
+               : "memory");
+}
+// two consecutive words (16-B aligned), each single-copy atomic
+__device__ __forceinline__ ulonglong2 ld_tag2(const unsigned long long *p) {
+  ulonglong2 v;
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned tag_of(unsigned long long w) { return static_cast<unsigned>(w >> 32); }
+__device__ __forceinline__ float val_of(unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+// acquire side of a hand-off that also publishes plain data (fence after
+// the poll observed the writer's word; the writer fenced before storing it)
+__device__ __forceinline__ void fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// Polls tagged words into shared memory as floats: up to three segments
+// (src[k][0 .. n[k]), n[k] % 4 == 0, 16-B aligned) into dst[k], every
+// compute thread taking groups of 4 words, two groups in flight, until each
+// word carries `tag`.  Bounded (~2 s): on expiry sets the error flag and
+// returns false.  The caller synchronises the CTA before reading dst.
+__device__ __noinline__ bool poll_to_smem(const unsigned long long *s0, int n0, float *d0,
+                                          const unsigned long long *s1, int n1, float *d1,
+                                          const unsigned long long *s2, int n2, float *d2, unsigned tag,
+                                          unsigned *err) {
+  const int g0n = n0 / 4, g1n = n1 / 4, ng = g0n + g1n + n2 / 4;
+  auto at = [&](int g, const unsigned long long *&src, float *&dst) {
+    if (g < g0n) {
+      src = s0 + 4 * g;
+      dst = d0 + 4 * g;
+    } else if (g < g0n + g1n) {
+      src = s1 + 4 * (g - g0n);
+      dst = d1 + 4 * (g - g0n);
+    } else {
+      src = s2 + 4 * (g - g0n - g1n);
+      dst = d2 + 4 * (g - g0n - g1n);
+    }
+  };
+  bool ok = true;
+  for (int base = 0; base < ng; base += 2 * kThreads) {
+    const int ga = base + threadIdx.x, gb = ga + kThreads;
+    const unsigned long long *pa = nullptr, *pb = nullptr;
+    float *da = nullptr, *db = nullptr;
+    ulonglong2 a0, a1, b0, b1;
+    if (ga < ng) {
+      at(ga, pa, da);
+      a0 = ld_tag2(pa);
+      a1 = ld_tag2(pa + 2);
+    }
+    if (gb < ng) {
+      at(gb, pb, db);
+      b0 = ld_tag2(pb);
+      b1 = ld_tag2(pb + 2);
+    }
+    long long t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+      bool all = true;
+      if (ga < ng && (tag_of(a0.x) != tag || tag_of(a0.y) != tag || tag_of(a1.x) != tag || tag_of(a1.y) != tag)) {
+        all = false;
+        a0 = ld_tag2(pa);
+        a1 = ld_tag2(pa + 2);
+      }
+      if (gb < ng && (tag_of(b0.x) != tag || tag_of(b0.y) != tag || tag_of(b1.x) != tag || tag_of(b1.y) != tag)) {
+        all = false;
+        b0 = ld_tag2(pb);
+        b1 = ld_tag2(pb + 2);
+      }
+      if (all) break;
+      if (it == 0) {
+        t0 = clock64();
+      } else if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+        atomicOr(err, kErrCounter);
+        ok = false;
+        break;
+      }
+    }
+    if (ga < ng) *reinterpret_cast<float4 *>(da) = make_float4(val_of(a0.x), val_of(a0.y), val_of(a1.x), val_of(a1.y));
+    if (gb < ng) *reinterpret_cast<float4 *>(db) = make_float4(val_of(b0.x), val_of(b0.y), val_of(b1.x), val_of(b1.y));
+    if (!ok) break;
+  }
+  return ok;
+}
+
+// Polls the 8 tagged words x[8*lane .. 8*lane+7] of one 256-value block
+// (16-B aligned) until each carries `tag`; bounded like poll_to_smem.
+__device__ __forceinline__ bool poll_block8(const unsigned long long *p, unsigned tag, float (&x)[8], unsigned *err) {
+  ulonglong2 w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w[j] = ld_tag2(p + 2 * j);
+  long long t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    bool all = true;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (tag_of(w[j].x) != tag || tag_of(w[j].y) != tag) all = false;
+    if (all) break;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = ld_tag2(p + 2 * j);
+    if (it == 0) {
+      t0 = clock64();
+    } else if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+      atomicOr(err, kErrCounter);
+      return false;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    x[2 * j] = val_of(w[j].x);
+    x[2 * j + 1] = val_of(w[j].y);
+  }
+  return true;
+}
+
+// one tagged word, polled until it carries `tag` (bounded); its value bits
+__device__ __forceinline__ bool poll_tag1(const unsigned long long *p, unsigned tag, uint32_t &bits, unsigned *err) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  const long long t0 = clock64();
+  for (uint32_t it = 0; tag_of(w) != tag; ++it) {
+    if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
+      atomicOr(err, kErrCounter);
+      return false;
+    }
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  }
+  bits = static_cast<uint32_t>(w);
+  return true;
+}
+
 }  // namespace c2s

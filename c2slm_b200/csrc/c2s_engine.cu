@@ -477,6 +477,9 @@ struct c2s_engine {
   PPhase *d_phases = nullptr;
   int nphase = 0;
   unsigned *gbar = nullptr;
+  unsigned long long *df_words = nullptr;  // tagged hand-off buffers of the one-GPU persistent kernel
+  size_t df_nwords = 0;
+  unsigned df_tag = 0;                     // tag base of the next launch (advanced past every tag used)
   PParams pp{};
   size_t p_smem = 0;
   bool use_persistent = true;
@@ -1019,10 +1022,30 @@ int persistent_setup(c2s_engine *e) {
   P.token_ids = e->token_ids;
   P.out_tokens = e->out_tokens;
   P.gbar = e->gbar;
-  P.ll = tp ? 1 : 0;  // one GPU: grid barriers and X (tagged words measured slower there)
-  CK(cudaFuncSetAttribute(k_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(e->p_smem)));
+  P.ll = tp ? 1 : 0;  // tensor parallel: the cross-GPU exchange of o-proj / down partial rows
+  // one GPU: phases hand off through tagged words, without grid barriers
+  P.df = tp ? 0 : 1;
+  if (P.df) {
+    const size_t nw[7] = {static_cast<size_t>(H), static_cast<size_t>(nq), static_cast<size_t>(kvd),
+                          static_cast<size_t>(kvd), static_cast<size_t>(nq), static_cast<size_t>(F), 2};
+    size_t tot = 0;
+    for (size_t w : nw) tot += (w + 3) & ~size_t(3);  // 32-byte aligned regions
+    CK(cudaMalloc(&e->df_words, tot * 8));
+    CK(cudaMemsetAsync(e->df_words, 0, tot * 8, e->stream));  // ordered before every launch on the stream
+    e->df_nwords = tot;
+    e->df_tag = 0;
+    unsigned long long *w = e->df_words;
+    unsigned long long **dst[7] = {&P.tX, &P.tq, &P.tk, &P.tv, &P.tatt, &P.th, &P.tsel};
+    for (int i = 0; i < 7; ++i) {
+      *dst[i] = w;
+      w += (nw[i] + 3) & ~size_t(3);
+    }
+  }
+  const void *kfn = P.df ? reinterpret_cast<const void *>(k_persistent<true>)
+                         : reinterpret_cast<const void *>(k_persistent<false>);
+  CK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(e->p_smem)));
   int blocks = 0;
-  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, k_persistent, kPThreads, e->p_smem));
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kfn, kPThreads, e->p_smem));
   const char *mode = getenv("C2S_DECODE");
   e->use_persistent = blocks >= 1 && !(mode && strcmp(mode, "graph") == 0);
   return C2S_OK;
@@ -1038,8 +1061,23 @@ int launch_persistent(c2s_engine *e, int n_steps, int rewind_period, int rewind_
   P.rewind_period = rewind_period;
   P.rewind_base = rewind_base;
   CK(cudaMemsetAsync(e->gbar, 0, 4 * static_cast<size_t>(e->num_sms), e->stream));
+  if (P.df) {
+    // tags of this launch: tag0 + 1 .. tag0 + phases; the next launch starts
+    // past them, so no word left by this one (finished or stopped) can match
+    const unsigned phases = static_cast<unsigned>(n_steps) * static_cast<unsigned>(e->nphase);
+    if (static_cast<unsigned long long>(e->df_tag) + phases + 2 >= 0x7fffffffull) {  // restart the tag space
+      CK(cudaMemsetAsync(e->df_words, 0, e->df_nwords * 8, e->stream));
+      e->df_tag = 0;
+    }
+    P.tag0 = e->df_tag;
+    e->df_tag += phases + 2;
+    // the attention's split arrivals accumulate from zero over the launch
+    CK(cudaMemsetAsync(e->st->attn_counter, 0, sizeof(e->st->attn_counter), e->stream));
+  }
   void *args[] = {&P};
-  CK(cudaLaunchCooperativeKernel(reinterpret_cast<const void *>(k_persistent), dim3(e->num_sms), dim3(kPThreads),
+  const void *kfn = P.df ? reinterpret_cast<const void *>(k_persistent<true>)
+                         : reinterpret_cast<const void *>(k_persistent<false>);
+  CK(cudaLaunchCooperativeKernel(kfn, dim3(e->num_sms), dim3(kPThreads),
                                  args, e->p_smem, e->stream));
   return C2S_OK;
 }
@@ -1284,7 +1322,9 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
     e->tp_persist_ok = e->use_persistent;
     e->use_persistent = false;
   }
-  CK(cudaStreamSynchronize(e->stream));
+  // every set-up copy and memset (some on the legacy stream, which the
+  // engine's non-blocking stream does not wait for) completes here
+  CK(cudaDeviceSynchronize());
   return C2S_OK;
 }
 
@@ -1438,7 +1478,7 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->out_tokens), static_cast<void *>(e->rows_idx),
                   static_cast<void *>(e->scratch_x), static_cast<void *>(e->st),
                   static_cast<void *>(e->gbar), static_cast<void *>(e->delta),
-                  static_cast<void *>(e->logits_full)})
+                  static_cast<void *>(e->logits_full), static_cast<void *>(e->df_words)})
     if (p) cudaFree(p);
   for (void *p : {static_cast<void *>(e->pf_x), static_cast<void *>(e->pf_q), static_cast<void *>(e->pf_k),
                   static_cast<void *>(e->pf_v), static_cast<void *>(e->pf_att), static_cast<void *>(e->pf_g),
@@ -1518,9 +1558,11 @@ struct DevBuf {
   ~DevBuf() {
     if (p) cudaFree(p);
   }
-  int alloc(size_t n) {
+  // zeroed on the op's stream: the op streams are non-blocking, so a memset
+  // on the legacy default stream would not be ordered before the kernels
+  int alloc(size_t n, cudaStream_t s) {
     if (cudaMalloc(&p, n * sizeof(T) + 64) != cudaSuccess) return fail(C2S_ERR_OOM, "cudaMalloc failed");
-    cudaMemset(p, 0, n * sizeof(T) + 64);
+    if (cudaMemsetAsync(p, 0, n * sizeof(T) + 64, s) != cudaSuccess) return fail(C2S_ERR_CUDA, "cudaMemsetAsync failed");
     return C2S_OK;
   }
 };
@@ -2220,8 +2262,8 @@ int c2s_quantize_row_q8_k(const float *x, uint8_t *y, int cols) {
   DevBuf<float> dx;
   DevBuf<uint8_t> dy;
   const size_t ybytes = static_cast<size_t>(cols / 256) * 292;
-  if (int rc = dx.alloc(cols)) return rc;
-  if (int rc = dy.alloc(ybytes)) return rc;
+  if (int rc = dx.alloc(cols, c->stream)) return rc;
+  if (int rc = dy.alloc(ybytes, c->stream)) return rc;
   CK(cudaMemcpyAsync(dx.p, x, cols * 4, cudaMemcpyHostToDevice, c->stream));
   const int nsb = cols / 256;
   k_quantize_q8k<<<(nsb + kWarps - 1) / kWarps, kThreads, 0, c->stream>>>(dx.p, dy.p, cols);
@@ -2238,9 +2280,9 @@ int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, i
   const size_t wb = row_bytes_of(type, cols) * rows;
   DevBuf<uint8_t> dw;
   DevBuf<float> dx, dy;
-  if (int rc = dw.alloc(wb)) return rc;
-  if (int rc = dx.alloc(cols)) return rc;
-  if (int rc = dy.alloc(rows)) return rc;
+  if (int rc = dw.alloc(wb, c->stream)) return rc;
+  if (int rc = dx.alloc(cols, c->stream)) return rc;
+  if (int rc = dy.alloc(rows, c->stream)) return rc;
   CK(cudaMemcpyAsync(dw.p, weight, wb, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c->stream));
   if (int rc = gemv_launch(c, type, dw.p, dx.p, dy.p, rows, cols, nullptr)) return rc;
@@ -2288,6 +2330,51 @@ int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x
   if (int rc = op_ctx(device, &c)) return rc;
   DeviceGuard g(device);
   return gemv_launch(c, type, d_weight, d_x, d_y, rows, cols, nullptr);
+}
+
+int c2s_bench_gemv(int device, int type, const void *d_weight, size_t copy_stride, int n_copies, const float *d_x,
+                   float *d_y, int rows, int cols, int reps, float *ms_out) {
+  if (!d_weight || !d_x || !d_y || !ms_out) return fail(C2S_ERR_ARG, "null argument");
+  if (n_copies < 1 || reps < 1) return fail(C2S_ERR_ARG, "n_copies and reps must be positive");
+  if (reps % 1000 && reps > 4000) return fail(C2S_ERR_ARG, "reps must be a multiple of 1000 or at most 4000");
+  if (n_copies > 1 && (copy_stride & 255)) return fail(C2S_ERR_ARG, "copy_stride must be a multiple of 256");
+  if (reinterpret_cast<uintptr_t>(d_weight) & 255) return fail(C2S_ERR_ARG, "d_weight must be 256-byte aligned");
+  if (int rc = check_matrix(type, rows, cols, "bench_gemv")) return rc;
+  OpCtx *c;
+  if (int rc = op_ctx(device, &c)) return rc;
+  DeviceGuard g(device);
+  const int per = reps % 1000 == 0 ? 1000 : reps, replays = reps / per;
+  const uint8_t *w0 = static_cast<const uint8_t *>(d_weight);
+  // one graph of `per` launches, launch i on copy i % n_copies
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  int rc = C2S_OK;
+  for (int i = 0; i < per && rc == C2S_OK; ++i)
+    rc = gemv_launch(c, type, w0 + static_cast<size_t>(i % n_copies) * copy_stride, d_x, d_y, rows, cols, nullptr);
+  const cudaError_t ec = cudaStreamEndCapture(c->stream, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (ec != cudaSuccess) return fail(C2S_ERR_CUDA, "bench_gemv capture: %s", cudaGetErrorString(ec));
+  const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) return fail(C2S_ERR_CUDA, "bench_gemv instantiate: %s", cudaGetErrorString(ei));
+  cudaEvent_t a, b;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&b));
+  cudaError_t er = cudaGraphLaunch(exec, c->stream);  // warm-up
+  if (!er) er = cudaEventRecord(a, c->stream);
+  for (int r = 0; r < replays && !er; ++r) er = cudaGraphLaunch(exec, c->stream);
+  if (!er) er = cudaEventRecord(b, c->stream);
+  if (!er) er = cudaEventSynchronize(b);
+  if (!er) er = cudaEventElapsedTime(ms_out, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  cudaGraphExecDestroy(exec);
+  if (er) return fail(C2S_ERR_CUDA, "bench_gemv: %s", cudaGetErrorString(er));
+  return op_finish(c);
 }
 
 int c2s_gemv_noalloc(int type, const void *weight, const float *x, float *y, int rows, int cols) {
@@ -2348,10 +2435,10 @@ int c2s_kquant_partials(int type, const void *weight, const float *x, int32_t *d
   DevBuf<uint8_t> dw;
   DevBuf<float> dx, dy;
   DevBuf<int32_t> dd;
-  if (int rc = dw.alloc(wb)) return rc;
-  if (int rc = dx.alloc(cols)) return rc;
-  if (int rc = dy.alloc(rows)) return rc;
-  if (int rc = dd.alloc(nd)) return rc;
+  if (int rc = dw.alloc(wb, c->stream)) return rc;
+  if (int rc = dx.alloc(cols, c->stream)) return rc;
+  if (int rc = dy.alloc(rows, c->stream)) return rc;
+  if (int rc = dd.alloc(nd, c->stream)) return rc;
   CK(cudaMemcpyAsync(dw.p, weight, wb, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c->stream));
   if (int rc = gemv_launch(c, type, dw.p, dx.p, dy.p, rows, cols, dd.p)) return rc;
@@ -2370,10 +2457,10 @@ int c2s_dot_rows_f32x(int type, const void *weight, const float *x, const int32_
   DevBuf<uint8_t> dw;
   DevBuf<float> dx, dout;
   DevBuf<int> di;
-  if (int rc = dw.alloc(wb)) return rc;
-  if (int rc = dx.alloc(cols)) return rc;
-  if (int rc = dout.alloc(n)) return rc;
-  if (int rc = di.alloc(n)) return rc;
+  if (int rc = dw.alloc(wb, c->stream)) return rc;
+  if (int rc = dx.alloc(cols, c->stream)) return rc;
+  if (int rc = dout.alloc(n, c->stream)) return rc;
+  if (int rc = di.alloc(n, c->stream)) return rc;
   CK(cudaMemcpyAsync(dw.p, weight, wb, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(cols) * 4, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemcpyAsync(di.p, rows_idx, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
@@ -2390,9 +2477,9 @@ int c2s_rmsnorm(float *out, const float *x, const float *w, int n, float eps) {
   OpCtx *c;
   if (int rc = op_ctx(current_device(), &c)) return rc;
   DevBuf<float> dx, dw, dout;
-  if (int rc = dx.alloc(n)) return rc;
-  if (int rc = dw.alloc(n)) return rc;
-  if (int rc = dout.alloc(n)) return rc;
+  if (int rc = dx.alloc(n, c->stream)) return rc;
+  if (int rc = dw.alloc(n, c->stream)) return rc;
+  if (int rc = dout.alloc(n, c->stream)) return rc;
   CK(cudaMemcpyAsync(dx.p, x, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemcpyAsync(dw.p, w, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
   CK(cudaFuncSetAttribute(k_rmsnorm_op, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
@@ -2407,9 +2494,9 @@ int c2s_swiglu(float *out, const float *gate, const float *up, int n) {
   OpCtx *c;
   if (int rc = op_ctx(current_device(), &c)) return rc;
   DevBuf<float> dg, du, dout;
-  if (int rc = dg.alloc(n)) return rc;
-  if (int rc = du.alloc(n)) return rc;
-  if (int rc = dout.alloc(n)) return rc;
+  if (int rc = dg.alloc(n, c->stream)) return rc;
+  if (int rc = du.alloc(n, c->stream)) return rc;
+  if (int rc = dout.alloc(n, c->stream)) return rc;
   CK(cudaMemcpyAsync(dg.p, gate, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemcpyAsync(du.p, up, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, c->stream));
   k_swiglu_op<<<(n + 255) / 256, 256, 0, c->stream>>>(dout.p, dg.p, du.p, n);
@@ -2426,8 +2513,8 @@ int c2s_dequant_row(int type, const void *row, float *out, int cols) {
   if (int rc = op_ctx(current_device(), &c)) return rc;
   DevBuf<uint8_t> dr;
   DevBuf<float> dout;
-  if (int rc = dr.alloc(rb)) return rc;
-  if (int rc = dout.alloc(cols)) return rc;
+  if (int rc = dr.alloc(rb, c->stream)) return rc;
+  if (int rc = dout.alloc(cols, c->stream)) return rc;
   CK(cudaMemcpyAsync(dr.p, row, rb, cudaMemcpyHostToDevice, c->stream));
   k_dequant_op<<<1, kThreads, 0, c->stream>>>(type, dr.p, dout.p, cols);
   CK(cudaGetLastError());

@@ -795,6 +795,13 @@ struct AttnJob {
   int hd, qpk, max_splits;
   int store_kv;                    // this item writes the cache row of pos (one item per kv head)
   float eps, scale;
+  // dataflow hand-off of the persistent kernel (tq null: plain q/k/v/out):
+  // q/k/v read as tagged words polled until they carry tag_in, outputs
+  // stored as tagged words with tag_out; the split arrivals of this phase
+  // wait for cnt_base + nsplit (the counter accumulates over the launch)
+  const unsigned long long *tq = nullptr, *tk = nullptr, *tv = nullptr;
+  unsigned long long *tout = nullptr;
+  unsigned tag_in = 0, tag_out = 0, cnt_base = 0;
 };
 
 // Work items of the attention of position pos on one rank (nh local query
@@ -866,6 +873,7 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
   float *buf = asmem, *qs = buf + NB * SUB * hd;
   float *knew = qs + qpk * hd, *vnew = knew + hd, *sc = vnew + hd;
   __shared__ int s_last;
+  bool ok_in = true;  // a tagged input poll gave up (error flag set)
   const int nwin = (p1 - p0 + WIN - 1) / WIN;
   // load q of the sequence: window w, K (r < nsw) or V, sub-chunk r mod nsw
   struct Ld {
@@ -904,10 +912,14 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
     for (int q = 0; q < NB && q < n_loads; ++q) issue(q);
   }
   // projections: every load in flight at once
-  for (int i = tid; i < qpk * hd; i += kThreads) qs[i] = __ldcg(J.q + i);
-  for (int i = tid; i < hd; i += kThreads) {
-    knew[i] = __ldcg(J.k + i);
-    vnew[i] = __ldcg(J.v + i);
+  if (J.tq) {  // tagged words of the QKV phase
+    ok_in = poll_to_smem(J.tq, qpk * hd, qs, J.tk, hd, knew, J.tv, hd, vnew, J.tag_in, err);
+  } else {
+    for (int i = tid; i < qpk * hd; i += kThreads) qs[i] = __ldcg(J.q + i);
+    for (int i = tid; i < hd; i += kThreads) {
+      knew[i] = __ldcg(J.k + i);
+      vnew[i] = __ldcg(J.v + i);
+    }
   }
   csync();
   if (J.q_norm || J.k_norm) {  // Qwen3 per-head QK-norm (engine/forward.go:80-91)
@@ -940,7 +952,7 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
   float m = -INFINITY, l = 0.f, acc[E];  // acc: d = lane*E .. lane*E+E-1
 #pragma unroll
   for (int j = 0; j < E; ++j) acc[j] = 0.f;
-  bool ok = true;
+  bool ok = ok_in;
   // wait for load q (if it reads the cache), complete it with row pos, and
   // return its buffer
   auto arrive = [&](int q, const Ld &L) {
@@ -1069,7 +1081,13 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
   if (J.nsplit == 1) {  // single split: normalise and write the heads directly
     if (lead)
 #pragma unroll
-      for (int j = 0; j < E; ++j) J.out[(h0 + hw) * hd + lane * E + j] = acc[j] / l;
+      for (int j = 0; j < E; ++j) {
+        const int o = (h0 + hw) * hd + lane * E + j;
+        if (J.tout)
+          st_tag(J.tout + o, J.tag_out, acc[j] / l);
+        else
+          J.out[o] = acc[j] / l;
+      }
     return ok;
   }
   // partial (m, l, acc) of this split; the last split of the group combines
@@ -1089,7 +1107,7 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
     if (J.dist) {  // arrive, then wait (bounded) for every split of the group
       asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(J.counter) : "memory");
       const long long t0 = clock64();
-      for (uint32_t it = 0; ld_acquire_gpu_u32(J.counter) < static_cast<unsigned>(ns); ++it)
+      for (uint32_t it = 0; ld_acquire_gpu_u32(J.counter) < J.cnt_base + static_cast<unsigned>(ns); ++it)
         if ((it & 15u) == 15u && clock64() - t0 > kSpinCycles) {
           atomicOr(err, kErrCounter);
           ok = false;
@@ -1178,8 +1196,11 @@ __device__ bool attend_t(const AttnJob &J, float *asmem, uint64_t *bars, uint32_
     csync();
   }
   for (int i = o_lo + tid; i < o_hi; i += kThreads) {
-    const int h = i / hd;
-    J.out[(h0 + h) * hd + (i - h * hd)] = Os[i] / s_L[h - hlo];
+    const int h = i / hd, o = (h0 + h) * hd + (i - h * hd);
+    if (J.tout)
+      st_tag(J.tout + o, J.tag_out, Os[i] / s_L[h - hlo]);
+    else
+      J.out[o] = Os[i] / s_L[h - hlo];
   }
   if (!J.dist && tid == 0) *J.counter = 0;
   return ok;

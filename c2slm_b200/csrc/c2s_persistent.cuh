@@ -89,6 +89,20 @@ struct PParams {
   float *xbuf;
   const unsigned long long *recv, *argbuf;
   unsigned long long *peer_recv[8], *peer_arg[8];
+  // dataflow hand-off (one GPU): no grid barrier between phases.  Every
+  // phase writes its output as tagged 64-bit words (tag << 32 | value bits)
+  // with the tag of its phase, tag(kp) = tag0 + kp + 1 (kp counts the
+  // launch's phases; the host advances tag0 past every tag a launch can
+  // write, so a stale word never matches), and the next phase polls the
+  // words it reads until they carry the previous phase's tag.  Each phase
+  // reads the output of the phase just before it, so the poll is the only
+  // wait.  Buffers: tX[H] residual (o-proj, down), tq/tk/tv (QKV), tatt
+  // (attention), th[F] (gate/up: SwiGLU output), tsel[0] the selected
+  // token (logits), tsel[1] the forward's commit (down of the last layer,
+  // CTA 0), which also publishes the state it wrote before it.
+  int df;
+  unsigned tag0;
+  unsigned long long *tX, *tq, *tk, *tv, *tatt, *th, *tsel;
 };
 constexpr int kMaxRanks = 8;
 
@@ -257,6 +271,31 @@ __device__ __forceinline__ void build_q8k_global(const float *src, int cols, int
   }
 }
 
+// Q8_K of a tagged global vector (the dataflow hand-off of h) into shared
+// memory: warp w quantises superblocks w, w + kWarps, ..., each polled until
+// every word carries `tag`.  False if a poll gave up (error flag set).
+__device__ __noinline__ bool build_q8k_tagged(const unsigned long long *src, unsigned tag, int cols, int8_t *qs,
+                                              float *d, int32_t *bsum, unsigned *err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nsb = cols / 256;
+  bool ok = true;
+  for (int sb = warp; sb < nsb; sb += kWarps) {
+    float x[8];
+    ok = poll_block8(src + sb * 256 + lane * 8, tag, x, err) && ok;
+    quantize_sb_warp(x, d + sb, bsum + sb * 16, [&](int ln, const int (&q)[8]) {
+      int8_t *dst = qs + q8_pad_index(sb * 256 + ln * 8);
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w0 |= (static_cast<uint32_t>(q[i]) & 0xFFu) << (8 * i);
+        w1 |= (static_cast<uint32_t>(q[4 + i]) & 0xFFu) << (8 * i);
+      }
+      *reinterpret_cast<uint2 *>(dst) = make_uint2(w0, w1);
+    });
+  }
+  return ok;
+}
+
 // phase pi of a decode step: 0 = logits, then per layer qkv, attn, o-proj,
 // gate/up, down
 __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
@@ -337,8 +376,10 @@ __device__ void build_phase(const PParams &P, int pi, PPhase &ph) {
 // position ranges, so the CTA that stores a cache row is the one that reads
 // it in later steps.
 // ---------------------------------------------------------------------------
+template <bool DF>
 __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, uint64_t *abar, uint32_t (&uses)[kAttnBufs],
-                            int item, int pos, const float *rope_row) {
+                            int item, int pos, const float *rope_row, unsigned tag_in, unsigned tag_out,
+                            const unsigned *cbase) {
   DevState *st = P.st;
   if (pos < 0 || pos >= P.max_tokens) {
     if (threadIdx.x == 0 && item == 0) atomicOr(&st->err, kErrPos);
@@ -375,6 +416,15 @@ __device__ bool p_attention(const PParams &P, const PPhase &ph, float *asmem, ui
   J.max_splits = P.max_splits;
   J.eps = P.eps;
   J.scale = P.scale;
+  if (DF) {  // inputs and outputs as tagged words; split arrivals counted over the launch
+    J.tq = P.tq + static_cast<size_t>(J.h0) * hd;
+    J.tk = P.tk + J.g * hd;
+    J.tv = P.tv + J.g * hd;
+    J.tout = P.tatt;
+    J.tag_in = tag_in;
+    J.tag_out = tag_out;
+    J.cnt_base = cbase[x];
+  }
   return attend(J, asmem, abar, uses, &st->err);
 }
 
@@ -464,9 +514,10 @@ __device__ __forceinline__ bool warp_wait_full(uint64_t *bar, uint32_t parity, u
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+template <bool DF>
 __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint32_t &k_ring, float (*red)[kWarps],
                          float *scratch, int *s_flag, int *s_pos, float *s_rope, unsigned long long *tr,
-                         unsigned &xb, bool from_X) {
+                         unsigned &xb, bool from_X, unsigned tag_in, unsigned tag_out, int step, int *s_halt) {
   const int G = gridDim.x, c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   DevState *st = P.st;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
@@ -486,20 +537,26 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   PhaseRows R;
   const int nchunks = phase_rows(ph, c, G, P.slot_bytes, R);
   // the attention's split arrivals of this layer: every split has finished
-  // waiting on them before the grid barrier this phase follows
-  if (ph.kind == K_OPROJ && tid == 0 && c < 64) st->attn_counter[c] = 0;
+  // waiting on them before the grid barrier this phase follows (dataflow:
+  // the counters accumulate over the launch instead)
+  if (!DF && ph.kind == K_OPROJ && tid == 0 && c < 64) st->attn_counter[c] = 0;
+  // dataflow: this phase's input is the previous phase's tagged output (the
+  // first phase of a launch reads the plain buffers the host or the last
+  // launch left)
+  const bool dfi = DF && !from_X;
   const bool residual = ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN;
   const bool normed = ph.kind == K_QKV || ph.kind == K_FFN_UP || ph.kind == K_LOGITS;
   // ---- loads the epilogue needs, requested first
   float xres = 0.f, bias[kMaxSegs] = {0.f, 0.f, 0.f};
-  const bool tp = P.world > 1, ll = P.ll != 0;
+  // (the dataflow kernel is the one-GPU specialisation: no tensor-parallel paths)
+  const bool tp = !DF && P.world > 1, ll = !DF && P.ll != 0;
   if (residual && !ll && R.r0[0] + tid < R.r1[0]) xres = __ldcg(P.X + R.r0[0] + tid);
 #pragma unroll
   for (int s = 0; s < kMaxSegs; ++s)
     if (s < ph.nseg && ph.seg[s].bias && R.r0[s] + tid < R.r1[s]) bias[s] = __ldg(ph.seg[s].bias + R.r0[s] + tid);
   __shared__ int win[kThreads];
-  __shared__ int s_fail;
-  if (ph.kind == K_LOGITS) {
+  __shared__ int s_fail, s_tok;
+  auto read_window = [&]() {
     // SeqLen = the position this step forwards; the penalty window's ids and
     // the RoPE row of that position (kept in shared memory for the step)
     const int wpos = ldst(&st->seq_len);
@@ -509,8 +566,12 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     const int half = P.hd / 2;
     if (wpos >= 0 && wpos < P.rope_len && tid < P.hd)
       s_rope[tid] = __ldg((tid < half ? P.rope_cos : P.rope_sin) + static_cast<size_t>(wpos) * half + (tid % half));
-  }
-  if (tid == 0) s_fail = 0;
+  };
+  if (ph.kind == K_LOGITS && !dfi) read_window();
+  // the flag is clear between phases (a phase that set it ended the loop);
+  // the first phase of a launch clears it before anything can set it
+  if (from_X && tid == 0) s_fail = 0;
+  if (from_X) csync();
   // ---- input vector: 4 values per thread per float4 slot (cols <= 16 * kThreads)
   const int n4 = cols >> 2;
   if (normed) {
@@ -519,10 +580,26 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     const float4 *w4 = reinterpret_cast<const float4 *>(ph.norm_w);
     const bool embed = ph.kind == K_QKV && ph.do_embed;
     if (embed) {
-      int tok = ldst(&st->fwd_token);
+      if (dfi) {  // the token the previous step's logits phase selected
+        if (tid == 0) {
+          uint32_t bits = 0;
+          if (!poll_tag1(P.tsel, tag_in, bits, &st->err)) s_fail = 1;
+          fence_gpu();  // the selection's state and every CTA's earlier K/V rows
+          s_tok = static_cast<int>(bits);
+        }
+      } else if (tid == 0) {
+        s_tok = ldst(&st->fwd_token);
+      }
+      csync();
+      int tok = s_tok;
       if (tok < 0 || tok >= st->vocab) tok = 0;  // engine/model.go:222-224
       dequant_row_cta(P.embd_type, P.embd_w + static_cast<size_t>(tok) * P.embd_row_bytes, xn, cols);
       csync();
+      if (DF) {  // the residual rows this CTA owns in o-proj / down (same thread)
+        int a, b;
+        seg_rows(P.H, c, G, a, b);
+        if (a + tid < b) P.X[a + tid] = xn[a + tid];
+      }
     }
     // tensor parallel: X = residual + the partials every rank sent (rank
     // order), from xbuf[par]; this CTA stores its share of the new X in
@@ -538,8 +615,29 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       const int i = tid + k * kThreads;
       xv[k] = wv[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i < n4) {
-        xv[k] = embed ? reinterpret_cast<const float4 *>(xn)[i] : __ldcg(xs4 + i);
         wv[k] = __ldg(w4 + i);
+        if (!(dfi && !embed)) xv[k] = embed ? reinterpret_cast<const float4 *>(xn)[i] : __ldcg(xs4 + i);
+      }
+    }
+    if (dfi && !embed) {  // the residual of the previous phase, as tagged words (via xn)
+      if (!poll_to_smem(P.tX, cols, xn, nullptr, 0, nullptr, nullptr, 0, nullptr, tag_in, &st->err)) s_fail = 1;
+      csync();
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (tid + k * kThreads < n4) xv[k] = reinterpret_cast<const float4 *>(xn)[tid + k * kThreads];
+      if (ph.kind == K_LOGITS) {  // the forward's commit: SeqLen, TokenIDs, the stop flag
+        if (tid == 0) {
+          uint32_t bits = 0;
+          if (!poll_tag1(P.tsel + 1, tag_in, bits, &st->err)) s_fail = 1;
+          fence_gpu();
+          s_tok = ldst(&st->halted);
+        }
+        csync();
+        if (s_tok) {  // the stop token was forwarded: a normal end
+          *s_halt = 1;
+          return true;
+        }
+        read_window();
       }
     }
     if (reduce) {  // the exchange this phase follows is number xb
@@ -606,15 +704,28 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       build_q8k(xn, cols, q8qs, q8d, q8bs);
     }
   } else {
+    // o-proj: the attention output; down: the SwiGLU output
+    const unsigned long long *tin = ph.kind == K_OPROJ ? P.tatt : P.th;
     if (ph.need_f32) {
       const float4 *x4 = reinterpret_cast<const float4 *>(ph.x_in);
+      if (dfi) {  // via xn (cols <= H)
+        if (!poll_to_smem(tin, cols, xn, nullptr, 0, nullptr, nullptr, 0, nullptr, tag_in, &st->err)) s_fail = 1;
+        csync();
+        x4 = reinterpret_cast<const float4 *>(xn);
+      }
       for (int i0 = 0; i0 < n4; i0 += kThreads) {
         const int i = i0 + tid;
-        const float4 v = i < n4 ? __ldcg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 v = i < n4 ? (dfi ? x4[i] : __ldcg(x4 + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
         put_limbs(v, i, i < n4, la, lb, lc, ls, nb);
       }
     }
-    if (ph.need_q8k) build_q8k_global(ph.x_in, cols, q8qs, q8d, q8bs);
+    if (ph.need_q8k) {
+      if (dfi) {
+        if (!build_q8k_tagged(tin, tag_in, cols, q8qs, q8d, q8bs, &st->err)) s_fail = 1;
+      } else {
+        build_q8k_global(ph.x_in, cols, q8qs, q8d, q8bs);
+      }
+    }
   }
   csync();
   if (tr) tr[1] = globaltimer_ns();
@@ -692,8 +803,13 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
   if (ph.kind == K_QKV) {
 #pragma unroll
     for (int s = 0; s < kMaxSegs; ++s)
-      if (s < ph.nseg && R.r0[s] + tid < R.r1[s])
-        ph.seg[s].out[R.r0[s] + tid] = __fadd_rn(ybuf[s * P.yrows + tid], bias[s]);
+      if (s < ph.nseg && R.r0[s] + tid < R.r1[s]) {
+        const float v = __fadd_rn(ybuf[s * P.yrows + tid], bias[s]);
+        if (DF)
+          st_tag((s == 0 ? P.tq : s == 1 ? P.tk : P.tv) + R.r0[s] + tid, tag_out, v);
+        else
+          ph.seg[s].out[R.r0[s] + tid] = v;
+      }
   } else if (residual) {
     if (ll) {  // partial rows to every rank, tagged as exchange xb + 1 (summed by the next normed phase)
       const int par = ph.kind == K_OPROJ ? 0 : 1;
@@ -703,15 +819,25 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
         for (int r = 0; r < P.world; ++r) st_tagged(P.peer_recv[r] + at, xb + 1, v);
       }
     } else if (R.r0[0] + tid < R.r1[0]) {
-      P.X[R.r0[0] + tid] = __fadd_rn(xres, ybuf[tid]);
+      const float v = __fadd_rn(xres, ybuf[tid]);
+      P.X[R.r0[0] + tid] = v;
+      if (DF) st_tag(P.tX + R.r0[0] + tid, tag_out, v);
     }
-    if (ph.kind == K_FFN_DOWN && ph.commit_here && c == 0 && tid == 0 && ldst(&st->commit)) {
-      const int pos = ldst(&st->fwd_pos);
-      if (pos >= 0 && pos < st->out_cap) P.token_ids[pos] = ldst(&st->fwd_token);  // KVCache.StoreTokenID
-      st->seq_len = pos + 1;
-      if (ldst(&st->halt_pending)) {
-        st->halted = 1;
-        st->halt_pending = 0;
+    if (ph.kind == K_FFN_DOWN && ph.commit_here && c == 0 && tid == 0) {
+      if (ldst(&st->commit)) {
+        const int pos = ldst(&st->fwd_pos);
+        if (pos >= 0 && pos < st->out_cap) P.token_ids[pos] = ldst(&st->fwd_token);  // KVCache.StoreTokenID
+        st->seq_len = pos + 1;
+        if (ldst(&st->halt_pending)) {
+          st->halted = 1;
+          st->halt_pending = 0;
+        }
+      }
+      // bench rewind: SeqLen returns to the prompt every rewind_period steps
+      if (P.rewind_period > 0 && (step + 1) % P.rewind_period == 0) st->seq_len = P.rewind_base;
+      if (DF) {  // publish the commit (and the state above) to the next logits phase
+        fence_gpu();
+        st_tag(P.tsel + 1, tag_out, 0.f);
       }
     }
   } else if (ph.kind == K_FFN_UP) {
@@ -719,7 +845,11 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
     if (R.r0[0] + tid < R.r1[0]) {
       const double g = static_cast<double>(ybuf[tid]);
       const float silu = static_cast<float>(g / (1.0 + exp(-g)));
-      P.h[R.r0[0] + tid] = __fmul_rn(silu, ybuf[P.yrows + tid]);
+      const float v = __fmul_rn(silu, ybuf[P.yrows + tid]);
+      if (DF)
+        st_tag(P.th + R.r0[0] + tid, tag_out, v);
+      else
+        P.h[R.r0[0] + tid] = v;
     }
   } else if (ph.kind == K_LOGITS) {
     const int lo = R.r0[0], n = R.r1[0] - lo;
@@ -875,11 +1005,18 @@ __device__ bool p_matvec(const PParams &P, const PPhase &ph, uint8_t *smem, uint
       st->commit = 1;
       if (st->stop_on_special && (best_i == st->im_end || best_i == st->eos)) st->halt_pending = 1;
       st->logits_counter = 0;
+      if (DF) {  // publish the selection (and the state above) to the next forward
+        fence_gpu();
+        st_tag(P.tsel, tag_out, __int_as_float(best_i));
+      }
     }
   }
   return true;
 }
 
+// DF: the one-GPU dataflow specialisation (PParams::df); otherwise grid
+// barriers between phases and the tensor-parallel exchanges.
+template <bool DF>
 __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[kWarps][kWarps];
@@ -889,6 +1026,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   __shared__ PPhase s_ph, s_pph;  // current phase: compute side / producer side
   __shared__ int s_pos;           // position forwarded by the current step
   __shared__ float s_rope[256];   // its RoPE row: cos[hd/2], sin[hd/2]
+  __shared__ unsigned s_cbase[64];  // dataflow: split arrivals counted so far per attention unit
+  __shared__ int s_halt;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + P.off_full);
   uint64_t *empty = reinterpret_cast<uint64_t *>(smem + P.off_empty);
   uint64_t *abar = reinterpret_cast<uint64_t *>(smem + P.off_abar);
@@ -902,8 +1041,9 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
     for (int i = 0; i < kAttnBufs; ++i) mbar_init(&abar[i], 1);
     fence_mbar_init();
     // split arrivals start from zero (a launch that stopped on an error may
-    // have left counts); the first attention phase follows a grid barrier
-    if (c < 64) st->attn_counter[c] = 0;
+    // have left counts); the first attention phase follows a grid barrier.
+    // Dataflow: no barrier orders this store, so the host clears them.
+    if (!DF && c < 64) st->attn_counter[c] = 0;
     s_stop = 0;
   }
   __syncthreads();
@@ -983,6 +1123,8 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
   bool crossed = false;  // the previous phase ended with a cross-GPU barrier
   int last_kind = -1;    // kind of the last phase completed
   if (tid == 0) s_pos = ldst(&st->fwd_pos);  // the forward's position when phase0 == 1
+  if (tid < 64) s_cbase[tid] = 0;
+  if (tid == 0) s_halt = 0;
   if (tid < P.hd && P.phase0 == 1) {
     const int pos0 = ldst(&st->fwd_pos), half = P.hd / 2;
     if (pos0 >= 0 && pos0 < P.rope_len)
@@ -996,12 +1138,15 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
       csync();
       const PPhase &ph = s_ph;
       const long long b0 = P.trace ? clock64() : 0;
-      if (kp > 0 && !(crossed && pi != 0)) {
+      if (kp > 0 && !DF && !(crossed && pi != 0)) {
         bar_target += 1;
         if (!grid_barrier(P.gbar, bar_target, &st->err, &s_ok)) { ok = false; break; }
       }
       crossed = false;
-      if (pi == 0 && ldst(&st->halted)) break;  // stop token forwarded: a normal end
+      // stop token forwarded: a normal end (dataflow: the logits phase reads
+      // the flag once the forward's commit is published)
+      if (pi == 0 && (!DF || kp == 0) && ldst(&st->halted)) break;
+      const unsigned tag_in = P.tag0 + static_cast<unsigned>(kp), tag_out = tag_in + 1u;
       unsigned long long *tr =
           (P.trace && tid == 0)
               ? P.trace + (static_cast<size_t>(kp) * G + c) * kTraceFields
@@ -1013,33 +1158,40 @@ __global__ void __launch_bounds__(kPThreads, 1) k_persistent(const PParams P) {
         tr[7] = static_cast<unsigned long long>(b1);
       }
       if (ph.kind == K_ATTN) {
-        if (!p_attention(P, ph, reinterpret_cast<float *>(smem + P.off_act), abar, abar_uses, c, s_pos, s_rope)) {
+        if (!p_attention<DF>(P, ph, reinterpret_cast<float *>(smem + P.off_act), abar, abar_uses, c, s_pos, s_rope,
+                         tag_in, tag_out, s_cbase)) {
           ok = false;
           break;
+        }
+        if (DF && s_pos >= 0 && s_pos < P.max_tokens) {
+          // every unit's splits arrived once each when there was more than
+          // one (the layout is the same on every CTA)
+          csync();
+          const AttnLayout AL = attn_layout(s_pos, P.split_len, P.n_kv, P.tp_h1 - P.tp_h0, G);
+          if (AL.nsplit > 1 && tid < (AL.per_head ? P.tp_h1 - P.tp_h0 : P.n_kv))
+            s_cbase[tid] += static_cast<unsigned>(AL.nsplit);
         }
       } else {
-        if (!p_matvec(P, ph, smem, k_ring, red, scratch, &s_flag, &s_pos, s_rope, tr, xb, kp == 0)) {
+        if (!p_matvec<DF>(P, ph, smem, k_ring, red, scratch, &s_flag, &s_pos, s_rope, tr, xb, kp == 0, tag_in, tag_out,
+                      step, &s_halt)) {
           ok = false;
           break;
         }
+        if (s_halt) break;
       }
       csync();
       if (tr) tr[3] = globaltimer_ns();
-      // bench rewind: the down phase of the last layer set SeqLen = pos + 1
-      if (ph.kind == K_FFN_DOWN && ph.commit_here && P.rewind_period > 0 && c == 0 && tid == 0 &&
-          (step + 1) % P.rewind_period == 0)
-        st->seq_len = P.rewind_base;
       // tensor parallel: o-proj / down sent exchange xb + 1; the next phase
       // polls its tagged words instead of waiting at a grid barrier (except
       // logits, which reads the state the down phase committed)
-      if (P.ll && (ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN)) {
+      if (!DF && P.ll && (ph.kind == K_OPROJ || ph.kind == K_FFN_DOWN)) {
         xb += 1;
         crossed = true;
       }
       last_kind = ph.kind;
     }
   }
-  if (P.ll && ok && last_kind == K_FFN_DOWN) {
+  if (!DF && P.ll && ok && last_kind == K_FFN_DOWN) {
     // the launch ends after a forward: leave its residual in X for the
     // per-phase kernels and the next launch (X = xbuf[1] + the down partials)
     const int n4 = P.H / 4;

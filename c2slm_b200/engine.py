@@ -58,6 +58,7 @@ SIGNATURES = {
     "c2s_gemv": (I, [I, P, P, P, I, I]),
     "c2s_gemv_noalloc": (I, [I, P, P, P, I, I]),
     "c2s_gemv_device": (I, [I, I, P, P, P, I, I]),
+    "c2s_bench_gemv": (I, [I, I, P, C.c_size_t, I, P, P, I, I, I, C.POINTER(F)]),
     "c2s_kquant_partials": (I, [I, P, P, P, I, I]),
     "c2s_dot_rows_f32x": (I, [I, P, P, P, I, P, I, I]),
     "c2s_rmsnorm": (I, [P, P, P, I, F]),
@@ -149,6 +150,16 @@ def gemv_noalloc(kind: int, w, x, rows: int, cols: int) -> np.ndarray:
     y = np.zeros(rows, np.float32)
     _check(load_library().c2s_gemv_noalloc(kind, _ptr(w), _ptr(x), _ptr(y), rows, cols))
     return y
+
+
+def bench_gemv(device: int, kind: int, d_weight: int, copy_stride: int, n_copies: int, d_x: int, d_y: int,
+               rows: int, cols: int, reps: int) -> float:
+    """Device time (ms) of `reps` back-to-back matvecs on device pointers,
+    launch i on weight copy i % n_copies (c2s_bench_gemv)."""
+    ms = C.c_float(0.0)
+    _check(load_library().c2s_bench_gemv(device, kind, C.c_void_p(d_weight), copy_stride, n_copies,
+                                         C.c_void_p(d_x), C.c_void_p(d_y), rows, cols, reps, C.byref(ms)))
+    return float(ms.value)
 
 
 def kquant_partials(kind: int, w, x, rows: int, cols: int) -> np.ndarray:

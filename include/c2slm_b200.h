@@ -220,6 +220,17 @@ int c2s_gemv(int type, const void *weight, const float *x, float *y, int rows, i
 int c2s_gemv_device(int device, int type, const void *d_weight, const float *d_x, float *d_y,
                     int rows, int cols);
 
+/* Single-op benchmark of c2s_gemv_device (config 0 of the bench): `reps`
+ * launches back to back on the library's stream for `device`, launch i on
+ * weight copy i % n_copies (copy k at d_weight + k * copy_stride bytes; one
+ * copy stays L2-resident, many copies stream from HBM), captured in a CUDA
+ * graph of up to 1000 launches and timed with CUDA events after one untimed
+ * replay.  reps: a multiple of 1000, or at most 4000.  *ms_out = device time
+ * of the `reps` launches.  The reference times GEMVQ4_K_Q8_K on the host
+ * (tensor/ops_test.go:143-156). */
+int c2s_bench_gemv(int device, int type, const void *d_weight, size_t copy_stride, int n_copies,
+                   const float *d_x, float *d_y, int rows, int cols, int reps, float *ms_out);
+
 /* c2s_gemv without any device allocation or free, for callers that cannot
  * allocate when they need the matvec (device memory held by another
  * allocator; loops that must not take cudaFree's device-wide
