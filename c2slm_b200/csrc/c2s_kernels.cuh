@@ -147,178 +147,47 @@ __device__ __forceinline__ float blockdot_q5_0_reg(const uint8_t *blk, const flo
   return d * ((a0 + a1) + (a2 + a3));
 }
 
-// Q8_0 block (int8 weights) . limb-split x
-__device__ __forceinline__ float blockdot_q8_0_limbs(const uint8_t *blk, const XLimbs &L) {
-  const float d = h2f(ld16(blk));
-  int A = 0, B = 0, C = 0;
-#pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    const int w = static_cast<int>(ld32u(blk + 2 + 4 * t));
-    A = __dp4a(w, L.a[t], A);
-    B = __dp4a(w, L.b[t], B);
-    C = __dp4a(w, L.c[t], C);
-  }
-  return d * limbs_combine(A, B, C, L.s);
-}
-
-// Q5_0 block . limb-split x: int8(u - 16) = nibble | (hbit ? 0 : 0xF0)
-__device__ __forceinline__ float blockdot_q5_0_limbs(const uint8_t *blk, const XLimbs &L) {
-  const float d = h2f(ld16(blk));
-  const uint32_t qh = static_cast<uint32_t>(ld16(blk + 2)) | (static_cast<uint32_t>(ld16(blk + 4)) << 16);
-  int A = 0, B = 0, C = 0;
-#pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const uint32_t w = ld32u(blk + 6 + 4 * t);
-    const uint32_t hl = spread4((qh >> (4 * t)) & 0xFu) ^ 0x01010101u;
-    const uint32_t hh = spread4((qh >> (16 + 4 * t)) & 0xFu) ^ 0x01010101u;
-    const int lo = static_cast<int>((w & 0x0F0F0F0Fu) | (hl * 0xF0u));
-    const int hi = static_cast<int>(((w >> 4) & 0x0F0F0F0Fu) | (hh * 0xF0u));
-    A = __dp4a(lo, L.a[t], A);
-    B = __dp4a(lo, L.b[t], B);
-    C = __dp4a(lo, L.c[t], C);
-    A = __dp4a(hi, L.a[4 + t], A);
-    B = __dp4a(hi, L.b[4 + t], B);
-    C = __dp4a(hi, L.c[4 + t], C);
-  }
-  return d * limbs_combine(A, B, C, L.s);
-}
-
-// One warp's partial over units u = u0 + lane + k*ustep of one row (K-quants
-// and the generic f32 path).  All lanes must call it (Q6_K shuffles).
+// K-quant rows of one staged chunk with their integer partials recorded in
+// P.dbg (c2s_kquant_partials, the bit-exact contract): warp w takes rows w,
+// w + kWarps, ...; lanes take the row's 64-value units (unit_q4k /
+// unit_q6k_isum, the same integer arithmetic as the warp-row core).
 template <int TYPE>
-__device__ __forceinline__ float row_units(const MatParams &P, const uint8_t *row, int grow, bool rowok, int u0,
-                                           int ustep, int U, const float *xt, int nbx, const Q8KView &q8) {
-  const int lane = threadIdx.x & 31;
-  float acc = 0.f;
-  for (int ub = u0; ub < U; ub += ustep) {
-    const int u = ub + lane;
-    const bool ok = rowok && u < U;
-    if (TYPE == T_Q4_K) {
-      if (ok) {
-        int lo, hi;
-        const int sbi = u >> 2, j = u & 3;
-        acc += unit_q4k(row + sbi * 144, sbi, j, q8, lo, hi);
-        if (P.dbg) {
+__device__ __forceinline__ void dbg_chunk_t(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
+                                            int grow0, const Q8KView &q8, float *y) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int U = S.units;
+  for (int r = warp; r < nr; r += kWarps) {
+    const uint8_t *row = rows_smem + static_cast<size_t>(r) * S.row_bytes;
+    const int grow = grow0 + r;
+    float acc = 0.f;
+    for (int ub = 0; ub < U; ub += 32) {
+      const int u = ub + lane;
+      const bool ok = u < U;
+      if (TYPE == T_Q4_K) {
+        if (ok) {
+          int lo, hi;
+          const int sbi = u >> 2, j = u & 3;
+          acc += unit_q4k(row + sbi * 144, sbi, j, q8, lo, hi);
           int32_t *dst = P.dbg + (static_cast<size_t>(grow) * (U >> 2) + sbi) * 8 + 2 * j;
           dst[0] = lo;
           dst[1] = hi;
         }
-      }
-    } else if (TYPE == T_Q6_K) {
-      int is = 0;
-      const int sbi = u >> 2;
-      if (ok) is = unit_q6k_isum(row + sbi * 210, sbi, (u >> 1) & 1, u & 1, q8);
-      is += __shfl_xor_sync(0xffffffffu, is, 1);
-      is += __shfl_xor_sync(0xffffffffu, is, 2);
-      if (ok && (u & 3) == 0) {
-        const float d6 = h2f(ld16(row + sbi * 210 + 208));
-        acc += __fmul_rn(static_cast<float>(is), __fmul_rn(d6, q8.d[sbi]));
-        if (P.dbg) P.dbg[static_cast<size_t>(grow) * (U >> 2) + sbi] = is;
-      }
-    } else if (TYPE == T_Q5_0) {
-      if (ok) acc += unit_q5_0(row + u * 22, xt + u, nbx);
-    } else if (TYPE == T_Q8_0) {
-      if (ok) acc += unit_q8_0(row + u * 34, xt + u, nbx);
-    }
-  }
-  return acc;
-}
-
-// Rows of one staged chunk -> y[0..nr).  Few wide rows: several warps per
-// row, partials combined in a fixed order.  Otherwise one warp per row with
-// no block-level barrier.  f32-activation types with <= 32 blocks per row use
-// the x values each lane holds in registers (xr, block = lane).
-template <int TYPE>
-__device__ __forceinline__ void compute_chunk_t(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
-                                                int grow0, const float *xt, int nbx, const Q8KView &q8, float *y,
-                                                float (*red)[kWarps], const XLimbs &xl, bool xreg) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int U = S.units;
-  if ((TYPE == T_Q5_0 || TYPE == T_Q8_0) && xreg) {
-    // lane = block; two rows per round for instruction-level parallelism
-    const int bsz = TYPE == T_Q8_0 ? 34 : 22;
-    int r = warp;
-    for (; r + kWarps < nr; r += 2 * kWarps) {
-      const uint8_t *r0 = rows_smem + static_cast<size_t>(r) * S.row_bytes + lane * bsz;
-      const uint8_t *r1 = r0 + static_cast<size_t>(kWarps) * S.row_bytes;
-      float a0 = 0.f, a1 = 0.f;
-      if (lane < U) {
-        a0 = TYPE == T_Q8_0 ? blockdot_q8_0_limbs(r0, xl) : blockdot_q5_0_limbs(r0, xl);
-        a1 = TYPE == T_Q8_0 ? blockdot_q8_0_limbs(r1, xl) : blockdot_q5_0_limbs(r1, xl);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
-      }
-      if (lane == 0) {
-        y[r] = a0;
-        y[r + kWarps] = a1;
+      } else {
+        int is = 0;
+        const int sbi = u >> 2;
+        if (ok) is = unit_q6k_isum(row + sbi * 210, sbi, (u >> 1) & 1, u & 1, q8);
+        is += __shfl_xor_sync(0xffffffffu, is, 1);
+        is += __shfl_xor_sync(0xffffffffu, is, 2);
+        if (ok && (u & 3) == 0) {
+          const float d6 = h2f(ld16(row + sbi * 210 + 208));
+          acc += __fmul_rn(static_cast<float>(is), __fmul_rn(d6, q8.d[sbi]));
+          P.dbg[static_cast<size_t>(grow) * (U >> 2) + sbi] = is;
+        }
       }
     }
-    if (r < nr) {
-      const uint8_t *r0 = rows_smem + static_cast<size_t>(r) * S.row_bytes + lane * bsz;
-      float a0 = 0.f;
-      if (lane < U) a0 = TYPE == T_Q8_0 ? blockdot_q8_0_limbs(r0, xl) : blockdot_q5_0_limbs(r0, xl);
-      a0 = warp_sum(a0);
-      if (lane == 0) y[r] = a0;
-    }
-    return;
-  }
-  int wpr = 1;
-  if (nr < kWarps) {
-    const int want = kWarps / nr;
-    const int cap = (U + 31) / 32;
-    while (wpr * 2 <= want && wpr * 2 <= cap) wpr *= 2;
-  }
-  if (wpr == 1) {
-    for (int r = warp; r < nr; r += kWarps) {
-      const uint8_t *row = rows_smem + static_cast<size_t>(r) * S.row_bytes;
-      float acc = row_units<TYPE>(P, row, grow0 + r, true, 0, 32, U, xt, nbx, q8);
-      acc = warp_sum(acc);
-      if (lane == 0) y[r] = acc;
-    }
-    return;
-  }
-  const int rows_per_pass = kWarps / wpr;
-  const int sub = warp % wpr;
-  for (int rb = 0; rb < nr; rb += rows_per_pass) {
-    const int r = rb + warp / wpr;
-    const bool rowok = r < nr;
-    const uint8_t *row = rows_smem + static_cast<size_t>(rowok ? r : 0) * S.row_bytes;
-    float acc = row_units<TYPE>(P, row, grow0 + r, rowok, sub * 32, wpr * 32, U, xt, nbx, q8);
     acc = warp_sum(acc);
-    if (lane == 0 && rowok) red[r - rb][sub] = acc;
-    csync();
-    if (threadIdx.x < rows_per_pass && rb + static_cast<int>(threadIdx.x) < nr) {
-      const int rr = rb + threadIdx.x;
-      float sum = 0.f;
-      for (int k = 0; k < wpr; ++k) sum += red[rr - rb][k];
-      y[rr] = sum;
-    }
-    csync();
+    if (lane == 0) y[r] = acc;
   }
-}
-
-__device__ __forceinline__ void compute_chunk(const MatParams &P, const Seg &S, const uint8_t *rows_smem, int nr,
-                                              int grow0, const float *xt, int nbx, const Q8KView &q8, float *y,
-                                              float (*red)[kWarps], const XLimbs &xl, bool xreg) {
-  switch (S.type) {
-    case T_Q4_K: compute_chunk_t<T_Q4_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
-    case T_Q6_K: compute_chunk_t<T_Q6_K>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
-    case T_Q5_0: compute_chunk_t<T_Q5_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
-    case T_Q8_0: compute_chunk_t<T_Q8_0>(P, S, rows_smem, nr, grow0, xt, nbx, q8, y, red, xl, xreg); break;
-    default: break;
-  }
-}
-
-// this lane's block (block = lane) of the transposed f32 activation -> limbs
-__device__ __forceinline__ void lane_limbs(const float *xt, int nbx, XLimbs &xl) {
-  const int lane = threadIdx.x & 31;
-  float xr[32];
-#pragma unroll
-  for (int k = 0; k < 32; ++k) xr[k] = lane < nbx ? xt[k * nbx + lane] : 0.f;
-  make_limbs(xr, xl);
 }
 
 // Loads n floats (n % 4 == 0, 16-B aligned) from global into shared memory,
@@ -513,8 +382,10 @@ __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
       float *y = ybuf + ch.seg * P.ybuf_rows + (ch.r0 - my0[ch.seg]);
       const int nr = ch.r1 - ch.r0, warp = tid >> 5;
       if (P.dbg) {  // integer partials of the K-quant dots (bit-exact contract)
-        XLimbs none{};
-        compute_chunk(P, S, rows, nr, ch.r0, nullptr, nbx, q8, y, red, none, false);
+        if (S.type == T_Q4_K)
+          dbg_chunk_t<T_Q4_K>(P, S, rows, nr, ch.r0, q8, y);
+        else if (S.type == T_Q6_K)
+          dbg_chunk_t<T_Q6_K>(P, S, rows, nr, ch.r0, q8, y);
       } else if (warp < nr) {
         const int cnt = (nr - warp + kWarps - 1) / kWarps;
         switch (S.type) {

@@ -398,3 +398,57 @@ def test_prefill_suffix_and_rewind_match_token_by_token(model_cache, monkeypatch
     assert rel(t[0], r[0]) <= TOL and rel(t[2], r[2]) <= TOL
     assert rel(t[5], r[5]) <= 1e-5  # a layer-0 row the rewound ingest rewrote
     assert t[6][0] == r[6][0]
+
+
+def _long_context_case(name):
+    import json
+    import os
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "long_context.json")
+    if not os.path.exists(p):
+        pytest.skip("tests/golden/long_context.json not generated")
+    return json.load(open(p))[name]
+
+
+@pytest.mark.slow
+def test_attention_over_4096_positions_against_the_oracle(model_cache):
+    """The 7B shape (2 layers) after a 4096-token IngestFrom, against the CPU
+    oracle's committed results (tests/golden/make_long_context_fixtures.py):
+    the last NormX, then greedy decode at positions 4096.. whose attention
+    covers 33 position splits per kv head, with the tolerance-tie rule."""
+    c = _long_context_case("attn4096")
+    path = synth.cached_model(c["model"], layers=c["layers"], cache_dir=model_cache)
+    prompt = np.random.default_rng(c["seed"]).integers(0, 151643, c["n"]).astype(np.int32)
+    with K.Engine(path, max_tokens=c["max_tokens"]) as e:
+        nx = e.ingest_from(0, prompt)
+        assert rel(nx, c["normx"]) <= TOL, rel(nx, c["normx"])
+        got = e.generate(c["gen"], stop_on_special=False)
+    ones = np.ones(len(c["ids"]))
+    assert_greedy_parity(got, c["ids"], np.array(c["rel_margin"]), ones, len(c["ids"]))
+
+
+@pytest.mark.slow
+def test_prefill_2048_tokens_against_the_oracle(model_cache):
+    """IngestFrom of a 2048-token prompt through the tensor-core prefill (two
+    1024-token chunks, the second attending to the first) against the CPU
+    oracle's token-by-token results: the last NormX, the K/V cache rows at
+    positions 0, 1024 and 2047 of both layers, and the first greedy ids."""
+    c = _long_context_case("prefill2048")
+    path = synth.cached_model(c["model"], layers=c["layers"], cache_dir=model_cache)
+    prompt = np.random.default_rng(c["seed"]).integers(0, 151643, c["n"]).astype(np.int32)
+    with K.Engine(path, max_tokens=c["max_tokens"]) as e:
+        nx = e.ingest_from(0, prompt)
+        assert rel(nx, c["normx"]) <= TOL, rel(nx, c["normx"])
+        errs = []
+        for r in c["kv"]:
+            ek = rel(e.get_key(r["layer"], r["kv_head"], r["pos"]), r["k"])
+            ev = rel(e.get_value(r["layer"], r["kv_head"], r["pos"]), r["v"])
+            errs.append(max(ek, ev))
+            if r["layer"] == 0:  # identical Q8_K activations: only the f32 order of the K-quant sums differs
+                assert max(ek, ev) <= 1e-5, (r["pos"], ek, ev)
+        print(f"prefill 2048 vs oracle: normx {rel(nx, c['normx']):.2e}, kv rows {['%.1e' % x for x in errs]}")
+        # layer 1 rows see layer 0's residual, which a Q8_K byte moved by a
+        # last-bit difference can shift by one quantisation step
+        assert np.median(errs) <= 1e-4 and max(errs) <= 1e-2
+        got = e.generate(c["gen"], stop_on_special=False)
+    ones = np.ones(len(c["ids"]))
+    assert_greedy_parity(got, c["ids"], np.array(c["rel_margin"]), ones, len(c["ids"]))

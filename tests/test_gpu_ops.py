@@ -136,3 +136,38 @@ def test_argument_errors_are_reported():
         K.gemv(O.Q4_K, b"\0" * 144, np.zeros(300, np.float32), 1, 300)  # cols % 256
     with pytest.raises(K.C2SError):
         K.quantize_row_q8_k(np.zeros(100, np.float32))
+
+
+@pytest.mark.parametrize("kind", [O.Q5_0, O.Q8_0])
+def test_f32x_blocks_with_high_dynamic_range(rng, kind):
+    """tensor/ops.go:40-95 multiplies the f32 activation itself; the GPU splits
+    each 32-value block of x into three int8 limbs scaled by the block's
+    max|x| (error <= 6.2e-8 * max|x| per element), so small elements beside a
+    large one keep less relative precision.  Blocks whose elements span
+    1e-4 .. 1e4 in magnitude (one 1e4 element per block, the rest
+    log-uniform), against the exact (float64) dot of the dequantised row:
+      * the GPU's error is within 5e-7 of the dot's scale sum_j |w_ij x_j|
+        (the reference's own sequential f32 sums are off by up to ~1e-7 of
+        it here, and by up to 1e-4 of outputs that cancel -- so a per-output
+        relative bar against the reference would measure the reference);
+      * the GPU is no less accurate than the reference on any output, up
+        to 1e-7 of the scale;
+      * GPU and oracle agree within the suite's 1e-5 of max|out|."""
+    rows, cols = 512, 896
+    w = synth.gen_blocks(rng, kind, rows, cols)
+    sign = np.where(rng.random(cols) < 0.5, -1.0, 1.0)
+    x = (sign * 10.0 ** rng.uniform(-4, 4, cols)).astype(np.float32)
+    x[::32] = (1e4 * sign[::32]).astype(np.float32)
+    got = K.gemv(kind, w, x, rows, cols).astype(np.float64)
+    want = O.gemv(kind, w, x, rows, cols).astype(np.float64)
+    rb = w.size // rows
+    wd = np.stack([O.dequant_row(kind, w[r * rb:(r + 1) * rb], cols) for r in range(rows)]).astype(np.float64)
+    exact = wd @ x.astype(np.float64)
+    scale = np.abs(wd) @ np.abs(x.astype(np.float64))
+    e_gpu = np.abs(got - exact) / scale
+    e_ref = np.abs(want - exact) / scale
+    print(f"high-dynamic-range {kind}: |gpu-exact|/scale max {e_gpu.max():.2e}, "
+          f"|reference-exact|/scale max {e_ref.max():.2e}")
+    assert e_gpu.max() <= 5e-7
+    assert np.all(e_gpu <= e_ref + 1e-7)
+    assert maxabs_rel(got, want) <= 1e-5

@@ -125,3 +125,21 @@ def test_generate_stops_after_forwarding_special(tiny):
             assert toks[-1] in (m.info.im_end, m.info.eos)
         assert m.seq_len == 3 + len(toks)
         assert np.array_equal(m.token_ids(m.seq_len)[3:], toks)
+
+
+def test_greedy_fixture_is_reproduced_by_the_oracle(model_cache):
+    """tests/golden/greedy_qwen05b.json (made by make_greedy_fixtures.py) is
+    what the oracle computes: prompt 0's first 8 greedy ids and margins."""
+    import json
+    import os
+    from c2slm_b200 import synth
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "greedy_qwen05b.json")
+    fx = json.load(open(p))
+    path = synth.cached_model(fx["model"], cache_dir=model_cache)
+    pr = fx["prompts"][0]
+    prompt = np.random.default_rng(fx["seed_base"] + pr["seed"]).integers(0, 151643, fx["plen"]).astype(np.int32)
+    with O.OracleModel(path, max_tokens=fx["plen"] + 16, nthreads=os.cpu_count() or 1) as o:
+        nx = o.ingest_from(0, prompt)
+        ids, m, mx = o.generate(nx, 8, penalty=fx["penalty"], window=fx["window"], stop_on_special=False)
+    assert list(ids) == pr["ids"][:8]
+    np.testing.assert_allclose(m / mx, pr["rel_margin"][:8], rtol=1e-3)
