@@ -246,25 +246,6 @@ def test_qwen05b_config1_parity_within_reference_build_envelope(model_cache):
 
 
 @pytest.mark.slow
-def test_qwen05b_config1_greedy_free_running(model_cache):
-    """Free-running greedy ids (the reference's generate loop on both sides).
-    Reported, not bounded beyond the first step: the trajectory is chaotic
-    under the reference's Q8_K activation quantisation (its own AVX2 build
-    leaves its scalar build's sequence at step 36 on this prompt); the
-    per-step envelope test above is the parity bar."""
-    path = synth.cached_model("qwen05b", cache_dir=model_cache)
-    with K.Engine(path, max_tokens=512) as e, O.OracleModel(path, max_tokens=512, nthreads=8) as o:
-        prompt = np.random.default_rng(0).integers(0, 151643, 32).astype(np.int32)
-        e.ingest_from(0, prompt)
-        nx_o = o.ingest_from(0, prompt)
-        got = e.generate(64, stop_on_special=False)
-        want, m, mx = o.generate(nx_o, 64, stop_on_special=False)
-        same = next((i for i in range(64) if got[i] != want[i]), 64)
-        print(f"identical greedy steps: {same}")
-        assert same >= 1
-
-
-@pytest.mark.slow
 @pytest.mark.parametrize("name", ["qwen15b", "qwen7b"])
 def test_large_shapes_reduced_depth(model_cache, name):
     """BASELINE configs 2 and 3 at full width, 2 layers (oracle time bound)."""
