@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", default="qwen05b")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder depth of the headline model (profiling captures of a shallower copy)")
     ap.add_argument("--profile-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp7b", action="store_true", help="skip the 7B tensor-parallel line (config 3)")
@@ -197,7 +199,7 @@ def run_reference(args) -> None:
     from c2slm_b200 import synth
     import numpy as np
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle")], check=True)
-    path = synth.cached_model(args.model)
+    path = synth.cached_model(args.model, layers=args.layers)
     prompt = np.random.default_rng(0).integers(0, 151643, PROMPT).astype(np.int32)
     threads = min(os.cpu_count() or 1, 32)  # engine/pool.go:47-53
     max_steps = min(args.steps, 256)
@@ -248,9 +250,9 @@ def run_ours(args) -> None:
         return float(t.item())
 
     if rank == 0:
-        path = synth.cached_model(args.model)
+        path = synth.cached_model(args.model, layers=args.layers)
     barrier()
-    path = synth.cached_model(args.model)
+    path = synth.cached_model(args.model, layers=args.layers)
     eng = K.Engine(path, device=local, max_tokens=1024)
     prompt = np.random.default_rng(rank).integers(0, 151643, PROMPT).astype(np.int32)
     eng.ingest_from(0, prompt)
