@@ -924,8 +924,12 @@ int persistent_setup(c2s_engine *e) {
   const size_t at_act = attn_smem_bytes(hd, qpk);
   const size_t act = a16(std::max(mv_act, at_act));
   const size_t budget = 227 * 1024 - 8192;  // dynamic smem; static smem of the kernel is < 8 KB
-  // weight ring: a few large slots (each warp consumes many rows per slot)
-  int slot_kb = 48;
+  // weight ring: a few large slots (each warp consumes many rows per slot).
+  // Measured: three 48 KB slots with one warp group at the 0.5B / 1.5B
+  // widths; 32 KB slots with two groups where phases have hundreds of rows
+  // per CTA (the 7B width, F > 12288: 2.89 vs 2.97 ms per step)
+  const bool wide = F > 12288;
+  int slot_kb = wide ? 32 : 48;
   if (const char *sk = getenv("C2S_SLOT_KB")) slot_kb = std::max(8, std::min(96, atoi(sk)));
   size_t max_row = 0;
   for (auto &p : ph)
@@ -941,7 +945,7 @@ int persistent_setup(c2s_engine *e) {
   P.nslot = nslot;
   // warp groups of the many-row phases: each group holds one slot while it
   // computes, so fewer groups than slots leave slots to fill meanwhile
-  int lng = nslot >= 8 ? 3 : nslot >= 4 ? 2 : nslot >= 2 ? 1 : 0;
+  int lng = wide ? 1 : nslot >= 8 ? 3 : nslot >= 4 ? 2 : nslot >= 2 ? 1 : 0;
   if (const char *lg = getenv("C2S_LNG")) lng = atoi(lg);
   P.lng = ring_groups_log2(nslot, lng);
   P.slot_bytes = static_cast<int>(slot_bytes);

@@ -433,3 +433,22 @@ def test_prefill_2048_tokens_against_the_oracle(model_cache):
         got = e.generate(c["gen"], stop_on_special=False)
     ones = np.ones(len(c["ids"]))
     assert_greedy_parity(got, c["ids"], np.array(c["rel_margin"]), ones, len(c["ids"]))
+
+
+@pytest.mark.parametrize("ggml_type,nbytes_per", [(1, 2.0), (2, 18 / 32)])
+def test_f16_and_q4_0_projections_are_rejected(models, ggml_type, nbytes_per):
+    """F16 (type 1) and Q4_0 (type 2) tensors are sized by both GGUF readers
+    as gguf/reader.go:513-546 does, but the reference's DispatchGEMV
+    (engine/model.go:250-270) yields zero rows for them: the engine refuses
+    such a projection at creation (C2S_ERR_UNSUPPORTED) rather than build a
+    model that computes nothing."""
+    from c2slm_b200 import gguf
+    import c2slm_b200.engine as KE
+    with gguf.File(models["tiny05"]) as f:
+        ti = f.tensor_map["blk.0.attn_q.weight"]
+        cols, rows = int(ti.dimensions[0]), int(ti.dimensions[1])
+        ti.type = ggml_type
+        ti.data = memoryview(bytearray(int(rows * cols * nbytes_per)))
+        with pytest.raises(KE.C2SError) as exc:
+            K.Engine(gguf_file=f, max_tokens=64)
+    assert exc.value.code == -4 and f"type {ggml_type}" in str(exc.value)
