@@ -281,8 +281,11 @@ class Engine:
                 descs[i].dims[k] = v
             descs[i].data = arr.ctypes.data
             descs[i].nbytes = len(ti.data)
-        _check(load_library().c2s_engine_create(C.byref(d), descs, len(f.tensors), device, C.byref(h)))
-        self._keep = None
+        del arr  # no view of the caller's mapping outlives this call, even when it raises
+        try:
+            _check(load_library().c2s_engine_create(C.byref(d), descs, len(f.tensors), device, C.byref(h)))
+        finally:
+            self._keep = None
 
     # lifecycle -------------------------------------------------------------
     def close(self) -> None:

@@ -83,3 +83,19 @@ def test_ring_warp_groups_own_whole_slots(lib):
             # the largest count that keeps the property is the one used
             best = max(l for l in range(want + 1) if nslot % (1 << l) == 0)
             assert lng == best
+
+
+def test_failed_create_releases_the_callers_mapping(lib, model_cache):
+    """c2s_engine_create over tensors the caller keeps mapped (the cgo path):
+    when creation fails (here: no device, or a rejected tensor on a GPU box)
+    the binding keeps no view of the mapping, so the caller can close it."""
+    import c2slm_b200 as K
+    from c2slm_b200 import gguf, synth
+    path = synth.cached_model("tiny05", cache_dir=model_cache)
+    with gguf.File(path) as f:
+        ti = f.tensor_map["blk.0.attn_q.weight"]
+        ti.type = 1  # F16: sized by the reader, rejected by the engine
+        ti.data = memoryview(bytearray(int(ti.dimensions[0]) * int(ti.dimensions[1]) * 2))
+        with pytest.raises(K.C2SError) as exc:
+            K.Engine(gguf_file=f, max_tokens=64)
+    assert exc.value.code in (-2, -4)  # no CUDA device here; UNSUPPORTED on a GPU box
