@@ -925,11 +925,12 @@ int persistent_setup(c2s_engine *e) {
   const size_t act = a16(std::max(mv_act, at_act));
   const size_t budget = 227 * 1024 - 8192;  // dynamic smem; static smem of the kernel is < 8 KB
   // weight ring: a few large slots (each warp consumes many rows per slot).
-  // Measured: three 48 KB slots with one warp group at the 0.5B / 1.5B
-  // widths; 32 KB slots with two groups where phases have hundreds of rows
-  // per CTA (the 7B width, F > 12288: 2.89 vs 2.97 ms per step)
+  // Measured per step: three 48 KB slots with one warp group at the 0.5B
+  // width (F 4864); three 40 KB slots at the 1.5B width (F 8960: 1476 vs
+  // 1517 us); 32 KB slots with two groups where phases have hundreds of rows
+  // per CTA (the 7B width, F > 12288: 2.86 vs 2.96 ms)
   const bool wide = F > 12288;
-  int slot_kb = wide ? 32 : 48;
+  int slot_kb = wide ? 32 : F > 6144 ? 40 : 48;
   if (const char *sk = getenv("C2S_SLOT_KB")) slot_kb = std::max(8, std::min(96, atoi(sk)));
   size_t max_row = 0;
   for (auto &p : ph)
@@ -1067,7 +1068,7 @@ int launch_persistent(c2s_engine *e, int n_steps, int rewind_period, int rewind_
   P.n_steps = n_steps;
   P.rewind_period = rewind_period;
   P.rewind_base = rewind_base;
-  CK(cudaMemsetAsync(e->gbar, 0, 4 * static_cast<size_t>(e->num_sms), e->stream));
+  if (!P.df) CK(cudaMemsetAsync(e->gbar, 0, 4 * static_cast<size_t>(e->num_sms), e->stream));  // grid barriers only
   if (P.df) {
     // tags of this launch: tag0 + 1 .. tag0 + phases; the next launch starts
     // past them, so no word left by this one (finished or stopped) can match
