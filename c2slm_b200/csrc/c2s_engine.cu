@@ -460,6 +460,7 @@ struct c2s_engine {
   int16_t *pf_bs = nullptr;   // tokens' Q8_K sub-block sums
   uint8_t *pf_planes = nullptr;  // every layer projection's digit planes and row tables
   float *pf_fpart = nullptr;     // attention split partials (PfFlash::part)
+  float *pf_delta = nullptr;     // tensor parallel: the chunk's partial o-proj / down rows, allreduced
   unsigned *pf_fcount = nullptr; // attention split arrivals (PfFlash::count)
   int pf_fsplit = 0, pf_fns = 0; // keys per attention split, most splits of a block
   std::vector<std::array<const uint8_t *, 7>> pf_pl;  // per layer: q, k, v, o, gate, up, down
@@ -1302,7 +1303,7 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   {  // prefill on the tensor cores: one GPU, every layer projection a K-quant, superblock-aligned widths
-    bool okp = e->plan.world == 1 && d.embd % 256 == 0 && d.ffn % 256 == 0 && (hd == 64 || hd == 128);
+    bool okp = d.embd % 256 == 0 && d.ffn % 256 == 0 && (hd == 64 || hd == 128);
     for (int l = 0; l < d.n_layers && okp; ++l) {
       const LayerDev &Ld = e->layers[l];
       for (int t : {Ld.tq, Ld.tk, Ld.tv, Ld.to, Ld.tgate, Ld.tup, Ld.tdown}) okp = okp && is_kquant(t);
@@ -1492,7 +1493,7 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->pf_v), static_cast<void *>(e->pf_att), static_cast<void *>(e->pf_g),
                   static_cast<void *>(e->pf_u), static_cast<void *>(e->pf_d8), static_cast<void *>(e->pf_q8),
                   static_cast<void *>(e->pf_tok), static_cast<void *>(e->pf_planes), static_cast<void *>(e->pf_bs),
-                  static_cast<void *>(e->pf_fpart), static_cast<void *>(e->pf_fcount)})
+                  static_cast<void *>(e->pf_fpart), static_cast<void *>(e->pf_fcount), static_cast<void *>(e->pf_delta)})
     if (p) cudaFree(p);
   for (int k = 0; k < 8; ++k)
     if (e->peer_shared[k] && e->peer_shared[k] != e->tp_shared) cudaIpcCloseMemHandle(e->peer_shared[k]);
@@ -1887,8 +1888,13 @@ int c2s_kv_get(const c2s_engine *e, int is_value, int layer, int kv_head, int po
 static int pf_alloc(c2s_engine *e) {
   if (e->pf_cap) return C2S_OK;
   const c2s_model_desc &d = e->d;
-  const int cap = 1024, H = d.embd, F = d.ffn, nq = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
-  const int kmax = std::max(H, F);
+  const TpPlan &pl = e->plan;
+  const bool tp = pl.world > 1;
+  // this rank's shard (the whole model on one GPU)
+  const int nqh = tp ? pl.h1 - pl.h0 : d.n_heads, nkv = tp ? pl.g1 - pl.g0 : d.n_kv_heads;
+  const int cap = 1024, H = d.embd, F = tp ? (pl.f1 - pl.f0) * 256 : d.ffn, nq = nqh * d.head_dim,
+            kvd = nkv * d.head_dim;
+  const int kmax = std::max(std::max(H, F), nq);
   auto al = [&](void **p, size_t bytes) -> int {
     if (cudaMalloc(p, bytes) != cudaSuccess) return fail(C2S_ERR_OOM, "prefill buffers: cudaMalloc(%zu) failed", bytes);
     return C2S_OK;
@@ -1903,6 +1909,7 @@ static int pf_alloc(c2s_engine *e) {
       (rc = al(reinterpret_cast<void **>(&e->pf_q8), c * kmax)) || (rc = al(reinterpret_cast<void **>(&e->pf_tok), c * 4)) ||
       (rc = al(reinterpret_cast<void **>(&e->pf_bs), c * (kmax / 256) * 16)))
     return rc;
+  if (tp && (rc = al(reinterpret_cast<void **>(&e->pf_delta), c * H * 4))) return rc;
   // attention splits: keys of a query block in splits of pf_fsplit (a
   // multiple of the key tile), at most 16 per block at max_tokens
   {
@@ -1910,7 +1917,7 @@ static int pf_alloc(c2s_engine *e) {
     e->pf_fsplit = std::max(2 * kFkN, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
     e->pf_fns = (mt + e->pf_fsplit - 1) / e->pf_fsplit;
     const size_t nblk = (c * (d.n_heads / d.n_kv_heads) + kFqN - 1) / kFqN;
-    const size_t blocks = static_cast<size_t>(d.n_kv_heads) * nblk;
+    const size_t blocks = static_cast<size_t>(nkv) * nblk;
     if ((rc = al(reinterpret_cast<void **>(&e->pf_fpart), blocks * e->pf_fns * kFqN * (hd + 2) * 4)) ||
         (rc = al(reinterpret_cast<void **>(&e->pf_fcount), blocks * 4)))
       return rc;
@@ -1991,8 +1998,27 @@ static int pf_gemm(c2s_engine *e, int l, int which, int type, int rows, int cols
 // the last NormX
 static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
   const c2s_model_desc &d = e->d;
-  const int H = d.embd, F = d.ffn, hd = d.head_dim, nqh = d.n_heads, nkv = d.n_kv_heads;
-  const int nq = nqh * hd, kvd = nkv * hd, L = d.n_layers, qpk = nqh / nkv;
+  const TpPlan &pl = e->plan;
+  const bool tp = pl.world > 1;
+  // this rank's shard (the whole model on one GPU): query heads, kv groups,
+  // FFN rows; attn_output and ffn_down give partial rows, summed over the
+  // ranks before the residual add
+  const int H = d.embd, hd = d.head_dim, L = d.n_layers, qpk = d.n_heads / d.n_kv_heads;
+  const int nqh = tp ? pl.h1 - pl.h0 : d.n_heads, nkv = tp ? pl.g1 - pl.g0 : d.n_kv_heads;
+  const int F = tp ? (pl.f1 - pl.f0) * 256 : d.ffn;
+  const int nq = nqh * hd, kvd = nkv * hd;
+  const NcclApi *nc = nullptr;
+  if (tp)
+    if (int rc = nccl_api(&nc)) return rc;
+  // tensor parallel: out = the chunk's partial rows -> allreduce -> x += out
+  auto reduce_add = [&]() -> int {
+    const size_t cnt = static_cast<size_t>(n) * H;
+    const ncclResult_t r = nc->all_reduce(e->pf_delta, e->pf_delta, cnt, ncclFloat32, ncclSum, e->comm, e->stream);
+    if (r != ncclSuccess) return fail(C2S_ERR_CUDA, "prefill ncclAllReduce: %s", nc->err_str(r));
+    k_pf_add<<<e->num_sms * 4, kThreads, 0, e->stream>>>(e->pf_x, e->pf_delta, cnt);
+    CK(cudaGetLastError());
+    return C2S_OK;
+  };
 
   const size_t head_stride = static_cast<size_t>(d.max_tokens) * hd;
   const size_t plane = static_cast<size_t>(L) * nkv * head_stride;
@@ -2024,6 +2050,8 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     A.p0 = p0;
     A.qpk = qpk;
     A.n_heads = nqh;
+    A.hbase = tp ? pl.h0 : 0;
+    A.gbase = tp ? pl.g0 : 0;
     A.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));  // engine/forward.go:59
     A.part = e->pf_fpart;
     A.count = e->pf_fcount;
@@ -2035,7 +2063,11 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     else
       k_pf_flash<64><<<fgrid, kThreads, pf_flash_smem(64), s>>>(A);
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
-    if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
+    if (tp) {
+      if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_delta, H, PF_STORE, nullptr)) || (rc = reduce_add())) return rc;
+    } else if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) {
+      return rc;
+    }
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.ffn_norm, d.eps, H, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
     if ((rc = pf_gemm(e, l, 4, Ld.tgate, F, H, n, e->pf_g, F, PF_STORE, nullptr)) ||
         (rc = pf_gemm(e, l, 5, Ld.tup, F, H, n, e->pf_u, F, PF_STORE, nullptr)))
@@ -2043,7 +2075,11 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     // SwiGLU(gate, up) quantised straight into the down projection's token tiles
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr,
                                          e->pf_u);
-    if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) return rc;
+    if (tp) {
+      if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_delta, H, PF_STORE, nullptr)) || (rc = reduce_add())) return rc;
+    } else if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) {
+      return rc;
+    }
     CK(cudaGetLastError());
   }
   // the last token's residual stream (read by a following ComputeLogits /

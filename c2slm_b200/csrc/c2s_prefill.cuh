@@ -520,6 +520,14 @@ __global__ void __launch_bounds__(kThreads) k_pf_rope_store(float *q, const floa
   }
 }
 
+// x += d over n values (tensor parallel: the residual plus the ranks' summed
+// o-proj / down rows of the chunk)
+__global__ void k_pf_add(float *x, const float *d, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = __fadd_rn(x[i], d[i]);
+}
+
 // the chunk's bookkeeping on the device: TokenIDs, SeqLen and the forward
 // inputs of its last token (as the per-token path leaves them)
 __global__ void k_pf_commit(DevState *st, int *token_ids, const int *tok, int n, int p0, int cap) {
@@ -558,6 +566,11 @@ struct PfFlash {
   const float *kc, *vc;  // this layer's planes: group g row p at [g * head_stride + p * hd]
   size_t head_stride;
   int ldq, n, p0, qpk, n_heads;
+  // tensor-parallel shard: this rank's query heads are global heads
+  // [hbase, hbase + n_heads) and its kv groups start at global group gbase;
+  // the CTA of local group g takes the group's heads the rank holds (a
+  // group may straddle ranks).  One GPU: 0, 0.
+  int hbase, gbase;
   float scale;
   float *part;           // [group][block][max_splits][kFqN][hd + 2]: (m, l, O) of a split
   unsigned *count;       // [group][block]: arrivals of the block's splits (0 between launches)
@@ -588,20 +601,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   int *s_lim = reinterpret_cast<int *>(s_alpha + kFqN);  // last key position of each query
   const int tid = threadIdx.x, g = blockIdx.x;
   const int nblk = gridDim.y, blk = nblk - 1 - blockIdx.y, sp = blockIdx.z;
-  const int nv = A.n * A.qpk, v0 = blk * kFqN;
+  // this group's query heads on this rank: local heads [h0, h0 + qg)
+  const int gg = A.gbase + g;
+  const int hlo = max(A.hbase, gg * A.qpk), hhi = min(A.hbase + A.n_heads, (gg + 1) * A.qpk);
+  const int qg = hhi - hlo, h0 = hlo - A.hbase;
+  if (qg <= 0) return;
+  const int nv = A.n * qg, v0 = blk * kFqN;
   if (v0 >= nv) return;
   const int vlast = min(nv, v0 + kFqN) - 1;
-  const int kall = A.p0 + vlast / A.qpk + 1;  // the block's keys 0 .. kall-1
+  const int kall = A.p0 + vlast / qg + 1;  // the block's keys 0 .. kall-1
   const int nsplit = (kall + A.split_keys - 1) / A.split_keys;
   if (sp >= nsplit) return;  // this block has fewer splits
   const int kbeg = sp * A.split_keys, kend = min(kall, kbeg + A.split_keys);  // this split's keys
-  const int h0 = g * A.qpk;
   // ---- queries of the block, transposed (a warp: 32 queries of one d4); causal limits
   for (int i = tid; i < kFqN * (HD / 4); i += kThreads) {
     const int qi = i % kFqN, d4 = (i / kFqN) * 4, v = v0 + qi;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
     if (v < nv) {
-      const int t = v / A.qpk, h = v - t * A.qpk;
+      const int t = v / qg, h = v - t * qg;
       x = *reinterpret_cast<const float4 *>(A.q + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + d4);
     }
     Qt[(d4 + 0) * kFqN + qi] = x.x;
@@ -611,7 +628,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   }
   if (tid < kFqN) {
     const int v = v0 + tid;
-    s_lim[tid] = v < nv ? A.p0 + v / A.qpk : -1;
+    s_lim[tid] = v < nv ? A.p0 + v / qg : -1;
     s_m[tid] = -INFINITY;
     s_l[tid] = 0.f;
   }
@@ -741,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     for (int a = 0; a < 8; ++a) {
       const int q = qof(a), v = v0 + q;
       if (v < nv) {
-        const int t = v / A.qpk, h = v - t * A.qpk;
+        const int t = v / qg, h = v - t * qg;
         const float l = s_l[q];
         float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD;
 #pragma unroll
@@ -798,7 +815,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     float acc = 0.f;
     for (int j = 0; j < nsplit; ++j)
       acc = __fadd_rn(acc, __fmul_rn(s_w[j * kFqN + qi], __ldcg(pblk + (static_cast<size_t>(j) * kFqN + qi) * PW + 2 + dd)));
-    const int t = v / A.qpk, h = v - t * A.qpk;
+    const int t = v / qg, h = v - t * qg;
     A.out[static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + dd] = acc / s_l[qi];
   }
 }
