@@ -424,8 +424,9 @@ __device__ __forceinline__ void row_group(const uint8_t *base, size_t rstep, int
 }
 
 // Rows first, first + ws, ... (cnt of them) of a staged chunk -> y[local
-// row], in groups of 8, 4, 2 and 1 rows.  U units per row; ws warps share
-// the chunk.
+// row], in groups of 8 (Q5_0 / Q8_0; 4 for the K-quants, whose larger
+// per-row register state makes 8-row groups slower), 4, 2 and 1 rows.  U
+// units per row; ws warps share the chunk.
 template <int TYPE>
 __device__ __forceinline__ void warp_rows(const uint8_t *rows, int row_bytes, int U, int first, int cnt,
                                           const LimbsView &LV, const Q8KView &q8, float *y, int ws = kWarps) {
@@ -433,8 +434,13 @@ __device__ __forceinline__ void warp_rows(const uint8_t *rows, int row_bytes, in
   const uint8_t *base = rows + static_cast<size_t>(first) * row_bytes;
   float *yp = y + first;
   int left = cnt;
-  for (; left >= 8; left -= 8, base += 8 * rstep, yp += 8 * ws)
-    row_group<TYPE, 8>(base, rstep, U, LV, q8, yp, ws);
+  if constexpr (TYPE == T_Q4_K || TYPE == T_Q6_K) {
+    for (; left >= 4; left -= 4, base += 4 * rstep, yp += 4 * ws)
+      row_group<TYPE, 4>(base, rstep, U, LV, q8, yp, ws);
+  } else {
+    for (; left >= 8; left -= 8, base += 8 * rstep, yp += 8 * ws)
+      row_group<TYPE, 8>(base, rstep, U, LV, q8, yp, ws);
+  }
   if (left >= 4) {
     row_group<TYPE, 4>(base, rstep, U, LV, q8, yp, ws);
     left -= 4, base += 4 * rstep, yp += 4 * ws;
