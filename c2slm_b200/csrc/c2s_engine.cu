@@ -22,6 +22,7 @@
 #include <mutex>
 #include <string>
 #include <array>
+#include <initializer_list>
 #include <vector>
 
 #include "../../include/c2slm_b200.h"
@@ -1966,30 +1967,54 @@ static int pf_alloc(c2s_engine *e) {
   return C2S_OK;
 }
 
-// K-quant GEMM of the chunk's n tokens (their Q8_K rows in pf_q8 / pf_d8)
-static int pf_gemm(c2s_engine *e, int l, int which, int type, int rows, int cols, int n, float *out, int ldo, int mode,
-                   const float *bias) {
-  PfGemm G{};
-  G.planes = e->pf_pl[l][which];
-  G.rowinfo = e->pf_ri[l][which];
-  G.type = type;
-  G.rows = rows;
-  G.cols = cols;
-  G.a = e->pf_q8;
-  G.ad = e->pf_d8;
-  G.abs = e->pf_bs;
-  G.M = n;
-  G.out = out;
-  G.ldo = ldo;
-  G.mode = mode;
-  G.bias = bias;
-  G.err = &e->st->err;
-  const dim3 grid((rows + kPfM - 1) / kPfM, (n + kPfN - 1) / kPfN);
+// One K-quant GEMM of the chunk's n tokens (their Q8_K rows in pf_q8 /
+// pf_d8): weight matrix `which` of layer l
+struct PfJob {
+  int which, type, rows, cols;
+  float *out;
+  int ldo, mode;
+  const float *bias;
+};
+
+// The jobs of one weight type in one launch (none: nothing)
+static int pf_gemm_type(c2s_engine *e, int l, int n, int type, std::initializer_list<PfJob> jobs) {
+  PfGemmSet S{};
+  int tiles = 0;
+  for (const PfJob &j : jobs) {
+    if (j.type != type) continue;
+    PfGemm &G = S.g[S.n];
+    G.planes = e->pf_pl[l][j.which];
+    G.rowinfo = e->pf_ri[l][j.which];
+    G.type = j.type;
+    G.rows = j.rows;
+    G.cols = j.cols;
+    G.a = e->pf_q8;
+    G.ad = e->pf_d8;
+    G.abs = e->pf_bs;
+    G.M = n;
+    G.out = j.out;
+    G.ldo = j.ldo;
+    G.mode = j.mode;
+    G.bias = j.bias;
+    G.err = &e->st->err;
+    S.tiles[S.n] = (j.rows + kPfM - 1) / kPfM;
+    tiles += S.tiles[S.n++];
+  }
+  if (S.n == 0) return C2S_OK;
+  const dim3 grid(tiles, (n + kPfN - 1) / kPfN);
   if (type == T_Q4_K)
-    k_pf_gemm<T_Q4_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(G);
+    k_pf_gemm<T_Q4_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(S);
   else
-    k_pf_gemm<T_Q6_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(G);
+    k_pf_gemm<T_Q6_K><<<grid, kPfThreads, kPfSmem, e->stream>>>(S);
   CK(cudaGetLastError());
+  return C2S_OK;
+}
+
+// Up to three GEMMs over the same tokens: one launch per weight type
+static int pf_gemm(c2s_engine *e, int l, int n, std::initializer_list<PfJob> jobs) {
+  if (jobs.size() > 3) return fail(C2S_ERR_ARG, "pf_gemm: more than three jobs");
+  for (const int type : {T_Q4_K, T_Q6_K})
+    if (int rc = pf_gemm_type(e, l, n, type, jobs)) return rc;
   return C2S_OK;
 }
 
@@ -2031,9 +2056,9 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     const LayerDev &Ld = e->layers[l];
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.attn_norm, d.eps, H, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
     int rc;
-    if ((rc = pf_gemm(e, l, 0, Ld.tq, nq, H, n, e->pf_q, nq, PF_STORE, Ld.qb)) ||
-        (rc = pf_gemm(e, l, 1, Ld.tk, kvd, H, n, e->pf_k, kvd, PF_STORE, Ld.kb)) ||
-        (rc = pf_gemm(e, l, 2, Ld.tv, kvd, H, n, e->pf_v, kvd, PF_STORE, Ld.vb)))
+    if ((rc = pf_gemm(e, l, n,
+                      {{0, Ld.tq, nq, H, e->pf_q, nq, PF_STORE, Ld.qb}, {1, Ld.tk, kvd, H, e->pf_k, kvd, PF_STORE, Ld.kb},
+                       {2, Ld.tv, kvd, H, e->pf_v, kvd, PF_STORE, Ld.vb}})))
       return rc;
     float *kc = e->kv + static_cast<size_t>(l) * nkv * head_stride, *vc = kc + plane;
     k_pf_rope_store<<<n, kThreads, static_cast<size_t>(nqh + nkv) * hd * 4, s>>>(
@@ -2064,20 +2089,22 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
       k_pf_flash<64><<<fgrid, kThreads, pf_flash_smem(64), s>>>(A);
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
     if (tp) {
-      if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_delta, H, PF_STORE, nullptr)) || (rc = reduce_add())) return rc;
-    } else if ((rc = pf_gemm(e, l, 3, Ld.to, H, nq, n, e->pf_x, H, PF_ADD, nullptr))) {
+      if ((rc = pf_gemm(e, l, n, {{3, Ld.to, H, nq, e->pf_delta, H, PF_STORE, nullptr}})) || (rc = reduce_add()))
+        return rc;
+    } else if ((rc = pf_gemm(e, l, n, {{3, Ld.to, H, nq, e->pf_x, H, PF_ADD, nullptr}}))) {
       return rc;
     }
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_x, H, Ld.ffn_norm, d.eps, H, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
-    if ((rc = pf_gemm(e, l, 4, Ld.tgate, F, H, n, e->pf_g, F, PF_STORE, nullptr)) ||
-        (rc = pf_gemm(e, l, 5, Ld.tup, F, H, n, e->pf_u, F, PF_STORE, nullptr)))
+    if ((rc = pf_gemm(e, l, n,
+                      {{4, Ld.tgate, F, H, e->pf_g, F, PF_STORE, nullptr}, {5, Ld.tup, F, H, e->pf_u, F, PF_STORE, nullptr}})))
       return rc;
     // SwiGLU(gate, up) quantised straight into the down projection's token tiles
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_g, F, nullptr, 0.f, F, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr,
                                          e->pf_u);
     if (tp) {
-      if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_delta, H, PF_STORE, nullptr)) || (rc = reduce_add())) return rc;
-    } else if ((rc = pf_gemm(e, l, 6, Ld.tdown, H, F, n, e->pf_x, H, PF_ADD, nullptr))) {
+      if ((rc = pf_gemm(e, l, n, {{6, Ld.tdown, H, F, e->pf_delta, H, PF_STORE, nullptr}})) || (rc = reduce_add()))
+        return rc;
+    } else if ((rc = pf_gemm(e, l, n, {{6, Ld.tdown, H, F, e->pf_x, H, PF_ADD, nullptr}}))) {
       return rc;
     }
     CK(cudaGetLastError());

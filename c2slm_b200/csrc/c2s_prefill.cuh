@@ -61,13 +61,11 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 __device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+// 8 consecutive 32-bit columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -239,14 +237,14 @@ __global__ void __launch_bounds__(128) k_pf_planes(const uint8_t *w, int rows, i
   }
 }
 
+// One CTA's tile (row tile R, token tile T) of G; smem: kPfSmem bytes.
 template <int TYPE>
-__global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfGemm G) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const int T, uint8_t *smem) {
   __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages], tfull[2], tempty[2];
   __shared__ uint32_t s_tmem;
   constexpr uint32_t kStageBytes = kPfStage;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int R = blockIdx.x, T = blockIdx.y, r0 = R * kPfM, t0 = T * kPfN;
+  const int r0 = R * kPfM, t0 = T * kPfN;
   const int nsb = G.cols / 256;
   if (tid == 0) {
     for (int i = 0; i < kPfStages; ++i) {
@@ -336,13 +334,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfGemm G) {
       const uint4 *sbs = reinterpret_cast<const uint4 *>(stg + kPfD8Bytes);
       const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(tb * 2 * kPfN + 64 * th);
 #pragma unroll
-      for (int c0 = 0; c0 < 64; c0 += 16) {
-        uint32_t hi[16], lo[16];
-        tmem_ld16(ta + c0, hi);
-        tmem_ld16(ta + kPfN + c0, lo);
+      for (int c0 = 0; c0 < 64; c0 += 8) {
+        uint32_t hi[8], lo[8];
+        tmem_ld8(ta + c0, hi);
+        tmem_ld8(ta + kPfN + c0, lo);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 8; ++i) {
           const int tk = 64 * th + c0 + i;
           // token scales four at a time (one broadcast load)
           const float4 d84 = *reinterpret_cast<const float4 *>(sd8 + (tk & ~3));
@@ -371,23 +369,63 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const PfGemm G) {
       }
     }
     if (ok && row < G.rows) {
-      const float bias = (G.mode == PF_STORE && G.bias) ? __ldg(G.bias + row) : 0.f;
+      float *o = G.out + static_cast<size_t>(t0 + 64 * th) * G.ldo + row;
+      const int nt = min(64, G.M - (t0 + 64 * th));
+      if (G.mode == PF_ADD) {
+        // residual add in batches of 16: all loads of a batch before its
+        // stores (one memory round trip per batch, not one per token)
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const int tok = t0 + 64 * th + i;
-        if (tok < G.M) {
-          float *o = G.out + static_cast<size_t>(tok) * G.ldo + row;
-          if (G.mode == PF_ADD)
-            *o = __fadd_rn(*o, acc[i]);
-          else
-            *o = G.bias ? __fadd_rn(acc[i], bias) : acc[i];
+        for (int i0 = 0; i0 < 64; i0 += 16) {
+          float old[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) old[i] = i0 + i < nt ? o[static_cast<size_t>(i0 + i) * G.ldo] : 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (i0 + i < nt) o[static_cast<size_t>(i0 + i) * G.ldo] = __fadd_rn(old[i], acc[i0 + i]);
         }
+      } else {
+        const float bias = G.bias ? __ldg(G.bias + row) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < nt) o[static_cast<size_t>(i) * G.ldo] = G.bias ? __fadd_rn(acc[i], bias) : acc[i];
       }
     }
   }
   tmem_fence_before();
   __syncthreads();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+}
+
+// Up to three GEMMs of one weight type over the same token tiles in one
+// launch (the q, k and v projections, whose narrow k / v matrices alone would
+// occupy 16 CTAs): blockIdx.x runs over the row tiles of job 0, then of job
+// 1, ...
+struct PfGemmSet {
+  PfGemm g[3];
+  int tiles[3];  // row tiles of each job
+  int n;         // jobs
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(const __grid_constant__ PfGemmSet S) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ PfGemm sG;  // this CTA's job (read from shared memory, not kept in registers)
+  __shared__ int sR;     // its row tile in the job
+  if (threadIdx.x == 0) {
+    const int R = blockIdx.x, t0 = S.tiles[0], t1 = S.tiles[1];
+    if (R < t0 || S.n == 1) {
+      sG = S.g[0];
+      sR = R;
+    } else if (R < t0 + t1 || S.n == 2) {
+      sG = S.g[1];
+      sR = R - t0;
+    } else {
+      sG = S.g[2];
+      sR = R - t0 - t1;
+    }
+  }
+  __syncthreads();
+  pf_gemm_tile<TYPE>(sG, sR, blockIdx.y, smem);
 }
 
 // ---------------------------------------------------------------------------
