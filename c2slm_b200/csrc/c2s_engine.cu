@@ -464,6 +464,9 @@ struct c2s_engine {
   float *pf_delta = nullptr;     // tensor parallel: the chunk's partial o-proj / down rows, allreduced
   unsigned *pf_fcount = nullptr; // attention split arrivals (PfFlash::count)
   int pf_fsplit = 0, pf_fns = 0; // keys per attention split, most splits of a block
+  uint8_t *pf_kvt = nullptr;     // one layer's K/V tiles of the tensor-core attention (k_pf_kv_tiles)
+  int pf_kvt_tpg = 0;            // tiles per kv group
+  int pf_attn_fp32 = 0;          // test switch (C2S_PF_ATTN=fp32): the FP32 attention kernel instead
   std::vector<std::array<const uint8_t *, 7>> pf_pl;  // per layer: q, k, v, o, gate, up, down
   std::vector<std::array<const uint4 *, 7>> pf_ri;
   DevState *h_st = nullptr;
@@ -1301,6 +1304,8 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
   CK(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
   CK(cudaFuncSetAttribute(k_pf_flash<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pf_flash_smem(128))));
   CK(cudaFuncSetAttribute(k_pf_flash<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pf_flash_smem(64))));
+  CK(cudaFuncSetAttribute(k_pf_attn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ta_smem(128))));
+  CK(cudaFuncSetAttribute(k_pf_attn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(ta_smem(64))));
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   CK(cudaFuncSetAttribute(k_pf_gemm<T_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmem));
   {  // prefill on the tensor cores: one GPU, every layer projection a K-quant, superblock-aligned widths
@@ -1311,6 +1316,8 @@ int engine_build(c2s_engine *e, const c2s_model_desc *desc, const c2s_tensor_des
     }
     const char *pe = getenv("C2S_PREFILL");
     e->pf_ok = okp && !(pe && strcmp(pe, "0") == 0) ? 1 : 0;
+    const char *pa = getenv("C2S_PF_ATTN");
+    e->pf_attn_fp32 = pa && strcmp(pa, "fp32") == 0 ? 1 : 0;
   }
   if ((rc = capture(e, &e->g_forward, 0)) || (rc = capture(e, &e->g_step, 1)) ||
       (rc = capture(e, &e->g_logits, 2)) || (rc = capture(e, &e->g_fwd_select, 3))) {
@@ -1494,7 +1501,8 @@ void engine_free(c2s_engine *e) {
                   static_cast<void *>(e->pf_v), static_cast<void *>(e->pf_att), static_cast<void *>(e->pf_g),
                   static_cast<void *>(e->pf_u), static_cast<void *>(e->pf_d8), static_cast<void *>(e->pf_q8),
                   static_cast<void *>(e->pf_tok), static_cast<void *>(e->pf_planes), static_cast<void *>(e->pf_bs),
-                  static_cast<void *>(e->pf_fpart), static_cast<void *>(e->pf_fcount), static_cast<void *>(e->pf_delta)})
+                  static_cast<void *>(e->pf_fpart), static_cast<void *>(e->pf_fcount), static_cast<void *>(e->pf_delta),
+                  static_cast<void *>(e->pf_kvt)})
     if (p) cudaFree(p);
   for (int k = 0; k < 8; ++k)
     if (e->peer_shared[k] && e->peer_shared[k] != e->tp_shared) cudaIpcCloseMemHandle(e->peer_shared[k]);
@@ -1883,6 +1891,18 @@ int c2s_kv_get(const c2s_engine *e, int is_value, int layer, int kv_head, int po
   return C2S_OK;
 }
 
+int c2s_prefill_debug(const c2s_engine *e, int which, float *out, int n_floats) {
+  if (!e || !out || n_floats < 0 || which < 0 || which > 1) return fail(C2S_ERR_ARG, "bad argument");
+  if (!e->pf_att) return fail(C2S_ERR_STATE, "no tensor-core prefill has run on this engine");
+  const int nqh = e->plan.world > 1 ? e->plan.h1 - e->plan.h0 : e->d.n_heads;
+  if (static_cast<size_t>(n_floats) > static_cast<size_t>(e->pf_cap) * nqh * e->d.head_dim)
+    return fail(C2S_ERR_ARG, "n_floats %d exceeds the prefill chunk's buffers", n_floats);
+  DeviceGuard dg(e->device);
+  CK(cudaStreamSynchronize(e->stream));
+  CK(cudaMemcpy(out, which == 0 ? e->pf_att : e->pf_q, static_cast<size_t>(n_floats) * 4, cudaMemcpyDeviceToHost));
+  return C2S_OK;
+}
+
 // ---------------------------------------------------------------------------
 // prefill: chunks of up to pf_cap tokens through every layer together
 // ---------------------------------------------------------------------------
@@ -1919,10 +1939,14 @@ static int pf_alloc(c2s_engine *e) {
     e->pf_fns = (mt + e->pf_fsplit - 1) / e->pf_fsplit;
     const size_t nblk = (c * (d.n_heads / d.n_kv_heads) + kFqN - 1) / kFqN;
     const size_t blocks = static_cast<size_t>(nkv) * nblk;
-    if ((rc = al(reinterpret_cast<void **>(&e->pf_fpart), blocks * e->pf_fns * kFqN * (hd + 2) * 4)) ||
+    if ((rc = al(reinterpret_cast<void **>(&e->pf_fpart), blocks * e->pf_fns * kFqN * pf_part_width(hd) * 4)) ||
         (rc = al(reinterpret_cast<void **>(&e->pf_fcount), blocks * 4)))
       return rc;
     CK(cudaMemsetAsync(e->pf_fcount, 0, blocks * 4, e->stream));
+    // K/V tiles of the tensor-core attention: one layer, every position
+    e->pf_kvt_tpg = (mt + kTaK - 1) / kTaK;
+    if ((rc = al(reinterpret_cast<void **>(&e->pf_kvt), static_cast<size_t>(nkv) * e->pf_kvt_tpg * ta_tile_bytes(hd))))
+      return rc;
   }
   // the digit planes of every layer projection, converted once
   auto plane_bytes = [](int, int rows, int cols) {
@@ -2082,11 +2106,26 @@ static int pf_run(c2s_engine *e, int p0, const int32_t *tokens, int n) {
     A.count = e->pf_fcount;
     A.split_keys = e->pf_fsplit;
     A.max_splits = e->pf_fns;
+    A.tiles = e->pf_kvt;
+    A.tiles_per_group = e->pf_kvt_tpg;
+    A.err = &e->st->err;
     const dim3 fgrid(nkv, (n * qpk + kFqN - 1) / kFqN, (p0 + n + e->pf_fsplit - 1) / e->pf_fsplit);
-    if (hd == 128)
-      k_pf_flash<128><<<fgrid, kThreads, pf_flash_smem(128), s>>>(A);
-    else
-      k_pf_flash<64><<<fgrid, kThreads, pf_flash_smem(64), s>>>(A);
+    if (e->pf_attn_fp32) {
+      if (hd == 128)
+        k_pf_flash<128><<<fgrid, kThreads, pf_flash_smem(128), s>>>(A);
+      else
+        k_pf_flash<64><<<fgrid, kThreads, pf_flash_smem(64), s>>>(A);
+    } else {
+      const dim3 tgrid((p0 + n + kTaK - 1) / kTaK, nkv);
+      if (hd == 128) {
+        k_pf_kv_tiles<128><<<tgrid, 256, 0, s>>>(kc, vc, head_stride, p0 + n, e->pf_kvt, e->pf_kvt_tpg);
+        k_pf_attn<128><<<fgrid, kTaThreads, ta_smem(128), s>>>(A);
+      } else {
+        k_pf_kv_tiles<64><<<tgrid, 256, 0, s>>>(kc, vc, head_stride, p0 + n, e->pf_kvt, e->pf_kvt_tpg);
+        k_pf_attn<64><<<fgrid, kTaThreads, ta_smem(64), s>>>(A);
+      }
+    }
+    CK(cudaGetLastError());
     k_pf_norm_q8k<<<n, kThreads, 0, s>>>(e->pf_att, nq, nullptr, 0.f, nq, n, e->pf_q8, e->pf_d8, e->pf_bs, nullptr);
     if (tp) {
       if ((rc = pf_gemm(e, l, n, {{3, Ld.to, H, nq, e->pf_delta, H, PF_STORE, nullptr}})) || (rc = reduce_add()))

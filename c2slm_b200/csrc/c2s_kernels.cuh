@@ -263,7 +263,6 @@ __device__ __forceinline__ void build_q8k(const float *src, int cols, int8_t *qs
 
 __global__ void __launch_bounds__(kThreads) k_matvec(const MatParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[kWarps][kWarps];
   __shared__ float scratch[kWarps];
   __shared__ int s_flag;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P.off_bars);

@@ -53,6 +53,31 @@ __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t d
       "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
+// instruction descriptor of kind::tf32: f32 accumulator, tf32 A and B, both
+// K-major, M x N
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// kind::tf32, A and B in shared memory
+__device__ __forceinline__ void umma_tf32_ss(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// kind::tf32, A in tensor memory (M lanes x K columns, one element a column),
+// B in shared memory
+__device__ __forceinline__ void umma_tf32_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                             uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
                : "memory");
@@ -68,6 +93,31 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes <- registers
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // K-quant x Q8_K GEMM: out[t][r] (+)= sum_k W[r][k] x[t][k], one CTA per tile
@@ -613,6 +663,11 @@ struct PfFlash {
   float *part;           // [group][block][max_splits][kFqN][hd + 2]: (m, l, O) of a split
   unsigned *count;       // [group][block]: arrivals of the block's splits (0 between launches)
   int split_keys, max_splits;
+  // tensor-core kernel (k_pf_attn): the layer's K/V tiles (k_pf_kv_tiles),
+  // tiles per group, and the status word its bounded waits report to
+  const uint8_t *tiles;
+  int tiles_per_group;
+  unsigned *err;
 };
 
 constexpr int kFqN = 128, kFkN = 128;
@@ -627,6 +682,57 @@ constexpr int kFps = kFqN + 16;
 __host__ __device__ constexpr int pf_flash_kp(int hd) { return hd * kFkN > kFkN * kFps ? hd * kFkN : kFkN * kFps; }
 __host__ __device__ constexpr size_t pf_flash_smem(int hd) {
   return (static_cast<size_t>(hd) * kFqN + pf_flash_kp(hd) + static_cast<size_t>(kFkN) * hd + 4 * kFqN) * 4;
+}
+
+// Split partials of a query block: per split and query row, (m, l, -, -,
+// O[HD]) -- rows of pf_part_width(HD) floats, O 16-byte aligned.
+__host__ __device__ constexpr int pf_part_width(int hd) { return hd + 4; }
+
+// The last-arriving split of a query block combines the block's nsplit
+// partials in split order: per query M = max m_s, w_s = exp(m_s - M) in
+// float64, L = sum w_s l_s, out = (sum w_s O_s) / L.  Four output columns a
+// task, every split's value loaded before the ordered sum.  s_w: shared
+// [nsplit][kFqN], s_l: shared [kFqN]; all nthreads threads call it.
+template <int HD>
+__device__ __forceinline__ void pf_split_combine(const PfFlash &A, const float *pblk, int nsplit, int v0, int nv,
+                                                 int qg, int h0, float *s_w, float *s_l, int tid, int nthreads) {
+  constexpr int PW = pf_part_width(HD);
+  if (tid < kFqN) {
+    float M = -INFINITY;
+    for (int j = 0; j < nsplit; ++j) M = fmaxf(M, __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW));
+    float L = 0.f;
+    for (int j = 0; j < nsplit; ++j) {
+      const float mj = __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW);
+      const float w = mj == -INFINITY ? 0.f : static_cast<float>(exp(static_cast<double>(__fsub_rn(mj, M))));
+      s_w[j * kFqN + tid] = w;
+      L = __fadd_rn(L, __fmul_rn(w, __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW + 1)));
+    }
+    s_l[tid] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < kFqN * (HD / 4); i += nthreads) {
+    const int qi = i / (HD / 4), d4 = (i - qi * (HD / 4)) * 4, v = v0 + qi;
+    if (v >= nv) continue;
+    float4 x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nsplit)
+        x[j] = __ldcg(reinterpret_cast<const float4 *>(pblk + (static_cast<size_t>(j) * kFqN + qi) * PW + 4 + d4));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < nsplit) {
+        const float w = s_w[j * kFqN + qi];
+        acc.x = __fadd_rn(acc.x, __fmul_rn(w, x[j].x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(w, x[j].y));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(w, x[j].z));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(w, x[j].w));
+      }
+    const float L = s_l[qi];
+    const int t = v / qg, h = v - t * qg;
+    *reinterpret_cast<float4 *>(A.out + static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + d4) =
+        make_float4(acc.x / L, acc.y / L, acc.z / L, acc.w / L);
+  }
 }
 
 template <int HD>
@@ -806,14 +912,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
     return;
   }
   // ---- partial (m, l, O) of this split; the block's last split combines
-  constexpr int PW = HD + 2;
+  constexpr int PW = pf_part_width(HD);
   float *pblk = A.part + (static_cast<size_t>(g) * nblk + blk) * A.max_splits * kFqN * PW;
   {
     float *pp = pblk + static_cast<size_t>(sp) * kFqN * PW;
 #pragma unroll
     for (int a = 0; a < 8; ++a)
 #pragma unroll
-      for (int b = 0; b < OD; ++b) pp[qof(a) * PW + 2 + dof(b)] = o[a][b];
+      for (int b = 0; b < OD; ++b) pp[qof(a) * PW + 4 + dof(b)] = o[a][b];
     if (tid < kFqN) {
       pp[tid * PW] = s_m[tid];
       pp[tid * PW + 1] = s_l[tid];
@@ -832,30 +938,399 @@ __global__ void __launch_bounds__(kThreads, 1) k_pf_flash(const PfFlash A) {
   __syncthreads();
   if (!*s_last) return;
   __threadfence();
-  // weights of the splits for each query: w_s = exp(m_s - M) (float64), over s in order
-  float *s_w = Pt;  // [max_splits][kFqN]
-  if (tid < kFqN) {
-    float M = -INFINITY;
-    for (int j = 0; j < nsplit; ++j) M = fmaxf(M, __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW));
-    float L = 0.f;
-    for (int j = 0; j < nsplit; ++j) {
-      const float mj = __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW);
-      const float w = mj == -INFINITY ? 0.f : static_cast<float>(exp(static_cast<double>(__fsub_rn(mj, M))));
-      s_w[j * kFqN + tid] = w;
-      L = __fadd_rn(L, __fmul_rn(w, __ldcg(pblk + (static_cast<size_t>(j) * kFqN + tid) * PW + 1)));
+  pf_split_combine<HD>(A, pblk, nsplit, v0, nv, qg, h0, Pt, s_l, tid, kThreads);
+}
+
+// ---------------------------------------------------------------------------
+// Causal attention of a prefill chunk on the tensor cores (kind::tf32).
+//
+// FP32 products from TF32 operands: each f32 operand x is split into
+// hi = x with its 13 low mantissa bits cleared (a TF32 value) and
+// lo = x - hi (exact), and a product is taken as hi*hi' + hi*lo' + lo*hi'
+// (lo read as TF32 in turn; the lo*lo' term, below 2^-20 of the product, is
+// dropped), accumulated in the MMA's f32 accumulator.  Against float64
+// attention from the same q, k and v this is as close as the FP32 kernel
+// (k_pf_flash): the error of both is set by the f32 rounding of large,
+// peaked scores, not by the split.
+//
+// CTA: kv group g, block of 128 query vectors (as k_pf_flash: v = token *
+// qg + head, the latest tokens' blocks first), key split sp; keys in tiles
+// of 64.  Two passes over the split's key tiles, as the reference's Softmax
+// (tensor/ops.go:317-339) takes the maximum of all scores before any
+// exponential:
+//   pass 1  S = Q K^T (TMEM), row maxima of S * scale over the causal keys;
+//   pass 2  S again, p = exp(S * scale - m) (exp_nonpos: f32 on the FMA pipe;
+//           the float64 exponential's conversions made the multi-function
+//           unit the kernel's bound), l += p in key order, O += P V (TMEM).
+// O / l at the end, or the split's (m, l, O) for the last-arriving split to
+// combine (the FP32 kernel's combine, in split order).
+// Warps 0-3: one query row per thread (TMEM lane): Q into TMEM, softmax,
+// epilogue.  Warp 4 lane 0: MMAs (and the TMEM allocation).  Warp 5 lane 0:
+// bulk copies of the K / V tiles.
+// TMEM columns: Q hi [0, HD), Q lo [HD, 2 HD), two S buffers of 64,
+// O [2 HD + 128, 3 HD + 128) -- 512 columns at HD = 128.
+// Shared memory: K hi | lo, V^T hi | lo of one tile (4 planes of 64 x HD
+// f32), P hi | lo (2 x 128 x 64 f32), all in the no-swizzle K-major
+// core-matrix layout of the GEMM (per 32-B K step: 8-row groups 256 B apart,
+// 16-B halves 128 B apart).
+// ---------------------------------------------------------------------------
+constexpr int kTaK = 64;          // keys per tile
+constexpr int kTaThreads = 192;
+__host__ __device__ constexpr int ta_plane(int hd) { return kTaK * hd * 4; }
+__host__ __device__ constexpr size_t ta_tile_bytes(int hd) { return 4 * static_cast<size_t>(ta_plane(hd)); }
+constexpr int kTaPPlane = 128 * kTaK * 4;
+__host__ __device__ constexpr size_t ta_smem(int hd) { return ta_tile_bytes(hd) + 2 * kTaPPlane; }
+
+// e^x for x <= 0 in f32 with FMA-pipe arithmetic only: Cody-Waite reduction
+// x = k ln2 + r, |r| <= ln2 / 2, with ln2 split into a head cut to 15
+// significant bits (k * head exact for |k| < 512) and the remainder; e^r by
+// its Taylor series to degree 7 in Horner form (truncation below 6e-9
+// relative); 2^k from the exponent bits.  Against the f32 rounding of the
+// float64 e^x (the reference's Softmax value) over [-87, 0]: within 1 ulp,
+// equal for ~94 % of arguments (200,000 uniform samples).  Returns 0
+// below e^-87 (under the smallest normal f32: next to the row maximum's
+// probability 1 such a term cannot change a sum or a weighted mean).
+__device__ __forceinline__ float exp_nonpos(float x) {
+  if (!(x > -87.f)) return 0.f;  // also -inf
+  const float k = rintf(x * 1.44269504088896341f);  // log2(e)
+  float r = fmaf(k, -0.693145751953125f, x);        // ln2 head
+  r = fmaf(k, -1.42860682030941723e-6f, r);         // ln2 - head
+  float p = 1.f / 5040.f;
+  p = fmaf(p, r, 1.f / 720.f);
+  p = fmaf(p, r, 1.f / 120.f);
+  p = fmaf(p, r, 1.f / 24.f);
+  p = fmaf(p, r, 1.f / 6.f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.f);
+  p = fmaf(p, r, 1.f);
+  return p * __int_as_float((static_cast<int>(k) + 127) << 23);
+}
+
+// x = hi + lo: hi = x with the 13 low mantissa bits cleared (a TF32 value),
+// lo = x - hi (exact; the tensor cores read it as TF32 too)
+__device__ __forceinline__ void tf32_split(float x, uint32_t &hi, uint32_t &lo) {
+  hi = __float_as_uint(x) & 0xFFFFE000u;
+  lo = __float_as_uint(__fsub_rn(x, __uint_as_float(hi)));
+}
+
+// K and V rows 0 .. nkeys-1 of every kv group of a layer -> the tiles the
+// tensor-core attention copies: per group and tile of 64 keys, four planes
+// [K hi | K lo | V^T hi | V^T lo], each 64 x HD f32.  K planes: the B
+// operand of Q K^T (rows = keys, K-major over dims); V^T planes: the B
+// operand of P V (rows = dims, K-major over keys).  Task i writes the 16
+// bytes at 16 i of a plane (coalesced stores).  Keys past nkeys are zero.
+template <int HD>
+__global__ void __launch_bounds__(256) k_pf_kv_tiles(const float *kc, const float *vc, size_t head_stride, int nkeys,
+                                                     uint8_t *tiles, int tiles_per_group) {
+  constexpr int PL = ta_plane(HD);
+  const int t = blockIdx.x, g = blockIdx.y, kb = t * kTaK;
+  uint8_t *dst = tiles + (static_cast<size_t>(g) * tiles_per_group + t) * 4 * PL;
+  const float *kg = kc + g * head_stride, *vg = vc + g * head_stride;
+  for (int i = threadIdx.x; i < kTaK * HD / 4; i += blockDim.x) {
+    uint4 h, l;
+    {  // K: row r = 8 grp + r8 (key), dims 8 s + 4 half ..
+      const int r8 = i & 7, half = (i >> 3) & 1, grp = (i >> 4) & 7, ks = i >> 7;
+      const int r = grp * 8 + r8, d4 = ks * 8 + half * 4;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (kb + r < nkeys) x = __ldcg(reinterpret_cast<const float4 *>(kg + static_cast<size_t>(kb + r) * HD + d4));
+      tf32_split(x.x, h.x, l.x);
+      tf32_split(x.y, h.y, l.y);
+      tf32_split(x.z, h.z, l.z);
+      tf32_split(x.w, h.w, l.w);
+      *reinterpret_cast<uint4 *>(dst + 16 * i) = h;
+      *reinterpret_cast<uint4 *>(dst + PL + 16 * i) = l;
     }
-    s_l[tid] = L;
+    {  // V^T: row n = 8 ng + n8 (dim), keys 8 ks + 4 half ..
+      const int n8 = i & 7, half = (i >> 3) & 1, ng = (i >> 4) % (HD / 8), ks = (i >> 4) / (HD / 8);
+      const int n = ng * 8 + n8, k0 = kb + ks * 8 + half * 4;
+      float x[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = k0 + e < nkeys ? __ldcg(vg + static_cast<size_t>(k0 + e) * HD + n) : 0.f;
+      tf32_split(x[0], h.x, l.x);
+      tf32_split(x[1], h.y, l.y);
+      tf32_split(x[2], h.z, l.z);
+      tf32_split(x[3], h.w, l.w);
+      *reinterpret_cast<uint4 *>(dst + 2 * PL + 16 * i) = h;
+      *reinterpret_cast<uint4 *>(dst + 3 * PL + 16 * i) = l;
+    }
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTaThreads, 1) k_pf_attn(const PfFlash A) {
+  extern __shared__ __align__(128) uint8_t tsm[];
+  constexpr int PL = ta_plane(HD);
+  uint8_t *sK = tsm, *sV = tsm + 2 * PL, *sP = tsm + 4 * PL;  // each: hi plane, then lo plane
+  __shared__ __align__(8) uint64_t k_full, k_empty, v_full, v_empty, s_full[2], s_empty[2], p_full, p_empty, q_ready,
+      o_full;
+  __shared__ uint32_t s_tmem;
+  __shared__ float s_l[kFqN];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = blockIdx.x, nblk = gridDim.y, blk = nblk - 1 - blockIdx.y, sp = blockIdx.z;
+  // this group's query heads on this rank: local heads [h0, h0 + qg)
+  const int gg = A.gbase + g;
+  const int hlo = max(A.hbase, gg * A.qpk), hhi = min(A.hbase + A.n_heads, (gg + 1) * A.qpk);
+  const int qg = hhi - hlo, h0 = hlo - A.hbase;
+  if (qg <= 0) return;
+  const int nv = A.n * qg, v0 = blk * kFqN;
+  if (v0 >= nv) return;
+  const int vlast = min(nv, v0 + kFqN) - 1;
+  const int kall = A.p0 + vlast / qg + 1;  // the block's keys 0 .. kall-1
+  const int nsplit = (kall + A.split_keys - 1) / A.split_keys;
+  if (sp >= nsplit) return;  // this block has fewer splits
+  const int kbeg = sp * A.split_keys, kend = min(kall, kbeg + A.split_keys);  // this split's keys
+  const int kt0 = kbeg / kTaK, nt = (kend - kbeg + kTaK - 1) / kTaK;
+  if (tid == 0) {
+    mbar_init(&k_full, 1);
+    mbar_init(&k_empty, 1);
+    mbar_init(&v_full, 1);
+    mbar_init(&v_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(&p_full, 4);
+    mbar_init(&p_empty, 1);
+    mbar_init(&q_ready, 4);
+    mbar_init(&o_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(&s_tmem)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tmem_fence_before();
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = s_tmem;
+  constexpr uint32_t cQh = 0, cQl = HD, cS = 2 * HD, cO = 2 * HD + 2 * kTaK;
+  bool ok = true;
+  if (warp == 5) {
+    // ------------------------------------------------------------ copies
+    if (lane == 0) {
+      const uint8_t *tg = A.tiles + static_cast<size_t>(g) * A.tiles_per_group * 4 * PL;
+      int ku = 0, vu = 0;
+      for (int pass = 0; pass < 2 && ok; ++pass)
+        for (int j = 0; j < nt && ok; ++j) {
+          const uint8_t *src = tg + static_cast<size_t>(kt0 + j) * 4 * PL;
+          if (ku > 0 && !(ok = mbar_wait_bounded(&k_empty, static_cast<uint32_t>((ku - 1) & 1), A.err))) break;
+          mbar_arrive_expect_tx(&k_full, 2 * PL);
+          bulk_g2s(sK, src, 2 * PL, &k_full);
+          ++ku;
+          if (pass == 1) {
+            if (vu > 0 && !(ok = mbar_wait_bounded(&v_empty, static_cast<uint32_t>((vu - 1) & 1), A.err))) break;
+            mbar_arrive_expect_tx(&v_full, 2 * PL);
+            bulk_g2s(sV, src + 2 * PL, 2 * PL, &v_full);
+            ++vu;
+          }
+        }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMAs
+    if (lane == 0) {
+      constexpr uint32_t idS = umma_idesc_tf32(128, kTaK), idO = umma_idesc_tf32(128, HD);
+      int ku = 0, su = 0, vu = 0, pu = 0;
+      // S(b) = Q K^T: the two cross terms, then hi x hi
+      auto issue_s = [&]() -> bool {
+        if (!mbar_wait_bounded(&k_full, static_cast<uint32_t>(ku & 1), A.err)) return false;
+        const int b = su & 1;
+        if (su >= 2 && !mbar_wait_bounded(&s_empty[b], static_cast<uint32_t>(((su >> 1) - 1) & 1), A.err))
+          return false;
+        tmem_fence_after();
+        const uint32_t d = tmem + cS + static_cast<uint32_t>(b * kTaK);
+#pragma unroll 1
+        for (int ks = 0; ks < HD / 8; ++ks) {
+          const uint64_t bl = umma_sdesc(smem_addr(sK + PL + ks * (kTaK * 32)), 128, 256);
+          const uint64_t bh = umma_sdesc(smem_addr(sK + ks * (kTaK * 32)), 128, 256);
+          umma_tf32_ts(d, tmem + cQh + 8 * ks, bl, idS, ks > 0 ? 1u : 0u);
+          umma_tf32_ts(d, tmem + cQl + 8 * ks, bh, idS, 1u);
+        }
+#pragma unroll 1
+        for (int ks = 0; ks < HD / 8; ++ks)
+          umma_tf32_ts(d, tmem + cQh + 8 * ks, umma_sdesc(smem_addr(sK + ks * (kTaK * 32)), 128, 256), idS, 1u);
+        umma_commit(&k_empty);
+        umma_commit(&s_full[b]);
+        ++ku, ++su;
+        return true;
+      };
+      // O += P V: the two cross terms, then hi x hi
+      auto issue_pv = [&](bool first) -> bool {
+        if (!mbar_wait_bounded(&v_full, static_cast<uint32_t>(vu & 1), A.err)) return false;
+        if (!mbar_wait_bounded(&p_full, static_cast<uint32_t>(pu & 1), A.err)) return false;
+        tmem_fence_after();
+        const uint32_t d = tmem + cO;
+#pragma unroll 1
+        for (int ks = 0; ks < kTaK / 8; ++ks) {
+          const uint64_t ah = umma_sdesc(smem_addr(sP + ks * 4096), 128, 256);
+          const uint64_t al = umma_sdesc(smem_addr(sP + kTaPPlane + ks * 4096), 128, 256);
+          const uint64_t bh = umma_sdesc(smem_addr(sV + ks * (HD * 32)), 128, 256);
+          const uint64_t bl = umma_sdesc(smem_addr(sV + PL + ks * (HD * 32)), 128, 256);
+          umma_tf32_ss(d, ah, bl, idO, (first && ks == 0) ? 0u : 1u);
+          umma_tf32_ss(d, al, bh, idO, 1u);
+        }
+#pragma unroll 1
+        for (int ks = 0; ks < kTaK / 8; ++ks)
+          umma_tf32_ss(d, umma_sdesc(smem_addr(sP + ks * 4096), 128, 256),
+                       umma_sdesc(smem_addr(sV + ks * (HD * 32)), 128, 256), idO, 1u);
+        umma_commit(&v_empty);
+        umma_commit(&p_empty);
+        ++vu, ++pu;
+        return true;
+      };
+      ok = mbar_wait_bounded(&q_ready, 0u, A.err);
+      for (int j = 0; j < nt && ok; ++j) ok = issue_s();  // pass 1
+      if (ok) ok = issue_s();                               // pass 2: S of the next tile before P V of this one
+      for (int j = 0; j < nt && ok; ++j) {
+        if (j + 1 < nt) ok = issue_s();
+        if (ok) ok = issue_pv(j == 0);
+      }
+      if (ok) umma_commit(&o_full);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int r = tid;  // query row of the block = TMEM lane
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+    const int v = v0 + r;
+    const bool valid = v < nv;
+    const int t = valid ? v / qg : 0, hh = valid ? v - t * qg : 0;
+    const int lim = valid ? A.p0 + t : -1;  // last key position of this query
+    {  // Q row -> TMEM, hi and lo
+      const float *qrow = A.q + static_cast<size_t>(t) * A.ldq + (h0 + hh) * HD;
+#pragma unroll 1
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        uint32_t qh[32], ql[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (valid) x = *reinterpret_cast<const float4 *>(qrow + c0 + i);
+          tf32_split(x.x, qh[i], ql[i]);
+          tf32_split(x.y, qh[i + 1], ql[i + 1]);
+          tf32_split(x.z, qh[i + 2], ql[i + 2]);
+          tf32_split(x.w, qh[i + 3], ql[i + 3]);
+        }
+        tmem_st32(tmem + lane_base + cQh + c0, qh);
+        tmem_st32(tmem + lane_base + cQl + c0, ql);
+      }
+      tmem_wait_st();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_ready);
+    }
+    float m = -INFINITY, l = 0.f;
+    int su = 0, pu = 0;
+    // scores of tile j into sv (the S buffer is released once they are in registers)
+    auto load_s = [&](uint32_t (&s0)[32], uint32_t (&s1)[32]) -> bool {
+      const int b = su & 1;
+      bool w = mbar_wait_bounded(&s_full[b], static_cast<uint32_t>((su >> 1) & 1), A.err);
+      w = __all_sync(0xffffffffu, w);
+      if (!w) return false;
+      tmem_fence_after();
+      tmem_ld32(tmem + lane_base + cS + static_cast<uint32_t>(b * kTaK), s0);
+      tmem_ld32(tmem + lane_base + cS + static_cast<uint32_t>(b * kTaK + 32), s1);
+      tmem_wait_ld();
+      tmem_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[b]);
+      ++su;
+      return true;
+    };
+#pragma unroll 1
+    for (int j = 0; j < nt && ok; ++j) {  // pass 1: maxima
+      uint32_t s0[32], s1[32];
+      if (!(ok = load_s(s0, s1))) break;
+      const int kb = kbeg + j * kTaK;
+#pragma unroll
+      for (int c = 0; c < kTaK; ++c)
+        if (kb + c < kend && kb + c <= lim)
+          m = fmaxf(m, __fmul_rn(__uint_as_float(c < 32 ? s0[c] : s1[c - 32]), A.scale));
+    }
+#pragma unroll 1
+    for (int j = 0; j < nt && ok; ++j) {  // pass 2: probabilities, P to shared memory
+      uint32_t s0[32], s1[32];
+      if (!(ok = load_s(s0, s1))) break;
+      if (pu > 0) {
+        bool w = mbar_wait_bounded(&p_empty, static_cast<uint32_t>((pu - 1) & 1), A.err);
+        if (!(ok = __all_sync(0xffffffffu, w))) break;
+      }
+      const int kb = kbeg + j * kTaK;
+      uint8_t *prow = sP + (r >> 3) * 256 + (r & 7) * 16;
+#pragma unroll
+      for (int c4 = 0; c4 < kTaK / 4; ++c4) {
+        uint32_t ph[4], pl[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = 4 * c4 + e, key = kb + c;
+          const float sc = __uint_as_float(c < 32 ? s0[c] : s1[c - 32]);
+          float p = 0.f;
+          if (key < kend && key <= lim)
+            p = exp_nonpos(__fsub_rn(__fmul_rn(sc, A.scale), m));
+          l = __fadd_rn(l, p);
+          tf32_split(p, ph[e], pl[e]);
+        }
+        const int off = (c4 >> 1) * 4096 + (c4 & 1) * 128;
+        *reinterpret_cast<uint4 *>(prow + off) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+        *reinterpret_cast<uint4 *>(prow + kTaPPlane + off) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the tensor cores
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full);
+      ++pu;
+    }
+    if (ok) {
+      bool w = mbar_wait_bounded(&o_full, 0u, A.err);
+      ok = __all_sync(0xffffffffu, w);
+    }
+    if (ok) {
+      tmem_fence_after();
+      constexpr int PW = pf_part_width(HD);
+      float *pp = nsplit == 1 ? nullptr
+                              : A.part + ((static_cast<size_t>(g) * nblk + blk) * A.max_splits + sp) * kFqN * PW +
+                                    static_cast<size_t>(r) * PW;
+      float *dst = A.out + static_cast<size_t>(t) * A.ldq + (h0 + hh) * HD;
+#pragma unroll 1
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + cO + c0, o);
+        tmem_wait_ld();
+        if (nsplit == 1) {
+          if (valid)
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4 *>(dst + c0 + i) =
+                  make_float4(__uint_as_float(o[i]) / l, __uint_as_float(o[i + 1]) / l, __uint_as_float(o[i + 2]) / l,
+                              __uint_as_float(o[i + 3]) / l);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4 *>(pp + 4 + c0 + i) = make_float4(
+                __uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]), __uint_as_float(o[i + 3]));
+        }
+      }
+      if (nsplit > 1) {
+        pp[0] = m;
+        pp[1] = l;
+        __threadfence();
+      }
+    }
+  }
+  tmem_fence_before();
+  const int all_ok = __syncthreads_and(ok ? 1 : 0);
+  if (warp == 4) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  if (nsplit == 1) return;
+  // ---- the block's last split to arrive combines the splits in order
+  float *pblk = A.part + (static_cast<size_t>(g) * nblk + blk) * A.max_splits * kFqN * pf_part_width(HD);
+  if (tid == 0) {
+    unsigned *cnt = A.count + static_cast<size_t>(g) * nblk + blk;
+    const unsigned prev = atomicAdd(cnt, 1u);
+    const int last = prev == static_cast<unsigned>(nsplit - 1) ? 1 : 0;
+    if (last) *cnt = 0u;  // for the next launch (every split of this one has arrived)
+    s_last = last;
   }
   __syncthreads();
-  for (int i = tid; i < kFqN * HD; i += kThreads) {
-    const int qi = i / HD, dd = i - qi * HD, v = v0 + qi;
-    if (v >= nv) continue;
-    float acc = 0.f;
-    for (int j = 0; j < nsplit; ++j)
-      acc = __fadd_rn(acc, __fmul_rn(s_w[j * kFqN + qi], __ldcg(pblk + (static_cast<size_t>(j) * kFqN + qi) * PW + 2 + dd)));
-    const int t = v / qg, h = v - t * qg;
-    A.out[static_cast<size_t>(t) * A.ldq + (h0 + h) * HD + dd] = acc / s_l[qi];
-  }
+  if (!s_last || !all_ok) return;
+  __threadfence();
+  pf_split_combine<HD>(A, pblk, nsplit, v0, nv, qg, h0, reinterpret_cast<float *>(sP), s_l, tid, kTaThreads);
 }
 
 }  // namespace c2s

@@ -43,6 +43,7 @@ SIGNATURES = {
     "c2s_kv_store_token_id": (I, [P, I, C.c_int32]),
     "c2s_kv_token_ids": (I, [P, P, I]),
     "c2s_kv_get": (I, [P, I, I, I, I, P]),
+    "c2s_prefill_debug": (I, [P, I, P, I]),
     "c2s_ingest_from": (I, [P, I, P, I, P]),
     "c2s_generate": (I, [P, I, F, I, I, P, C.POINTER(I)]),
     "c2s_decode_step": (I, [P, C.c_int32, F, I, C.POINTER(C.c_int32)]),
@@ -359,6 +360,15 @@ class Engine:
     def get_value(self, layer: int, kv_head: int, pos: int) -> np.ndarray:
         out = np.zeros(self.desc.head_dim, np.float32)
         _check(load_library().c2s_kv_get(self._h, 1, layer, kv_head, pos, _ptr(out)))
+        return out
+
+    def prefill_debug(self, which: str, n_tokens: int, n_heads: int) -> np.ndarray:
+        """Test surface: the last layer's buffers of the last tensor-core
+        prefill chunk, [n_tokens][n_heads * head_dim] -- which = "attention"
+        (the causal attention output) or "queries" (the rotated queries)."""
+        out = np.zeros((n_tokens, n_heads * self.desc.head_dim), np.float32)
+        w = {"attention": 0, "queries": 1}[which]
+        _check(load_library().c2s_prefill_debug(self._h, w, _ptr(out), out.size))
         return out
 
     # c2slm.Engine ------------------------------------------------------------

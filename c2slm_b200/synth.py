@@ -77,6 +77,9 @@ PRESETS = {
                      G.Q4_K, G.Q4_K, G.Q6_K, G.Q4_K, G.Q4_K, G.Q6_K, G.Q6_K, G.Q6_K, seed=6),
     "tiny7": Config("tiny7", 512, 3, 4, 2, 1024, 3000, False,
                     G.Q4_K, G.Q4_K, G.Q6_K, G.Q4_K, G.Q4_K, G.Q6_K, G.Q4_K, G.Q6_K, seed=7),
+    # K-quant projections with 64-wide heads (the tensor-core prefill's HD = 64 path)
+    "tiny64": Config("tiny64", 512, 2, 8, 2, 1024, 2048, True,
+                     G.Q4_K, G.Q4_K, G.Q6_K, G.Q4_K, G.Q4_K, G.Q6_K, G.Q6_K, G.Q6_K, seed=9),
     "tiny3": Config("tiny3", 256, 2, 4, 2, 512, 1024, False,
                     G.Q5_0, G.Q8_0, G.Q8_0, G.Q5_0, G.Q4_K, G.Q6_K, G.Q5_0, G.Q4_K, seed=8,
                     qk_norm=True),

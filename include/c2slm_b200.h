@@ -137,6 +137,12 @@ int c2s_kv_token_ids(const c2s_engine *e, int32_t *out, int n);    /* TokenIDs[0
 /* KVCache.GetKey / GetValue (engine/kvcache.go:161-169): head_dim floats. */
 int c2s_kv_get(const c2s_engine *e, int is_value, int layer, int kv_head, int pos, float *out);
 
+/* Test surface, no counterpart in the reference: buffers of the last layer of
+ * the last tensor-core prefill chunk, [tokens][query heads held x head_dim]
+ * floats, the first n_floats -- which = 0: the causal attention output
+ * (before attn_output), 1: the rotated queries it attended with. */
+int c2s_prefill_debug(const c2s_engine *e, int which, float *out, int n_floats);
+
 /* c2slm.Engine.IngestFrom(pos, tokens) (c2slm.go:92-115): clamps pos to
  * [0, SeqLen], rewinds, forwards each token and records it.  Returns the
  * number of tokens forwarded (>= 0) or a negative status; last_normx_out
