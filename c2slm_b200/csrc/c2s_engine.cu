@@ -1932,10 +1932,12 @@ static int pf_alloc(c2s_engine *e) {
     return rc;
   if (tp && (rc = al(reinterpret_cast<void **>(&e->pf_delta), c * H * 4))) return rc;
   // attention splits: keys of a query block in splits of pf_fsplit (a
-  // multiple of the key tile), at most 16 per block at max_tokens
+  // multiple of both kernels' key tiles, at least 512: at 256 the 2048-token
+  // prefill took 26.6 ms, at 512 24.8, at 1024 25.4), at most 16 per block at
+  // max_tokens
   {
     const int mt = d.max_tokens, hd = d.head_dim;
-    e->pf_fsplit = std::max(2 * kFkN, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
+    e->pf_fsplit = std::max(4 * kFkN, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
     e->pf_fns = (mt + e->pf_fsplit - 1) / e->pf_fsplit;
     const size_t nblk = (c * (d.n_heads / d.n_kv_heads) + kFqN - 1) / kFqN;
     const size_t blocks = static_cast<size_t>(nkv) * nblk;

@@ -417,7 +417,7 @@ def test_prefill_attention_tensor_cores_against_float64(model_cache, monkeypatch
     result by up to ~1e-4 of max|out| in either kernel; the tensor-core
     kernel is held to the FP32 kernel's own error (x 2, + 1e-6).  1100
     tokens: the second chunk's 76 tokens attend to all 1100 keys in splits of
-    256 (the split combine); the 7B shape: 7 query heads per kv head;
+    512 (the split combine); the 7B shape: 7 query heads per kv head;
     tiny64: 64-wide heads."""
     cfg = synth.get_config(name)
     hd = cfg.embd // cfg.heads
