@@ -478,7 +478,8 @@ def run_prefill(args, local: int) -> dict:
            "value": round(n / dt, 1), "unit": "tokens/s", "tokens": n, "ms": round(dt * 1000.0, 2),
            "api": "c2s_ingest_from (host ids in, NormX out)",
            "kernels": "tcgen05 kind::i8 GEMM per K-quant projection (128 rows x 128 tokens per CTA); "
-                      "FP32 tiled causal attention (128 queries x 128 keys, key splits)"}
+                      "tcgen05 kind::tf32 causal attention (f32 operands split hi + lo; 128 queries x 64-key "
+                      "tiles, key splits)"}
     if macs:
         tops = 2.0 * macs * n / dt / 1e12
         out.update({"int8_tops_projections": round(tops, 1), "int8_nominal_tops": INT8_NOMINAL_TOPS,
