@@ -145,9 +145,13 @@ constexpr int kPfM = 128, kPfN = 128, kPfThreads = 320;
 constexpr int kPfKStep = 128 * 32, kPfPlane = 8 * kPfKStep;  // per superblock: 32 KB
 constexpr int kPfTokTile = kPfPlane;                          // token tile per superblock
 constexpr int kPfD8Bytes = kPfN * 4, kPfBsBytes = kPfN * 16;
-constexpr int kPfStage = 2 * kPfPlane + kPfTokTile + kPfD8Bytes + kPfBsBytes;
+constexpr int kPfStage = 2 * kPfPlane + kPfTokTile;  // operands of one superblock
+// token scales of a superblock (d8, sub-block sums) in a ring of their own:
+// the epilogue reads them after the MMAs are done with the operand stage,
+// which is then free for the next copy without waiting for the epilogue
+constexpr int kPfScale = kPfD8Bytes + kPfBsBytes, kPfScaleSlots = 4;
 constexpr int kPfStages = 2;
-constexpr int kPfSmem = kPfStages * kPfStage + 128;
+constexpr int kPfSmem = kPfStages * kPfStage + kPfScaleSlots * kPfScale + 128;
 
 enum PfMode { PF_STORE = 0, PF_ADD = 1 };
 
@@ -290,16 +294,22 @@ __global__ void __launch_bounds__(128) k_pf_planes(const uint8_t *w, int rows, i
 // One CTA's tile (row tile R, token tile T) of G; smem: kPfSmem bytes.
 template <int TYPE>
 __device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const int T, uint8_t *smem) {
-  __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages], tfull[2], tempty[2];
+  __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages], tfull[2], tempty[2], sfull[kPfScaleSlots],
+      sempty[kPfScaleSlots];
   __shared__ uint32_t s_tmem;
   constexpr uint32_t kStageBytes = kPfStage;
+  uint8_t *sscale = smem + kPfStages * kPfStage;  // [kPfScaleSlots][d8 | bs]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = R * kPfM, t0 = T * kPfN;
   const int nsb = G.cols / 256;
   if (tid == 0) {
     for (int i = 0; i < kPfStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1 + 8);  // the MMAs' commit and the eight epilogue warps
+      mbar_init(&empty[i], 1);  // the MMAs' commit
+    }
+    for (int i = 0; i < kPfScaleSlots; ++i) {
+      mbar_init(&sfull[i], 1);
+      mbar_init(&sempty[i], 8);  // the eight epilogue warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
@@ -329,8 +339,14 @@ __device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const
         mbar_arrive_expect_tx(&full[st], kStageBytes);
         bulk_g2s(dst, pw + static_cast<size_t>(s) * 2 * kPfPlane, 2 * kPfPlane, &full[st]);
         bulk_g2s(dst + 2 * kPfPlane, G.a + (tb0 + s) * kPfTokTile, kPfTokTile, &full[st]);
-        bulk_g2s(dst + 2 * kPfPlane + kPfTokTile, G.ad + (tb0 + s) * kPfN, kPfD8Bytes, &full[st]);
-        bulk_g2s(dst + 2 * kPfPlane + kPfTokTile + kPfD8Bytes, G.abs + (tb0 + s) * kPfN * 8, kPfBsBytes, &full[st]);
+        const int ss = s % kPfScaleSlots;
+        if (s >= kPfScaleSlots)
+          ok = mbar_wait_bounded(&sempty[ss], static_cast<uint32_t>((s / kPfScaleSlots - 1) & 1), G.err);
+        if (!ok) break;
+        uint8_t *sd = sscale + ss * kPfScale;
+        mbar_arrive_expect_tx(&sfull[ss], kPfScale);
+        bulk_g2s(sd, G.ad + (tb0 + s) * kPfN, kPfD8Bytes, &sfull[ss]);
+        bulk_g2s(sd + kPfD8Bytes, G.abs + (tb0 + s) * kPfN * 8, kPfBsBytes, &sfull[ss]);
       }
     }
   } else if (warp == 9) {
@@ -366,10 +382,11 @@ __device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const
     const uint4 *ri = G.rowinfo + static_cast<size_t>(row) * nsb;
     uint4 rin = __ldg(ri);  // this row's table entry, one superblock ahead
     for (int s = 0; s < nsb && ok; ++s) {
-      const int st = s % kPfStages, tb = s & 1;
+      const int ss = s % kPfScaleSlots, tb = s & 1;
       const uint4 rv = rin;
       if (s + 1 < nsb) rin = __ldg(ri + s + 1);
-      ok = mbar_wait_bounded(&tfull[tb], static_cast<uint32_t>((s >> 1) & 1), G.err);
+      ok = mbar_wait_bounded(&tfull[tb], static_cast<uint32_t>((s >> 1) & 1), G.err) &&
+           mbar_wait_bounded(&sfull[ss], static_cast<uint32_t>((s / kPfScaleSlots) & 1), G.err);
       {  // ok made uniform over the epilogue warps (all leave together)
         uint32_t all;
         asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 2, 256, q;\n\t"
@@ -379,7 +396,7 @@ __device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const
       if (!ok) break;
       tmem_fence_after();
       const float dr = __uint_as_float(rv.x), dmr = __uint_as_float(rv.y);
-      const uint8_t *stg = smem + st * kPfStage + 2 * kPfPlane + kPfTokTile;
+      const uint8_t *stg = sscale + ss * kPfScale;
       const float *sd8 = reinterpret_cast<const float *>(stg);
       const uint4 *sbs = reinterpret_cast<const uint4 *>(stg + kPfD8Bytes);
       const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(tb * 2 * kPfN + 64 * th);
@@ -415,14 +432,14 @@ __device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&tempty[tb]);
-        mbar_arrive(&empty[st]);
+        mbar_arrive(&sempty[ss]);
       }
     }
     if (ok && row < G.rows) {
       float *o = G.out + static_cast<size_t>(t0 + 64 * th) * G.ldo + row;
       const int nt = min(64, G.M - (t0 + 64 * th));
       if (G.mode == PF_ADD) {
-        // residual add in batches of 16: all loads of a batch before its
+        // residual add in batches of 8: all loads of a batch before its
         // stores (one memory round trip per batch, not one per token)
 #pragma unroll
         for (int i0 = 0; i0 < 64; i0 += 16) {
