@@ -439,7 +439,7 @@ __device__ __forceinline__ void pf_gemm_tile(const PfGemm &G, const int R, const
       float *o = G.out + static_cast<size_t>(t0 + 64 * th) * G.ldo + row;
       const int nt = min(64, G.M - (t0 + 64 * th));
       if (G.mode == PF_ADD) {
-        // residual add in batches of 8: all loads of a batch before its
+        // residual add in batches of 16: all loads of a batch before its
         // stores (one memory round trip per batch, not one per token)
 #pragma unroll
         for (int i0 = 0; i0 < 64; i0 += 16) {
