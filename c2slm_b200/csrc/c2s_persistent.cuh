@@ -235,14 +235,14 @@ __device__ __forceinline__ float4 sum_tagged4(const PParams &P, int par, int i, 
 }
 
 // Q8_K of a global vector straight into shared memory: warp w quantises
-// superblocks w, w + kWarps, ... with all of its loads in flight first
-// (cols <= 4 * kWarps * 256 per call round).
+// superblocks w, w + kWarps, ..., kPer at a time, the loads of the next kPer
+// in flight while the current ones are quantised.
 __device__ __forceinline__ void build_q8k_global(const float *src, int cols, int8_t *qs, float *d, int32_t *bsum) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nsb = cols / 256;
   constexpr int kPer = 4;  // superblocks per warp per round
-  for (int base = 0; base < nsb; base += kPer * kWarps) {
-    float4 a[kPer], b[kPer];
+  float4 a[kPer], b[kPer];
+  auto load = [&](int base) {
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
       const int sb = base + warp + k * kWarps;
@@ -252,12 +252,21 @@ __device__ __forceinline__ void build_q8k_global(const float *src, int cols, int
         b[k] = __ldcg(reinterpret_cast<const float4 *>(src + sb * 256 + lane * 8 + 4));
       }
     }
+  };
+  load(0);
+  for (int base = 0; base < nsb; base += kPer * kWarps) {
+    float x[kPer][8];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      x[k][0] = a[k].x, x[k][1] = a[k].y, x[k][2] = a[k].z, x[k][3] = a[k].w;
+      x[k][4] = b[k].x, x[k][5] = b[k].y, x[k][6] = b[k].z, x[k][7] = b[k].w;
+    }
+    if (base + kPer * kWarps < nsb) load(base + kPer * kWarps);
 #pragma unroll
     for (int k = 0; k < kPer; ++k) {
       const int sb = base + warp + k * kWarps;
       if (sb >= nsb) break;
-      float x[8] = {a[k].x, a[k].y, a[k].z, a[k].w, b[k].x, b[k].y, b[k].z, b[k].w};
-      quantize_sb_warp(x, d + sb, bsum + sb * 16, [&](int ln, const int (&q)[8]) {
+      quantize_sb_warp(x[k], d + sb, bsum + sb * 16, [&](int ln, const int (&q)[8]) {
         int8_t *dst = qs + q8_pad_index(sb * 256 + ln * 8);
         uint32_t w0 = 0, w1 = 0;
 #pragma unroll
