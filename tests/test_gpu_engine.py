@@ -323,10 +323,11 @@ def test_many_split_attention_paths_agree(model_cache, monkeypatch):
     assert np.array_equal(out["graph"][1], out["persistent"][1])
 
 
-@pytest.mark.parametrize("n_prompt", [300, 1100])
+@pytest.mark.parametrize("n_prompt", [2, 65, 300, 1100])
 def test_prefill_on_tensor_cores_matches_token_by_token(model_cache, monkeypatch, n_prompt):
     """IngestFrom of a prompt through the tcgen05 int8 GEMM prefill (chunks of
-    up to 1024 tokens, 128-token tiles, a ragged last tile) against the
+    up to 1024 tokens, 128-token tiles, a ragged last tile; 2 and 65 tokens:
+    a nearly empty token tile and key tiles of 64 plus one) against the
     per-token forward path (itself pinned to the oracle by the tests above):
     the last NormX within the tolerance, the K/V cache rows, the same
     TokenIDs and SeqLen, and the same first greedy token after it."""
