@@ -138,8 +138,10 @@ __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.
 // integer dot on the CUDA cores.
 // Warps 0-7: epilogue (warp w: TMEM lanes 32 (w % 4) .. (the rows), tokens
 // 64 (w / 4) ..), warp 8 lane 0: copies, warp 9 lane 0: MMAs.  Two
-// shared-memory stages and two TMEM accumulator sets overlap the copies of
-// round s+1, the MMAs of round s and the epilogue of round s-1.
+// shared-memory operand stages (planes + token tile; freed by the MMAs'
+// commit), a ring of four token-scale slots (freed by the epilogue) and two
+// TMEM accumulator sets overlap the copies of round s+1, the MMAs of round s
+// and the epilogue of round s-1.
 // ---------------------------------------------------------------------------
 constexpr int kPfM = 128, kPfN = 128, kPfThreads = 320;
 constexpr int kPfKStep = 128 * 32, kPfPlane = 8 * kPfKStep;  // per superblock: 32 KB
