@@ -1932,9 +1932,9 @@ static int pf_alloc(c2s_engine *e) {
     return rc;
   if (tp && (rc = al(reinterpret_cast<void **>(&e->pf_delta), c * H * 4))) return rc;
   // attention splits: keys of a query block in splits of pf_fsplit (a
-  // multiple of both kernels' key tiles, at least 512: at 256 the 2048-token
-  // prefill took 26.6 ms, at 512 24.8, at 1024 25.4), at most 16 per block at
-  // max_tokens
+  // multiple of both kernels' key tiles, at least 512: the 2048-token prefill
+  // took 26.6 ms at 256, 25.2 at 384, 24.6-24.8 at 512, 26.5 at 768, 25.4 at
+  // 1024), at most 16 per block at max_tokens
   {
     const int mt = d.max_tokens, hd = d.head_dim;
     e->pf_fsplit = std::max(4 * kFkN, ((mt + 15) / 16 + kFkN - 1) / kFkN * kFkN);
